@@ -1,0 +1,165 @@
+"""Generate the golden fixtures in this folder by running the REFERENCE itself.
+
+Usage (needs the reference source tree; it is not needed afterwards):
+
+    python tests/golden/make_golden.py /path/to/GDNX
+
+The script imports the reference's own modules unchanged and records, for
+seeded inputs, what they return:
+
+* ``gdn3_frozen.pt``   -- ``gdn3._reference_recurrence.reference_recurrent_state``
+  (dense P >= T and compacting P = 16 cases, the parity recipe of
+  ``tests/test_chunk_parity.py:39-55`` at T = 64 and the T = 48 tail), plus the
+  reference's own chunked ``GDN3LinearAttn._gdn3_recurrent_state`` on the same
+  inputs (its fidelity floor).
+* ``gdn3_config0.pt``  -- config 0 (B=2,T=256,H=4,M=4,d=64, fp32, seed 0) through
+  the frozen loop with P = T (dense) -- every 4th token and the last one.
+* ``kmd2.pt``          -- ``research/kernel_ab/ref_scan.scan`` and
+  ``research/kmd2_ablation/exact_cache.reference_scan_with_scores``.
+* ``compaction.pt``    -- one ``GDN3LinearAttn._compact_vec`` call.
+* ``prologue.pt``      -- braided decay (``forward`` lines 809-822 restated by
+  calling the same torch ops on the module's buffers) and ``_apply_partial_rope``.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import types
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+
+def _layer(K, V, P, dims=(16, 16, 8, 8), rotary_factor=None):
+    from gdn3.gdn3_upgrade import GDN3LinearAttn
+    cfg = types.SimpleNamespace(hidden_size=64, linear_num_key_heads=2,
+                                linear_key_head_dim=K, linear_value_head_dim=V,
+                                linear_conv_kernel_dim=4)
+    if rotary_factor is not None:
+        cfg.partial_rotary_factor = rotary_factor
+    L = GDN3LinearAttn(cfg)
+    L.P = P
+    L.residual_rank = P
+    L.a_v, L.a_k, L.b_v, L.b_k = dims
+    return L
+
+
+def make_gdn3_frozen():
+    from gdn3._reference_recurrence import reference_recurrent_state
+    from oracle.inputs import scan_inputs, expand_lanes, parity_inputs
+    cases = {}
+    # (a) config-0 distribution, small, dense (P >= T) and compacting (P = 16)
+    inp = scan_inputs(1, 80, 2, 4, 64, 64, seed=10)
+    ins = [t.contiguous() for t in expand_lanes(inp, 4)]
+    for P in (80, 16):
+        L = _layer(64, 64, P, dims=(8, 8, 8, 8))
+        with torch.no_grad():
+            Y = reference_recurrent_state(L, *ins)
+            Yc = L._gdn3_recurrent_state(*ins)
+        # inputs stored lane-shared; expand_lanes() rebuilds the reference layout
+        cases[f'cfg0dist_P{P}'] = dict(inputs_compact=inp, P=P, dims=(8, 8, 8, 8), Y=Y, Y_chunked=Yc)
+    # (b) the reference parity recipe at d = 128, T = 64 and the T = 48 tail
+    for (B, T, seed) in ((1, 64, 0), (2, 48, 0)):
+        ins = parity_inputs(B, T, 1, 4, 128, 128, seed)
+        L = _layer(128, 128, 16)
+        with torch.no_grad():
+            Y = reference_recurrent_state(L, *ins)
+            Yc = L._gdn3_recurrent_state(*ins)
+        # inputs are regenerated from the seed; the checksum guards the generator
+        cases[f'parity_B{B}_T{T}'] = dict(shape=(B, T, 1, 4, 128, 128), seed=seed,
+                                          input_sums=[t.double().sum() for t in ins],
+                                          P=16, dims=(16, 16, 8, 8), Y=Y, Y_chunked=Yc)
+    torch.save(cases, HERE / 'gdn3_frozen.pt')
+
+
+def make_gdn3_config0():
+    from gdn3._reference_recurrence import reference_recurrent_state
+    from oracle.inputs import scan_inputs, expand_lanes, CONFIGS
+    c = CONFIGS[0]
+    inp = scan_inputs(c['B'], c['T'], c['H'], c['M'], c['K'], c['V'], c['seed'])
+    ins = [t.contiguous() for t in expand_lanes(inp, c['M'])]
+    L = _layer(64, 64, c['T'], dims=(8, 8, 8, 8))
+    with torch.no_grad():
+        Y = reference_recurrent_state(L, *ins)
+    keep = list(range(0, c['T'], 4)) + [c['T'] - 1]
+    torch.save(dict(t_index=torch.tensor(keep), Y=Y[:, keep].clone(),
+                    Y_sum=Y.double().sum(), Y_sq=Y.double().square().sum()),
+               HERE / 'gdn3_config0.pt')
+
+
+def make_kmd2():
+    sys.path.insert(0, str(Path(REF) / 'research' / 'kernel_ab'))
+    import ref_scan
+    from research.kmd2_ablation.exact_cache import reference_scan_with_scores
+    g = torch.Generator().manual_seed(77)
+    out = {}
+    B, T, H, dk, dv = 2, 40, 2, 32, 32
+    for r_out in (1, 4):
+        q = torch.randn(B, T, H, r_out, dk, generator=g) * dk ** -0.5
+        k = torch.nn.functional.normalize(torch.randn(B, T, H, dk, generator=g), dim=-1)
+        v = torch.randn(B, T, H, dv, generator=g)
+        gd = torch.exp(-torch.nn.functional.softplus(1.2 * torch.randn(B, T, H, dk, generator=g) - 0.6))
+        be = torch.sigmoid(torch.randn(B, T, H, generator=g))
+        bw = torch.sigmoid(torch.randn(B, T, H, generator=g))
+        mix = torch.randn(H, r_out, generator=g) if r_out > 1 else None
+        y = ref_scan.scan(q, k, v, gd, be, bw, mix)
+        y2, sc = reference_scan_with_scores(q, k, v, gd, be, bw, mix)
+        out[f'r{r_out}'] = dict(inputs=[q, k, v, gd, be, bw, mix], y=y, y_scored=y2, scores=sc)
+    # known-answer cases of tests/ablation/test_exact_cache_math.py:563-596
+    q = torch.tensor([[[[[3.0]]]]], dtype=torch.float64)
+    k = torch.tensor([[[[2.0]]]], dtype=torch.float64)
+    v = torch.tensor([[[[5.0]]]], dtype=torch.float64)
+    d = torch.tensor([[[[0.25]]]], dtype=torch.float64)
+    be = torch.tensor([[[0.7]]], dtype=torch.float64)
+    bw = torch.tensor([[[0.4]]], dtype=torch.float64)
+    y, sc = reference_scan_with_scores(q, k, v, d, be, bw)
+    out['kat'] = dict(inputs=[q, k, v, d, be, bw, None], y=y, scores=sc)
+    torch.save(out, HERE / 'kmd2.pt')
+
+
+def make_compaction():
+    g = torch.Generator().manual_seed(5)
+    N, R, V, K, P = 6, 4, 128, 128, 16
+    L = _layer(K, V, P)
+    A = torch.randn(N, R, 16, 16, generator=g) * 0.1
+    Bk = torch.randn(N, R, 8, 8, generator=g) * 0.1
+    U = torch.randn(N, V, P, generator=g) * 0.3
+    Vb = torch.randn(N, K, P, generator=g) * 0.3
+    with torch.no_grad():
+        An, Bn, Uo, Vo, err = L._compact_vec(A, Bk, U, Vb, L.slow_decay)
+    torch.save(dict(inputs=[A, Bk, U, Vb], A_new=An, B_new=Bn, err=err,
+                    slow_decay=L.slow_decay), HERE / 'compaction.pt')
+
+
+def make_prologue():
+    g = torch.Generator().manual_seed(9)
+    out = {}
+    for rf in (0.25, 0.5):
+        L = _layer(128, 128, 16, rotary_factor=rf)
+        x = torch.randn(1, 33, 1, 4, 128, generator=g)
+        out[f'rope_rf{rf}'] = dict(x=x, y=L._apply_partial_rope(x, 33))
+    L = _layer(128, 128, 16)
+    dp = torch.randn(1, 33, 2, 4, 4, generator=g) * 3
+    g_raw = torch.nn.functional.softplus(dp).clamp(max=5.0)
+    rates = L.base_decay_rates.view(1, 1, 1, 1, 4)
+    dec = torch.exp(-g_raw * rates).mean(dim=-1).clamp(max=L.decay_clamp)
+    out['braid'] = dict(decay_proj=dp, decay=dec, clamp=L.decay_clamp)
+    torch.save(out, HERE / 'prologue.pt')
+
+
+if __name__ == '__main__':
+    REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('GDNX_REFERENCE')
+    if not REF:
+        raise SystemExit('usage: make_golden.py /path/to/reference')
+    sys.path.insert(0, REF)
+    torch.manual_seed(0)
+    make_gdn3_frozen()
+    make_gdn3_config0()
+    make_kmd2()
+    make_compaction()
+    make_prologue()
+    for f in sorted(HERE.glob('*.pt')):
+        print(f.name, f.stat().st_size)
