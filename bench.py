@@ -1,0 +1,352 @@
+#!/usr/bin/env python
+"""Benchmark of the GDN3 recurrent-scan hot path on B200.
+
+Headline (BASELINE metric "chunked-scan prefill tok/s ... ; decode-step HBM GB/s"):
+  * prefill: config 1 -- one GDN3 linear-attention layer scan, B=8, T=4096,
+    H=16 heads x M=4 lanes, d_k=d_v=128, bf16 q/k/v/beta/log-decay (lane
+    shared q/k/v), fp32 state, bf16 per-lane outputs, lane RoPE (first 64 dims
+    on lane 0).  One step = one scan of the batch.  value = B*T tokens/s over
+    all ranks (weak scaling: every rank scans its own config-1 shard).
+  * decode (reported beside it): config 3 -- 24 layers x B=256 x H=16 x 4
+    lanes, fp32 128x128 states, one token; GB/s of algorithmic traffic.
+
+Timing: W warm-up steps, then exactly K steps between CUDA events on the
+launching stream, barrier + synchronize on both sides, max over ranks.
+Inputs (402 MB) and outputs (537 MB) exceed the 126 MB L2, so no flush is
+needed between steps.  ``--impl reference`` times the CPU restatement of the
+reference recurrence (the oracle port; the reference is pure Python/PyTorch)
+on the host cores, on a bounded T-slice of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG1 = dict(B=8, T=4096, H=16, M=4, K=128, V=128, chunk=64)
+CFG3 = dict(layers=24, B=256, H=16, M=4, K=128, V=128)
+
+
+def chunk_flops_per_chain_token(dk, dv, C):
+    """Algorithmic FLOPs of the chunked scan per chain-token (dense tiles, no C^3 solve)."""
+    return 6 * dk * dv + 2 * C * (3 * dk + 2 * dv)
+
+
+def prefill_bytes(c):
+    """q,k,v read once per head (bf16), beta + log-decay per lane (bf16), bf16 per-lane outputs."""
+    B, T, H, M, K, V = (c[x] for x in "BTHMKV")
+    return B * T * H * ((2 * K + V) * 2 + M * 2 * 2 + M * V * 2)
+
+
+def decode_bytes(c):
+    L, B, H, M, K, V = (c[x] for x in ("layers", "B", "H", "M", "K", "V"))
+    N = B * H * M
+    return L * (2 * N * V * K * 4 + B * H * (2 * K + V) * 2 + N * 2 * 2 + N * V * 2)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm=d["hbm_gbs"], bf16=d["bf16_tflops"], bf16_sust=d.get("bf16_tflops_sustained"),
+                    source="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sust=1400.0, source="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        time.sleep(0.25)
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = [r for r in self.rows if len(r) >= 7]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][1]) if rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_sample_rate(target_s, max_T=512, B=None):
+    """Oracle port (CPU restatement of the reference's frozen loop, dense case) on
+    a T-slice of config 1; returns (tok/s, threads, sample description)."""
+    from oracle import recurrence as R
+    from oracle.inputs import scan_inputs, expand_lanes
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    c = dict(CFG1)
+    if B is not None:
+        c["B"] = B
+    T = 8
+    while True:
+        inp = scan_inputs(c["B"], T, c["H"], c["M"], c["K"], c["V"], seed=1, dtype=torch.bfloat16)
+        ins = expand_lanes(inp, c["M"])
+        t0 = time.perf_counter()
+        R.dense_scan(*ins)
+        dt = time.perf_counter() - t0
+        if dt >= target_s or T >= max_T:
+            break
+        T = min(max_T, T * 2 if dt < target_s / 4 else int(T * target_s / dt * 1.1) + 1)
+    return c["B"] * T / dt, threads, f"config-1 T-slice B={c['B']},T={T},H=16,M=4,d=128 ({dt:.1f} s)", T
+
+
+def run_reference(args, rank):
+    """--impl reference: the reference recurrence restated on the CPU (rank 0 only)."""
+    if rank != 0:
+        return
+    rate0, threads, sample, T = cpu_sample_rate(target_s=2.0)
+    from oracle import recurrence as R
+    from oracle.inputs import scan_inputs, expand_lanes
+    c = CFG1
+    inp = scan_inputs(c["B"], T, c["H"], c["M"], c["K"], c["V"], seed=1, dtype=torch.bfloat16)
+    ins = expand_lanes(inp, c["M"])
+    for _ in range(args.warmup):
+        R.dense_scan(*ins)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        R.dense_scan(*ins)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = c["B"] * T / dt
+    line = {"impl": "reference", "metric": "chunked-scan prefill tok/s", "value": value, "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "config1-prefill T-slice", "B": c["B"], "T": T,
+                                            "H": c["H"], "M": c["M"], "K": c["K"], "V": c["V"]},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def make_prefill_inputs(c, dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    B, T, H, M, K, V = (c[x] for x in "BTHMKV")
+    bf = torch.bfloat16
+    q = torch.nn.functional.normalize(torch.randn(B, T, H, K, device=dev, generator=g), dim=-1).to(bf)
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, K, device=dev, generator=g), dim=-1).to(bf)
+    v = torch.randn(B, T, H, V, device=dev, generator=g).to(bf)
+    beta = torch.sigmoid(torch.randn(B, T, H, M, device=dev, generator=g)).to(bf)
+    tau = torch.tensor([0.05, 0.02, 0.005, 0.001][:M], device=dev)
+    logg = (-torch.nn.functional.softplus(torch.randn(B, T, H, M, device=dev, generator=g)) * tau).to(bf)
+    return dict(q=q, k=k, v=v, beta=beta, logg=logg)
+
+
+def timed(fn, steps, warmup, stream, barrier):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--algo", default="auto", choices=["auto", "recurrent", "chunked"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    from gdnx_b200 import ops
+    from gdnx_b200.prologue import lane_rope
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    barrier = (lambda: dist.barrier()) if dist else (lambda: None)
+    stream = torch.cuda.current_stream(dev)
+    peaks = load_peaks()
+
+    # ---------------- prefill (config 1 per rank) ----------------
+    c = CFG1
+    inp = make_prefill_inputs(c, dev, seed=1 + rank)
+    rope = lane_rope(c["M"], c["K"], c["K"], 0.5)
+    y = torch.empty(c["B"], c["T"], c["H"], c["M"], c["V"], dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        ops.gdn3_scan(inp["q"], inp["k"], inp["v"], inp["beta"], inp["beta"], inp["logg"], decay_kind="log",
+                      rope=rope, out=y, algo=args.algo, workspace=ws)
+
+    with ClockSampler(local) as clk:
+        ms = timed(step, args.steps, args.warmup, stream, barrier)
+    clocks = clk.summary()
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    tokens = c["B"] * c["T"] * world
+    value = tokens / (ms * 1e-3)
+    chain_tokens = c["B"] * c["T"] * c["H"] * c["M"]
+    flops = chain_tokens * chunk_flops_per_chain_token(c["K"], c["V"], c["chunk"])
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("prefill_config1_bytes_per_launch")
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16"], "traffic": traffic,
+                "peak_source": f"{peaks['source']} bf16 burst", "flops_per_launch": flops,
+                "alg_bytes_per_launch": prefill_bytes(c),
+                "hbm_frac": prefill_bytes(c) / (ms * 1e-3) / 1e9 / peaks["hbm"]}
+
+    # ---------------- end to end: host buffers through the public API ----------------
+    e2e = None
+    if not args.no_e2e:
+        host = {n: t.cpu().pin_memory() for n, t in inp.items()}
+        yh = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        dbuf = {n: torch.empty_like(t) for n, t in inp.items()}
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
+        d2h = yh.numel() * yh.element_size()
+
+        def e2e_step():
+            for n in host:
+                dbuf[n].copy_(host[n], non_blocking=True)
+            ops.gdn3_scan(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["beta"], dbuf["beta"], dbuf["logg"],
+                          decay_kind="log", rope=rope, out=y, algo=args.algo, workspace=ws)
+            yh.copy_(y, non_blocking=True)
+
+        ms_e2e = timed(e2e_step, max(3, args.steps // 3), 3, stream, barrier)
+        if dist:
+            t = torch.tensor([ms_e2e], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_e2e = t.item()
+        e2e = {"value": tokens / (ms_e2e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e}
+        del host, yh, dbuf
+
+    # ---------------- all-gather of per-head outputs (multi-GPU only) ----------------
+    gather = None
+    if dist:
+        full = torch.empty((world,) + tuple(y.shape), dtype=y.dtype, device=dev)
+        ms_g = timed(lambda: dist.all_gather_into_tensor(full, y), 3, 1, stream, barrier)
+        t = torch.tensor([ms_g], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gather = {"ms": t.item(), "bytes_per_rank_received": (world - 1) * y.numel() * y.element_size(),
+                  "collective": "nccl all_gather_into_tensor"}
+        del full
+
+    # ---------------- decode (config 3) ----------------
+    decode = None
+    if not args.no_decode:
+        d = CFG3
+        N = d["B"] * d["H"] * d["M"]
+        g = torch.Generator(device=dev).manual_seed(3 + rank)
+        states = [torch.randn(N, d["V"], d["K"], device=dev, generator=g) * 0.02 for _ in range(d["layers"])]
+        bf = torch.bfloat16
+        toks = []
+        for _ in range(d["layers"]):
+            qd = torch.nn.functional.normalize(torch.randn(d["B"], d["H"], d["K"], device=dev, generator=g), dim=-1).to(bf)
+            kd = torch.nn.functional.normalize(torch.randn(d["B"], d["H"], d["K"], device=dev, generator=g), dim=-1).to(bf)
+            vd = torch.randn(d["B"], d["H"], d["V"], device=dev, generator=g).to(bf)
+            bd = torch.sigmoid(torch.randn(d["B"], d["H"], d["M"], device=dev, generator=g)).to(bf)
+            tau = torch.tensor([0.05, 0.02, 0.005, 0.001], device=dev)
+            ld = (-torch.nn.functional.softplus(torch.randn(d["B"], d["H"], d["M"], device=dev, generator=g)) * tau).to(bf)
+            toks.append((qd, kd, vd, bd, ld))
+        yd = [torch.empty(d["B"], d["H"], d["M"], d["V"], dtype=bf, device=dev) for _ in range(d["layers"])]
+        drope = lane_rope(d["M"], d["K"], d["K"], 0.5, pos0=4096)
+
+        def dstep():
+            for l in range(d["layers"]):
+                qd, kd, vd, bd, ld = toks[l]
+                ops.decode_step(states[l], qd, kd, vd, bd, bd, ld, decay_kind="log", rope=drope, out=yd[l])
+
+        dms = timed(dstep, max(3, args.steps // 3), 3, stream, barrier)
+        if dist:
+            t = torch.tensor([dms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dms = t.item()
+        db = decode_bytes(d) * world
+        decode = {"metric": "decode-step HBM GB/s", "value": db / (dms * 1e-3) / 1e9, "unit": "GB/s",
+                  "ms_per_step": dms, "alg_bytes_per_step": db, "layers": d["layers"],
+                  "states_per_layer": N, "hbm_frac": db / world / (dms * 1e-3) / 1e9 / peaks["hbm"],
+                  "peak_gbs": peaks["hbm"], "launches_per_step": d["layers"]}
+        del states
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, threads, sample, _ = cpu_sample_rate(target_s=10.0)
+        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": "chunked-scan prefill tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "config1: GDN3 dense prefill layer scan per rank", **c,
+                           "rope": "lane RoPE, lane 0 first 64 dims base 10000",
+                           "state": "fp32", "io": "bf16", "algo": args.algo,
+                           "l2": "inputs 402 MB + outputs 537 MB > 126 MB L2 (no flush)",
+                           "parallelism": f"(batch x head) shards, dp{world}"},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+                "clocks": clocks, "decode": decode, "gather": gather}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

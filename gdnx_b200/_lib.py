@@ -1,0 +1,113 @@
+"""ctypes binding of the C ABI declared in ``include/gdnx.h``.
+
+The structures below mirror the header field for field.  Loading fails
+loudly when ``libgdnx.so`` is missing: there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libgdnx.so"
+
+GDNX_OK, GDNX_EINVAL, GDNX_ELAUNCH, GDNX_ETIMEOUT, GDNX_EUNSUPPORTED, GDNX_EWORKSPACE = range(6)
+GDNX_F32, GDNX_BF16, GDNX_F16 = 0, 1, 2
+GDNX_MODE_GDN3, GDNX_MODE_KMD2 = 0, 1
+GDNX_DECAY_GAMMA, GDNX_DECAY_LOG, GDNX_DECAY_BRAIDED = 0, 1, 2
+GDNX_ALGO_AUTO, GDNX_ALGO_RECURRENT, GDNX_ALGO_CHUNKED = 0, 1, 2
+
+EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
+            "gdnx_decode_step", "gdnx_status_string", "gdnx_version")
+
+
+class View(C.Structure):
+    _fields_ = [("ptr", C.c_void_p), ("dtype", C.c_int32), ("dim", C.c_int32),
+                ("sb", C.c_int64), ("st", C.c_int64), ("sh", C.c_int64), ("sm", C.c_int64),
+                ("ss", C.c_int64)]
+
+
+class Rope(C.Structure):
+    _fields_ = [("enable", C.c_int32), ("pairs", C.c_int32 * 4), ("scale", C.c_float * 4),
+                ("den", C.c_float * 4), ("pos0", C.c_int64)]
+
+
+class ScanArgs(C.Structure):
+    _fields_ = [("B", C.c_int64), ("T", C.c_int64), ("H", C.c_int64), ("M", C.c_int64),
+                ("K", C.c_int64), ("V", C.c_int64),
+                ("mode", C.c_int32), ("algo", C.c_int32), ("r_out", C.c_int32), ("chunk", C.c_int32),
+                ("q", View), ("k", View), ("v", View), ("gate_e", View), ("gate_w", View),
+                ("decay", View), ("decay_kind", C.c_int32), ("braid_rates", C.c_float * 4),
+                ("braid_clamp", C.c_float), ("rope", Rope),
+                ("out_mix", C.c_void_p),
+                ("y", C.c_void_p), ("y_dtype", C.c_int32),
+                ("y_sb", C.c_int64), ("y_st", C.c_int64), ("y_sh", C.c_int64), ("y_sm", C.c_int64),
+                ("scores", C.c_void_p),
+                ("state_in", C.c_void_p), ("state_out", C.c_void_p),
+                ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class KrScanArgs(C.Structure):
+    _fields_ = [("base", ScanArgs),
+                ("R", C.c_int32), ("P", C.c_int32), ("a_v", C.c_int32), ("a_k", C.c_int32),
+                ("b_v", C.c_int32), ("b_k", C.c_int32), ("slow_decay", C.c_float),
+                ("sketch", C.c_void_p), ("A", C.c_void_p), ("Bk", C.c_void_p),
+                ("U", C.c_void_p), ("Vb", C.c_void_p), ("slot", C.c_void_p), ("comp_err", C.c_void_p)]
+
+
+class CompactArgs(C.Structure):
+    _fields_ = [("N", C.c_int64), ("R", C.c_int32), ("P", C.c_int32), ("V", C.c_int32), ("K", C.c_int32),
+                ("a_v", C.c_int32), ("a_k", C.c_int32), ("b_v", C.c_int32), ("b_k", C.c_int32),
+                ("slow_decay", C.c_float), ("sketch", C.c_void_p), ("A", C.c_void_p), ("Bk", C.c_void_p),
+                ("U", C.c_void_p), ("Vb", C.c_void_p), ("err", C.c_void_p)]
+
+
+class DecodeArgs(C.Structure):
+    _fields_ = [("B", C.c_int64), ("H", C.c_int64), ("M", C.c_int64), ("K", C.c_int64), ("V", C.c_int64),
+                ("mode", C.c_int32), ("r_out", C.c_int32),
+                ("q", View), ("k", View), ("v", View), ("gate_e", View), ("gate_w", View), ("decay", View),
+                ("decay_kind", C.c_int32), ("braid_rates", C.c_float * 4), ("braid_clamp", C.c_float),
+                ("rope", Rope), ("out_mix", C.c_void_p),
+                ("S", C.c_void_p), ("y", C.c_void_p), ("y_dtype", C.c_int32),
+                ("y_sb", C.c_int64), ("y_sh", C.c_int64), ("y_sm", C.c_int64)]
+
+
+_lib = None
+
+
+def load(path: Path = LIB_PATH):
+    """Load ``libgdnx.so`` (once) and declare the exported signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not Path(path).exists():
+        raise ImportError(f"gdnx_b200: {path} is missing -- run `python -m gdnx_b200.build` "
+                          "(the CUDA library is required; there is no CPU fallback)")
+    lib = C.CDLL(str(path))
+    lib.gdnx_scan_fwd.argtypes = [C.POINTER(ScanArgs), C.c_void_p]
+    lib.gdnx_scan_fwd.restype = C.c_int
+    lib.gdnx_scan_workspace_bytes.argtypes = [C.POINTER(ScanArgs)]
+    lib.gdnx_scan_workspace_bytes.restype = C.c_size_t
+    lib.gdnx_kr_scan_fwd.argtypes = [C.POINTER(KrScanArgs), C.c_void_p]
+    lib.gdnx_kr_scan_fwd.restype = C.c_int
+    lib.gdnx_compact.argtypes = [C.POINTER(CompactArgs), C.c_void_p]
+    lib.gdnx_compact.restype = C.c_int
+    lib.gdnx_decode_step.argtypes = [C.POINTER(DecodeArgs), C.c_void_p]
+    lib.gdnx_decode_step.restype = C.c_int
+    lib.gdnx_status_string.argtypes = [C.c_int]
+    lib.gdnx_status_string.restype = C.c_char_p
+    lib.gdnx_version.argtypes = []
+    lib.gdnx_version.restype = C.c_char_p
+    _lib = lib
+    return lib
+
+
+class GdnxError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        msg = load().gdnx_status_string(status).decode()
+        super().__init__(f"{what}: {msg}")
+
+
+def check(status: int, what: str):
+    if status != GDNX_OK:
+        raise GdnxError(status, what)

@@ -1,0 +1,65 @@
+// Batched compaction entry (gdnx_compact): one CTA per chain.
+#include "compact.cuh"
+#include "kernels.h"
+
+namespace gdnx {
+namespace {
+
+constexpr int kThreads = kCompThreads;
+constexpr int kPT = kCompPT;
+
+struct CompParams {
+  gdnx_compact_args a;
+  CompactDims d;
+};
+
+__global__ void __launch_bounds__(kThreads) compact_kernel(const CompParams P) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const CompactDims d = P.d;
+  const gdnx_compact_args& a = P.a;
+  const int64_t n = blockIdx.x;
+  const int ld = compact_ld(d.n);
+  float* Rm = sm;
+  float* work = Rm + d.m * ld;
+  float* A_s = work + compact_work_floats();
+  float* B_s = A_s + d.R * d.m;
+  float* tileU = B_s + d.R * d.n;
+  float* tileV = tileU + a.V * kPT;
+
+  float* Ag = a.A + n * d.R * d.m;
+  float* Bg = a.Bk + n * d.R * d.n;
+  for (int i = threadIdx.x; i < d.R * d.m; i += kThreads) A_s[i] = Ag[i];
+  for (int i = threadIdx.x; i < d.R * d.n; i += kThreads) B_s[i] = Bg[i];
+  for (int i = threadIdx.x; i < d.m * ld; i += kThreads) Rm[i] = 0.f;
+  __syncthreads();
+  add_residual_rmat(Rm, a.U + n * a.V * a.P, a.Vb + n * a.K * a.P, nullptr, a.V, a.K, a.P, tileU, tileV, d);
+  add_kron_rmat(Rm, A_s, B_s, d);
+  __syncthreads();
+  const float err = compact_core(Rm, A_s, B_s, a.sketch + n * d.n * d.q, work, d);
+  for (int i = threadIdx.x; i < d.R * d.m; i += kThreads) Ag[i] = A_s[i];
+  for (int i = threadIdx.x; i < d.R * d.n; i += kThreads) Bg[i] = B_s[i];
+  if (a.err && threadIdx.x == 0) a.err[n] = err;
+}
+
+}  // namespace
+
+gdnx_status launch_compact(const gdnx_compact_args& a, cudaStream_t st) {
+  CompParams P;
+  P.a = a;
+  CompactDims& d = P.d;
+  d.R = a.R; d.a_v = a.a_v; d.a_k = a.a_k; d.b_v = a.b_v; d.b_k = a.b_k;
+  d.m = a.a_v * a.a_k; d.n = a.b_v * a.b_k;
+  d.q = min(a.R + 4, min(d.m, d.n));
+  d.delta = a.slow_decay;
+  if (d.m > kCompMaxM || d.n > kCompMaxN || d.q > kCompMaxQ || d.R > d.q) return GDNX_EUNSUPPORTED;
+  if (a.V > 128 || a.K > 128 || a.V * a.K > 64 * kThreads) return GDNX_EUNSUPPORTED;
+  const size_t smem = sizeof(float) * (size_t)(d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) +
+                                               (a.V + a.K) * kPT);
+  if (cudaFuncSetAttribute(compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return GDNX_ELAUNCH;
+  compact_kernel<<<(unsigned)a.N, kThreads, smem, st>>>(P);
+  return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+}
+
+}  // namespace gdnx

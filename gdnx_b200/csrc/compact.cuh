@@ -1,0 +1,297 @@
+// Rearrangement-SVD compaction of one chain, executed by one CTA on shared
+// memory (gdn3/gdn3_upgrade.py:650-719 semantics):
+//
+//   R_mat (m x n) = sum_r vec(A_r) vec(B_r)^T + rearrange(U Vb^T)   [built by the caller]
+//   Y = R G ; twice  Y = R (R^T Y)          (randomized range finder, G given)
+//   Q = orth(Y)                             (modified Gram-Schmidt, two passes)
+//   Bm = Q^T R  (q x n) ;  Bm = Ub S Vh     (one-sided Jacobi SVD, Hestenes)
+//   A_svd_r = (Q Ub)[:, r] S_r ,  B_svd_r = Vh[r]        (r < R, descending S)
+//   A <- d A + (1-d) A_svd ;  B <- d B + (1-d) B_svd   ;  U, Vb untouched
+//   err = |R|_F^2 - sum_{r<R} S_r^2
+//
+// The joint sign of each (A_svd_r, B_svd_r) pair is fixed so that the
+// largest-|.| entry of B_svd_r is positive; the span-level results (and Q's
+// own column signs) do not depend on the QR convention.
+#pragma once
+
+#include "common.cuh"
+
+namespace gdnx {
+
+constexpr int kCompMaxQ = 8;    // sketch width  q = min(R+4, m, n) <= 8
+constexpr int kCompMaxN = 64;   // n = b_v * b_k <= 64
+constexpr int kCompMaxM = 256;  // m = a_v * a_k <= 256
+constexpr int kCompThreads = 256;
+constexpr int kCompPT = 16;     // slots per staged tile of U / Vb
+
+struct CompactDims {
+  int R, m, n, q;
+  int a_v, a_k, b_v, b_k;
+  float delta;
+};
+
+// Shared-memory floats the core needs beyond R_mat (which is m x (n+1), padded).
+__host__ __device__ constexpr int compact_work_floats() {
+  return 2 * kCompMaxM * kCompMaxQ      // Y, Q
+         + kCompMaxN * kCompMaxQ        // Z
+         + kCompMaxQ * kCompMaxN        // Bm
+         + kCompMaxN * kCompMaxQ        // G
+         + kCompMaxQ * kCompMaxQ        // J
+         + 64;                          // scalars / reductions
+}
+__host__ __device__ constexpr int compact_ld(int n) { return n + 1; }
+
+GDNX_DEV float block_sum(float x, float* red) {
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  x = warp_sum(x);
+  __syncthreads();
+  if (lane == 0) red[warp] = x;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = blockDim.x / 32;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  __syncthreads();
+  return t;
+}
+
+// Returns err (discarded energy, not clamped) to every thread.  Rm (m x ld)
+// is read only.  A_s [R][m], B_s [R][n] hold the current (true) factors and
+// are overwritten with the blended ones.  G is [n][q] in global memory.
+GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float* G,
+                            float* work, const CompactDims d) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int lane = tid % 32, warp = tid / 32;
+  const int m = d.m, n = d.n, q = d.q, R = d.R;
+  const int ld = compact_ld(n);
+  float* Y = work;
+  float* Qm = Y + kCompMaxM * kCompMaxQ;
+  float* Z = Qm + kCompMaxM * kCompMaxQ;
+  float* Bm = Z + kCompMaxN * kCompMaxQ;
+  float* Gs = Bm + kCompMaxQ * kCompMaxN;
+  float* J = Gs + kCompMaxN * kCompMaxQ;
+  float* red = J + kCompMaxQ * kCompMaxQ;  // 64 floats
+
+  // energy
+  float e = 0.f;
+  for (int idx = tid; idx < m * n; idx += nt) {
+    const float x = Rm[(idx / n) * ld + idx % n];
+    e += x * x;
+  }
+  const float total = block_sum(e, red);
+
+  for (int idx = tid; idx < n * q; idx += nt) Gs[idx] = G[idx];
+  __syncthreads();
+  // Y = R G
+  for (int idx = tid; idx < m * q; idx += nt) {
+    const int i = idx / q, c = idx % q;
+    float acc = 0.f;
+    for (int j = 0; j < n; ++j) acc = fmaf(Rm[i * ld + j], Gs[j * q + c], acc);
+    Y[idx] = acc;
+  }
+  __syncthreads();
+  for (int it = 0; it < 2; ++it) {
+    for (int idx = tid; idx < n * q; idx += nt) {  // Z = R^T Y
+      const int j = idx / q, c = idx % q;
+      float acc = 0.f;
+      for (int i = 0; i < m; ++i) acc = fmaf(Rm[i * ld + j], Y[i * q + c], acc);
+      Z[idx] = acc;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < m * q; idx += nt) {  // Y = R Z
+      const int i = idx / q, c = idx % q;
+      float acc = 0.f;
+      for (int j = 0; j < n; ++j) acc = fmaf(Rm[i * ld + j], Z[j * q + c], acc);
+      Y[idx] = acc;
+    }
+    __syncthreads();
+  }
+  // Q = orth(Y): one warp, modified Gram-Schmidt with re-orthogonalisation.
+  if (warp == 0) {
+    for (int c = 0; c < q; ++c) {
+      for (int pass = 0; pass < 2; ++pass) {
+        for (int p = 0; p < c; ++p) {
+          float dot = 0.f;
+          for (int i = lane; i < m; i += 32) dot += Qm[i * q + p] * Y[i * q + c];
+          dot = warp_sum(dot);
+          for (int i = lane; i < m; i += 32) Y[i * q + c] -= dot * Qm[i * q + p];
+          __syncwarp();
+        }
+      }
+      float nn = 0.f;
+      for (int i = lane; i < m; i += 32) nn += Y[i * q + c] * Y[i * q + c];
+      nn = warp_sum(nn);
+      const float inv = nn > 1e-30f ? rsqrtf(nn) : 0.f;
+      for (int i = lane; i < m; i += 32) Qm[i * q + c] = Y[i * q + c] * inv;
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // Bm = Q^T R   (q x n)
+  for (int idx = tid; idx < q * n; idx += nt) {
+    const int c = idx / n, j = idx % n;
+    float acc = 0.f;
+    for (int i = 0; i < m; ++i) acc = fmaf(Qm[i * q + c], Rm[i * ld + j], acc);
+    Bm[idx] = acc;
+  }
+  __syncthreads();
+  // One-sided Jacobi on W = Bm^T (n x q): lane holds rows lane and lane+32.
+  if (warp == 0) {
+    float w0[kCompMaxQ], w1[kCompMaxQ];
+    const bool r0 = lane < n, r1 = lane + 32 < n;
+#pragma unroll
+    for (int c = 0; c < kCompMaxQ; ++c) {
+      w0[c] = (c < q && r0) ? Bm[c * n + lane] : 0.f;
+      w1[c] = (c < q && r1) ? Bm[c * n + lane + 32] : 0.f;
+    }
+    // J = I (row `lane` of J kept by lanes < q)
+    float jr[kCompMaxQ];
+#pragma unroll
+    for (int c = 0; c < kCompMaxQ; ++c) jr[c] = (lane == c) ? 1.f : 0.f;
+    for (int sweep = 0; sweep < 30; ++sweep) {
+      float off = 0.f;
+#pragma unroll
+      for (int i = 0; i < kCompMaxQ - 1; ++i) {
+#pragma unroll
+        for (int j = i + 1; j < kCompMaxQ; ++j) {
+          if (j >= q) continue;
+          const float al = warp_sum(w0[i] * w0[i] + w1[i] * w1[i]);
+          const float be = warp_sum(w0[j] * w0[j] + w1[j] * w1[j]);
+          const float ga = warp_sum(w0[i] * w0[j] + w1[i] * w1[j]);
+          const float nrm = sqrtf(al * be);
+          if (nrm <= 1e-37f || fabsf(ga) <= 1e-7f * nrm) continue;
+          off = fmaxf(off, fabsf(ga) / nrm);
+          const float zeta = (be - al) / (2.f * ga);
+          const float t = copysignf(1.f, zeta) / (fabsf(zeta) + sqrtf(1.f + zeta * zeta));
+          const float cs = rsqrtf(1.f + t * t);
+          const float sn = cs * t;
+          float a0 = w0[i], b0 = w0[j], a1 = w1[i], b1 = w1[j];
+          w0[i] = cs * a0 - sn * b0; w0[j] = sn * a0 + cs * b0;
+          w1[i] = cs * a1 - sn * b1; w1[j] = sn * a1 + cs * b1;
+          const float ja = jr[i], jb = jr[j];
+          jr[i] = cs * ja - sn * jb; jr[j] = sn * ja + cs * jb;
+        }
+      }
+      if (off < 2e-7f) break;
+    }
+    // singular values, descending order (selection; q <= 8)
+    float sv[kCompMaxQ];
+#pragma unroll
+    for (int c = 0; c < kCompMaxQ; ++c) sv[c] = c < q ? sqrtf(warp_sum(w0[c] * w0[c] + w1[c] * w1[c])) : -1.f;
+    int order[kCompMaxQ];
+#pragma unroll
+    for (int c = 0; c < kCompMaxQ; ++c) order[c] = c;
+    for (int a = 0; a < q; ++a)
+      for (int b = a + 1; b < q; ++b)
+        if (sv[order[b]] > sv[order[a]]) { int tmp = order[a]; order[a] = order[b]; order[b] = tmp; }
+    // Z <- right singular vectors of Bm (= normalised columns of W), columns r < R
+    // J <- Ub (left), sorted; red[0..R) <- singular values
+    for (int r = 0; r < R; ++r) {
+      int c = order[0];
+#pragma unroll
+      for (int cc = 0; cc < kCompMaxQ; ++cc) if (cc < q && order[r] == cc) c = cc;
+      float wc0 = 0.f, wc1 = 0.f, jc = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < kCompMaxQ; ++cc) if (cc == c) { wc0 = w0[cc]; wc1 = w1[cc]; jc = jr[cc]; }
+      const float s = sv[c];
+      const float inv = s > 1e-30f ? 1.f / s : 0.f;
+      float v0 = wc0 * inv, v1 = wc1 * inv;
+      // sign: largest-|.| entry of the right vector positive (first index on ties)
+      float best = r0 ? fabsf(v0) : -1.f;
+      int bidx = lane;
+      float bval = v0;
+      if (r1 && fabsf(v1) > best) { best = fabsf(v1); bidx = lane + 32; bval = v1; }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, bval, o);
+        if (ob > best || (ob == best && oi < bidx)) { best = ob; bidx = oi; bval = ov; }
+      }
+      const float sg = bval < 0.f ? -1.f : 1.f;
+      if (r0) Z[lane * kCompMaxQ + r] = sg * v0;
+      if (r1) Z[(lane + 32) * kCompMaxQ + r] = sg * v1;
+      if (lane < q) J[lane * kCompMaxQ + r] = sg * jc;
+      if (lane == 0) red[32 + r] = s;
+    }
+  }
+  __syncthreads();
+  // blend: A_r += (1-d)(Q Ub_r S_r - A_r) ; B_r likewise with Vs_r
+  const float dd = d.delta, od = 1.f - d.delta;
+  for (int idx = tid; idx < R * m; idx += nt) {
+    const int r = idx / m, i = idx % m;
+    float acc = 0.f;
+    for (int c = 0; c < q; ++c) acc = fmaf(Qm[i * q + c], J[c * kCompMaxQ + r], acc);
+    A_s[idx] = dd * A_s[idx] + od * (acc * red[32 + r]);
+  }
+  for (int idx = tid; idx < R * n; idx += nt) {
+    const int r = idx / n, j = idx % n;
+    B_s[idx] = dd * B_s[idx] + od * Z[j * kCompMaxQ + r];
+  }
+  float kept = 0.f;
+  for (int r = 0; r < R; ++r) kept += red[32 + r] * red[32 + r];
+  __syncthreads();
+  return total - kept;
+}
+
+// Adds sum_r vec(A_r) vec(B_r)^T to Rm (m x ld), A_s [R][m], B_s [R][n].
+GDNX_DEV void add_kron_rmat(float* Rm, const float* A_s, const float* B_s, const CompactDims d) {
+  const int ld = compact_ld(d.n);
+  for (int idx = threadIdx.x; idx < d.m * d.n; idx += blockDim.x) {
+    const int i = idx / d.n, j = idx % d.n;
+    float acc = 0.f;
+    for (int r = 0; r < d.R; ++r) acc = fmaf(A_s[r * d.m + i], B_s[r * d.n + j], acc);
+    Rm[i * ld + j] += acc;
+  }
+}
+
+// Rearranged position of dense residual element (v, k):
+// R[(av, ak)][(bv, bk)] = S[av*b_v + bv][ak*b_k + bk].
+GDNX_DEV int rmat_index(int v, int k, const CompactDims d) {
+  const int av = v / d.b_v, bv = v % d.b_v, ak = k / d.b_k, bk = k % d.b_k;
+  return (av * d.a_k + ak) * compact_ld(d.n) + bv * d.b_k + bk;
+}
+
+// Rm += rearrange(U diag(dsl) Vb^T) for V*K <= 64*256, built in registers tile by
+// tile (dsl = per-slot scale, nullptr = 1).  Needs blockDim.x == kCompThreads.
+GDNX_DEV void add_residual_rmat(float* Rm, const float* U, const float* Vb, const float* dsl, int V, int K, int P,
+                                float* tileU, float* tileV, const CompactDims d) {
+  const int tid = threadIdx.x;
+  const int per = (V * K + kCompThreads - 1) / kCompThreads;  // <= 64
+  float acc[64];
+#pragma unroll
+  for (int e = 0; e < 64; ++e) acc[e] = 0.f;
+  for (int p0 = 0; p0 < P; p0 += kCompPT) {
+    const int np = min(kCompPT, P - p0);
+    __syncthreads();
+    for (int idx = tid; idx < V * kCompPT; idx += kCompThreads) {
+      const int vv = idx / kCompPT, pp = idx % kCompPT;
+      tileU[idx] = pp < np ? U[(int64_t)vv * P + p0 + pp] : 0.f;
+    }
+    for (int idx = tid; idx < K * kCompPT; idx += kCompThreads) {
+      const int kk = idx / kCompPT, pp = idx % kCompPT;
+      tileV[idx] = pp < np ? Vb[(int64_t)kk * P + p0 + pp] * (dsl ? dsl[p0 + pp] : 1.f) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < 64; ++e) {
+      if (e >= per) break;
+      const int idx = tid + kCompThreads * e;
+      if (idx >= V * K) break;
+      const int vv = idx / K, kk = idx % K;
+      float s = acc[e];
+#pragma unroll
+      for (int pp = 0; pp < kCompPT; ++pp) s = fmaf(tileU[vv * kCompPT + pp], tileV[kk * kCompPT + pp], s);
+      acc[e] = s;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 64; ++e) {
+    if (e >= per) break;
+    const int idx = tid + kCompThreads * e;
+    if (idx >= V * K) break;
+    Rm[rmat_index(idx / K, idx % K, d)] += acc[e];
+  }
+  __syncthreads();
+}
+
+}  // namespace gdnx

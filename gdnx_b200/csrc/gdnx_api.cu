@@ -1,0 +1,177 @@
+// C-ABI entry points: host-side validation and kernel dispatch.
+#include <cstdio>
+#include <cuda_runtime.h>
+
+#include "gdnx.h"
+#include "kernels.h"
+
+namespace {
+
+bool is_device_ptr(const void* p) {
+  if (p == nullptr) return false;
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+bool dtype_ok(int dt) { return dt == GDNX_F32 || dt == GDNX_BF16 || dt == GDNX_F16; }
+
+// A required view: device pointer, known dtype, the expected last-dim size.
+bool view_ok(const gdnx_view& v, int dim_a, int dim_b = -1) {
+  if (!is_device_ptr(v.ptr) || !dtype_ok(v.dtype)) return false;
+  if (v.dim != dim_a && v.dim != dim_b) return false;
+  if (v.sb < 0 || v.st < 0 || v.sh < 0 || v.sm < 0 || v.ss < 0) return false;
+  return true;
+}
+
+bool rope_ok(const gdnx_rope& r, int64_t K) {
+  if (!r.enable) return true;
+  for (int i = 0; i < 4; ++i) {
+    if (r.pairs[i] < 0 || 2 * (int64_t)r.pairs[i] > K) return false;
+    if (r.pairs[i] > 0 && !(r.den[i] > 0.f)) return false;
+  }
+  return r.pos0 >= 0;
+}
+
+gdnx_status check_common(int64_t B, int64_t H, int64_t M, int64_t K, int64_t V, int mode, int r_out,
+                         const gdnx_view& q, const gdnx_view& k, const gdnx_view& v,
+                         const gdnx_view& ge, const gdnx_view& gw, const gdnx_view& dec,
+                         int decay_kind, const gdnx_rope& rope, const float* out_mix) {
+  if (B < 0 || H <= 0 || M <= 0 || K <= 0 || V <= 0) return GDNX_EINVAL;
+  if (mode != GDNX_MODE_GDN3 && mode != GDNX_MODE_KMD2) return GDNX_EINVAL;
+  if (r_out < 1 || r_out > 16) return GDNX_EINVAL;
+  if (mode == GDNX_MODE_GDN3 && r_out != 1) return GDNX_EINVAL;
+  if (r_out > 1 && !is_device_ptr(out_mix)) return GDNX_EINVAL;
+  if (!view_ok(q, (int)K) || !view_ok(k, (int)K) || !view_ok(v, (int)V)) return GDNX_EINVAL;
+  if (mode == GDNX_MODE_GDN3) {
+    if (!view_ok(ge, (int)K, 1) || !view_ok(gw, (int)V, 1)) return GDNX_EINVAL;
+  } else {
+    if (!view_ok(ge, 1) || !view_ok(gw, 1)) return GDNX_EINVAL;
+  }
+  if (decay_kind == GDNX_DECAY_BRAIDED) {
+    if (!view_ok(dec, 4)) return GDNX_EINVAL;
+  } else if (decay_kind == GDNX_DECAY_GAMMA || decay_kind == GDNX_DECAY_LOG) {
+    if (!view_ok(dec, 1, (int)K)) return GDNX_EINVAL;
+  } else {
+    return GDNX_EINVAL;
+  }
+  if (!rope_ok(rope, K)) return GDNX_EINVAL;
+  if (rope.enable && M > 4) return GDNX_EINVAL;
+  return GDNX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gdnx_status_string(gdnx_status s) {
+  switch (s) {
+    case GDNX_OK: return "GDNX_OK";
+    case GDNX_EINVAL: return "GDNX_EINVAL: invalid argument (shape, stride, dtype, alignment or non-device pointer)";
+    case GDNX_ELAUNCH: return "GDNX_ELAUNCH: CUDA launch failed";
+    case GDNX_ETIMEOUT: return "GDNX_ETIMEOUT: a bounded device-side wait ran out";
+    case GDNX_EUNSUPPORTED: return "GDNX_EUNSUPPORTED: no kernel for this configuration in this build";
+    case GDNX_EWORKSPACE: return "GDNX_EWORKSPACE: workspace missing or too small";
+  }
+  return "GDNX_UNKNOWN";
+}
+
+const char* gdnx_version(void) { return "gdnx-b200 0.1 sm_100a"; }
+
+size_t gdnx_scan_workspace_bytes(const gdnx_scan_args* a) {
+  if (!a) return 0;
+  if (a->algo != GDNX_ALGO_RECURRENT && gdnx::chunked_eligible(*a)) return gdnx::chunked_workspace_bytes(*a);
+  return 0;
+}
+
+gdnx_status gdnx_scan_fwd(const gdnx_scan_args* a, void* stream) {
+  if (!a) return GDNX_EINVAL;
+  gdnx_status s = check_common(a->B, a->H, a->M, a->K, a->V, a->mode, a->r_out, a->q, a->k, a->v,
+                               a->gate_e, a->gate_w, a->decay, a->decay_kind, a->rope, a->out_mix);
+  if (s != GDNX_OK) return s;
+  if (a->T < 0) return GDNX_EINVAL;
+  if (!is_device_ptr(a->y) || !dtype_ok(a->y_dtype)) return GDNX_EINVAL;
+  if (a->scores && !is_device_ptr(a->scores)) return GDNX_EINVAL;
+  if (a->state_in && !is_device_ptr(a->state_in)) return GDNX_EINVAL;
+  if (a->state_out && !is_device_ptr(a->state_out)) return GDNX_EINVAL;
+  if (a->B == 0 || a->T == 0) {
+    // nothing to scan: the final state equals the initial one
+    if (a->state_out && a->state_out != a->state_in) {
+      const size_t bytes = (size_t)(a->B * a->H * a->M * a->V * a->K) * sizeof(float);
+      cudaError_t e = a->state_in
+          ? cudaMemcpyAsync(a->state_out, a->state_in, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
+          : cudaMemsetAsync(a->state_out, 0, bytes, (cudaStream_t)stream);
+      if (e != cudaSuccess) return GDNX_ELAUNCH;
+    }
+    return GDNX_OK;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool chunk_ok = gdnx::chunked_eligible(*a);
+  if (a->algo == GDNX_ALGO_CHUNKED && !chunk_ok) return GDNX_EUNSUPPORTED;
+  if (a->algo != GDNX_ALGO_RECURRENT && chunk_ok) {
+    if (a->workspace_bytes < gdnx::chunked_workspace_bytes(*a)) return GDNX_EWORKSPACE;
+    if (gdnx::chunked_workspace_bytes(*a) && !is_device_ptr(a->workspace)) return GDNX_EWORKSPACE;
+    return gdnx::launch_chunked_scan(*a, st);
+  }
+  return gdnx::launch_recurrent_scan(*a, st);
+}
+
+gdnx_status gdnx_decode_step(const gdnx_decode_args* a, void* stream) {
+  if (!a) return GDNX_EINVAL;
+  gdnx_status s = check_common(a->B, a->H, a->M, a->K, a->V, a->mode, a->r_out, a->q, a->k, a->v,
+                               a->gate_e, a->gate_w, a->decay, a->decay_kind, a->rope, a->out_mix);
+  if (s != GDNX_OK) return s;
+  if (!is_device_ptr(a->S) || !is_device_ptr(a->y) || !dtype_ok(a->y_dtype)) return GDNX_EINVAL;
+  if (a->B == 0) return GDNX_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a->K == 128 && a->V == 128) return gdnx::launch_decode_128(*a, st);
+  // other head sizes: one step of the exact recurrent kernel, state in place
+  gdnx_scan_args sa = {};
+  sa.B = a->B; sa.T = 1; sa.H = a->H; sa.M = a->M; sa.K = a->K; sa.V = a->V;
+  sa.mode = a->mode; sa.algo = GDNX_ALGO_RECURRENT; sa.r_out = a->r_out; sa.chunk = 64;
+  sa.q = a->q; sa.k = a->k; sa.v = a->v; sa.gate_e = a->gate_e; sa.gate_w = a->gate_w;
+  sa.decay = a->decay; sa.decay_kind = a->decay_kind;
+  for (int i = 0; i < 4; ++i) sa.braid_rates[i] = a->braid_rates[i];
+  sa.braid_clamp = a->braid_clamp;
+  sa.rope = a->rope;
+  sa.out_mix = a->out_mix;
+  sa.y = a->y; sa.y_dtype = a->y_dtype;
+  sa.y_sb = a->y_sb; sa.y_st = 0; sa.y_sh = a->y_sh; sa.y_sm = a->y_sm;
+  sa.state_in = a->S; sa.state_out = a->S;
+  return gdnx::launch_recurrent_scan(sa, st);
+}
+
+gdnx_status gdnx_compact(const gdnx_compact_args* a, void* stream) {
+  if (!a) return GDNX_EINVAL;
+  if (a->N < 0 || a->R < 1 || a->P < 1) return GDNX_EINVAL;
+  if (a->a_v * a->b_v != a->V || a->a_k * a->b_k != a->K) return GDNX_EINVAL;
+  if (a->N == 0) return GDNX_OK;
+  if (!is_device_ptr(a->sketch) || !is_device_ptr(a->A) || !is_device_ptr(a->Bk) ||
+      !is_device_ptr(a->U) || !is_device_ptr(a->Vb))
+    return GDNX_EINVAL;
+  if (a->err && !is_device_ptr(a->err)) return GDNX_EINVAL;
+  return gdnx::launch_compact(*a, (cudaStream_t)stream);
+}
+
+gdnx_status gdnx_kr_scan_fwd(const gdnx_kr_scan_args* a, void* stream) {
+  if (!a) return GDNX_EINVAL;
+  const gdnx_scan_args& b = a->base;
+  if (b.mode != GDNX_MODE_GDN3) return GDNX_EINVAL;
+  gdnx_status s = check_common(b.B, b.H, b.M, b.K, b.V, b.mode, b.r_out, b.q, b.k, b.v,
+                               b.gate_e, b.gate_w, b.decay, b.decay_kind, b.rope, b.out_mix);
+  if (s != GDNX_OK) return s;
+  if (b.decay.dim != 1 && b.decay_kind != GDNX_DECAY_BRAIDED) return GDNX_EINVAL;  // scalar decay per chain
+  if (b.T < 0 || !is_device_ptr(b.y) || !dtype_ok(b.y_dtype)) return GDNX_EINVAL;
+  if (a->R < 1 || a->P < 1 || a->a_v * a->b_v != b.V || a->a_k * a->b_k != b.K) return GDNX_EINVAL;
+  if (!is_device_ptr(a->sketch) || !is_device_ptr(a->A) || !is_device_ptr(a->Bk) ||
+      !is_device_ptr(a->U) || !is_device_ptr(a->Vb) || !is_device_ptr(a->slot))
+    return GDNX_EINVAL;
+  if (a->comp_err && !is_device_ptr(a->comp_err)) return GDNX_EINVAL;
+  if (b.B == 0 || b.T == 0) return GDNX_OK;
+  return gdnx::launch_kr_scan(*a, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,330 @@
+// GDN3 Kronecker-residual scan with periodic compaction (gdnx_kr_scan_fwd).
+//
+// Semantics: the frozen token loop gdn3/_reference_recurrence.py:60-90, per
+// chain and token
+//     A *= g; Bk *= g; Vb *= g                       (Kronecker part decays g^2)
+//     h = b(.)k ; u = w(.)v ; r = u - S h ; a = alpha(k.h)
+//     y = S q + a (k.q) r ;  U[:,p] = a r ; Vb[:,p] = k ; p += 1
+//     p == P  ->  compaction (A, Bk blended, U/Vb kept) ; p = 0
+// with S x = vec(sum_r A_r X B_r^T) + U (Vb^T x).
+//
+// Design (one CTA of 256 threads per chain):
+//  * the residual operator U Vb^T (V x K) is kept DENSE in registers, row v
+//    split over TPR threads; each token applies the rank-2 update
+//    "decay, evict the overwritten slot, add the new write".  It is rebuilt
+//    exactly from the slots at every compaction (and at call start), so
+//    rounding cannot drift over a long sequence;
+//  * the slot ring lives in the caller's U / Vb buffers (global, L2
+//    resident).  New writes store the raw key and a per-slot decay factor
+//    d_p (smem) carries Vb = d_p k_p, exactly the product of per-token
+//    decays the reference applies;
+//  * A, Bk live in shared memory with one pending scalar decay fac
+//    (true A = fac A_s), folded in before each compaction;
+//  * the Kronecker read uses Z_r = X B_r^T computed cooperatively for the
+//    TB staged tokens, then each row contracts A_r (16 x 16) with Z_r;
+//  * compaction runs in-kernel on shared memory (compact.cuh).
+#include "compact.cuh"
+#include "kernels.h"
+
+namespace gdnx {
+namespace {
+
+constexpr int kNT = kCompThreads;  // 256
+constexpr int kTB = 8;             // tokens staged per block (<= P handled by the block split)
+constexpr int kMaxP = 1024;
+
+struct KrParams {
+  gdnx_kr_scan_args a;
+  CompactDims d;
+  int vec_e, vec_w;
+};
+
+template <int K, int V>
+struct KrSmem {
+  static constexpr int kTokK = 0, kTokH = K, kTokQ = 2 * K, kTokKold = 3 * K;
+  static constexpr int kTokU = 4 * K, kTokUold = 4 * K + V, kTokSc = 4 * K + 2 * V;
+  static constexpr int kTokPer = 4 * K + 2 * V + 8;
+};
+
+template <int K, int V>
+__global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
+  constexpr int TPR = kNT / V;     // threads per state row
+  constexpr int KC = K / 4 / TPR;  // float4 key chunks per thread
+  using SMT = KrSmem<K, V>;
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const gdnx_kr_scan_args& A = P.a;
+  const gdnx_scan_args& a = A.base;
+  const CompactDims d = P.d;
+  const int R = d.R, Pn = A.P;
+  const int zper = R * d.a_k * d.b_v;  // Z floats per vector
+  const int ld = compact_ld(d.n);
+
+  // ---- shared memory carve-up ----
+  float* Rm = sm;                                  // m x ld (compaction / rebuild)
+  float* work = Rm + d.m * ld;                     // compaction work
+  float* A_s = work + compact_work_floats();       // R x m
+  float* B_s = A_s + R * d.m;                      // R x n
+  float* dsl = B_s + R * d.n;                      // per-slot decay [P]
+  float* tok = dsl + kMaxP;                        // kTB x kTokPer
+  float* Zb = tok + kTB * SMT::kTokPer;            // kTB x 2 x zper
+  float* ybuf = Zb + kTB * 2 * zper;               // kTB x V
+  float* nbuf = ybuf + kTB * V;                    // kTB x V (new U columns)
+  float* tileU = nbuf + kTB * V;                   // V x kCompPT
+  float* tileV = tileU + V * kCompPT;              // K x kCompPT
+  float* misc = tileV + K * kCompPT;               // 32 floats
+
+  const int64_t n = blockIdx.x;
+  const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int v = tid / TPR, j = tid % TPR;
+  const int av = v / d.b_v, bv = v % d.b_v;
+
+  float* Ug = A.U + n * (int64_t)V * Pn;
+  float* Vg = A.Vb + n * (int64_t)K * Pn;
+  float* Ag = A.A + n * (int64_t)R * d.m;
+  float* Bg = A.Bk + n * (int64_t)R * d.n;
+  const float* Gg = A.sketch + n * (int64_t)d.n * d.q;
+
+  for (int i = tid; i < R * d.m; i += kNT) A_s[i] = Ag[i];
+  for (int i = tid; i < R * d.n; i += kNT) B_s[i] = Bg[i];
+  for (int i = tid; i < Pn; i += kNT) dsl[i] = 1.f;
+  int p = A.slot[n];
+  float fac = 1.f, err_acc = 0.f;
+
+  float4 Rs[KC];
+  // rebuild the dense residual from the slots (exact) into registers
+  auto rebuild = [&]() {
+    for (int i = tid; i < d.m * ld; i += kNT) Rm[i] = 0.f;
+    __syncthreads();
+    add_residual_rmat(Rm, Ug, Vg, dsl, V, K, Pn, tileU, tileV, d);
+#pragma unroll
+    for (int c = 0; c < KC; ++c) {
+      const int k0 = 4 * (c * TPR + j);
+      Rs[c].x = Rm[rmat_index(v, k0 + 0, d)];
+      Rs[c].y = Rm[rmat_index(v, k0 + 1, d)];
+      Rs[c].z = Rm[rmat_index(v, k0 + 2, d)];
+      Rs[c].w = Rm[rmat_index(v, k0 + 3, d)];
+    }
+    __syncthreads();
+  };
+  rebuild();
+
+  int64_t t0 = 0;
+  while (t0 < a.T) {
+    int64_t nt64 = a.T - t0;
+    if (nt64 > kTB) nt64 = kTB;
+    if (nt64 > Pn - p) nt64 = Pn - p;
+    const int nt = (int)nt64;
+    // ---------- stage A: per-token vectors (one warp per token) ----------
+    for (int tt = warp; tt < nt; tt += kNT / 32) {
+      const int64_t t = t0 + tt;
+      float* tk = tok + tt * SMT::kTokPer;
+      float* sk = tk + SMT::kTokK;
+      float* sh = tk + SMT::kTokH;
+      float* sq = tk + SMT::kTokQ;
+      const int64_t ko = view_off(a.k, b, t, h, m), qo = view_off(a.q, b, t, h, m);
+      for (int i = lane; i < K; i += 32) {
+        sk[i] = ld_as_f32(a.k.ptr, a.k.dtype, ko + i);
+        sq[i] = ld_as_f32(a.q.ptr, a.q.dtype, qo + i);
+      }
+      __syncwarp();
+      rope_row_warp(sk, a.rope, (int)m, a.rope.pos0 + t, lane);
+      rope_row_warp(sq, a.rope, (int)m, a.rope.pos0 + t, lane);
+      __syncwarp();
+      const int64_t eo = view_off(a.gate_e, b, t, h, m), wo = view_off(a.gate_w, b, t, h, m);
+      const float be = P.vec_e ? 1.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
+      const float bw = P.vec_w ? 1.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo);
+      float kh = 0.f, kq = 0.f;
+      const int ps = p + tt;  // slot overwritten by this token
+      for (int i = lane; i < K; i += 32) {
+        const float hv = (P.vec_e ? ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo + i) : be) * sk[i];
+        sh[i] = hv;
+        kh += sk[i] * hv;
+        kq += sk[i] * sq[i];
+        tk[SMT::kTokKold + i] = Vg[(int64_t)i * Pn + ps];
+      }
+      kh = warp_sum(kh);
+      kq = warp_sum(kq);
+      const int64_t vo = view_off(a.v, b, t, h, m);
+      for (int i = lane; i < V; i += 32) {
+        const float wv = P.vec_w ? ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo + i) : bw;
+        tk[SMT::kTokU + i] = wv * ld_as_f32(a.v.ptr, a.v.dtype, vo + i);
+        tk[SMT::kTokUold + i] = Ug[(int64_t)i * Pn + ps];
+      }
+      if (lane == 0) {
+        float* sc = tk + SMT::kTokSc;
+        sc[0] = decay_factor(a.decay, a.decay_kind, view_off(a.decay, b, t, h, m), true, a.braid_rates,
+                             a.braid_clamp);
+        sc[1] = stable_alpha(kh);
+        sc[2] = kq;
+      }
+    }
+    __syncthreads();
+    // ---------- stage B: running decays (thread 0) and Z = X B^T (all) ----------
+    if (tid == 0) {
+      float f = fac, pre = 1.f;
+      for (int tt = 0; tt < nt; ++tt) {
+        float* sc = tok + tt * SMT::kTokPer + SMT::kTokSc;
+        f *= sc[0];
+        pre *= sc[0];
+        sc[3] = f * f;                  // Kronecker scale
+        sc[4] = dsl[p + tt] * pre;      // decay of the evicted slot through t
+      }
+      misc[0] = f;
+      misc[1] = pre;
+    }
+    for (int idx = tid; idx < nt * 2 * zper; idx += kNT) {
+      const int tt = idx / (2 * zper), rem = idx % (2 * zper);
+      const int which = rem / zper, z = rem % zper;    // 0: h, 1: q
+      const int r = z / (d.a_k * d.b_v), ak = (z / d.b_v) % d.a_k, bvv = z % d.b_v;
+      const float* x = tok + tt * SMT::kTokPer + (which ? SMT::kTokQ : SMT::kTokH) + ak * d.b_k;
+      const float* br = B_s + r * d.n + bvv * d.b_k;
+      float acc = 0.f;
+      for (int bk = 0; bk < d.b_k; ++bk) acc = fmaf(x[bk], br[bk], acc);
+      Zb[idx] = acc;
+    }
+    __syncthreads();
+    // ---------- sequential token updates ----------
+    for (int tt = 0; tt < nt; ++tt) {
+      const float* tk = tok + tt * SMT::kTokPer;
+      const float* sc = tk + SMT::kTokSc;
+      const float gam = sc[0], al = sc[1], kq = sc[2], ks = sc[3], ev = sc[4];
+      // Kronecker reads (row v): sum_{r,ak} A_r[av][ak] Z_r[ak][bv], split over j
+      const float* Zh = Zb + tt * 2 * zper;
+      const float* Zq = Zh + zper;
+      float krh = 0.f, krq = 0.f;
+      for (int e = j; e < R * d.a_k; e += TPR) {
+        const int r = e / d.a_k, ak = e % d.a_k;
+        const float aw = A_s[r * d.m + av * d.a_k + ak];
+        const int zi = (r * d.a_k + ak) * d.b_v + bv;
+        krh = fmaf(aw, Zh[zi], krh);
+        krq = fmaf(aw, Zq[zi], krq);
+      }
+      float dh = 0.f, dq = 0.f;
+#pragma unroll
+      for (int c = 0; c < KC; ++c) {
+        const int k0 = 4 * (c * TPR + j);
+        const float4 h4 = *reinterpret_cast<const float4*>(tk + SMT::kTokH + k0);
+        const float4 q4 = *reinterpret_cast<const float4*>(tk + SMT::kTokQ + k0);
+        dh = fmaf(Rs[c].x, h4.x, dh); dh = fmaf(Rs[c].y, h4.y, dh);
+        dh = fmaf(Rs[c].z, h4.z, dh); dh = fmaf(Rs[c].w, h4.w, dh);
+        dq = fmaf(Rs[c].x, q4.x, dq); dq = fmaf(Rs[c].y, q4.y, dq);
+        dq = fmaf(Rs[c].z, q4.z, dq); dq = fmaf(Rs[c].w, q4.w, dq);
+      }
+#pragma unroll
+      for (int o = 1; o < TPR; o <<= 1) {
+        krh += __shfl_xor_sync(0xffffffffu, krh, o);
+        krq += __shfl_xor_sync(0xffffffffu, krq, o);
+        dh += __shfl_xor_sync(0xffffffffu, dh, o);
+        dq += __shfl_xor_sync(0xffffffffu, dq, o);
+      }
+      const float s_h = ks * krh + gam * dh;
+      const float r = tk[SMT::kTokU + v] - s_h;
+      const float wnew = al * r;
+      const float y = ks * krq + gam * dq + al * kq * r;
+      const float cold = tk[SMT::kTokUold + v] * ev;
+#pragma unroll
+      for (int c = 0; c < KC; ++c) {
+        const int k0 = 4 * (c * TPR + j);
+        const float4 ko4 = *reinterpret_cast<const float4*>(tk + SMT::kTokKold + k0);
+        const float4 k4 = *reinterpret_cast<const float4*>(tk + SMT::kTokK + k0);
+        Rs[c].x = fmaf(gam, Rs[c].x, fmaf(wnew, k4.x, -cold * ko4.x));
+        Rs[c].y = fmaf(gam, Rs[c].y, fmaf(wnew, k4.y, -cold * ko4.y));
+        Rs[c].z = fmaf(gam, Rs[c].z, fmaf(wnew, k4.z, -cold * ko4.z));
+        Rs[c].w = fmaf(gam, Rs[c].w, fmaf(wnew, k4.w, -cold * ko4.w));
+      }
+      if (j == 0) {
+        ybuf[tt * V + v] = y;
+        nbuf[tt * V + v] = wnew;
+      }
+    }
+    __syncthreads();
+    // ---------- flush: outputs, new slots, slot decays ----------
+    for (int idx = tid; idx < nt * V; idx += kNT) {
+      const int tt = idx / V, vv = idx % V;
+      st_from_f32(a.y, a.y_dtype, b * a.y_sb + (t0 + tt) * a.y_st + h * a.y_sh + m * a.y_sm + vv, ybuf[idx]);
+    }
+    for (int idx = tid; idx < V * nt; idx += kNT) {
+      const int vv = idx / nt, tt = idx % nt;
+      Ug[(int64_t)vv * Pn + p + tt] = nbuf[tt * V + vv];
+    }
+    for (int idx = tid; idx < K * nt; idx += kNT) {
+      const int kk = idx / nt, tt = idx % nt;
+      Vg[(int64_t)kk * Pn + p + tt] = tok[tt * SMT::kTokPer + SMT::kTokK + kk];
+    }
+    {
+      const float pre = misc[1];
+      for (int s = tid; s < Pn; s += kNT) {
+        if (s >= p && s < p + nt) {
+          float f = 1.f;  // decays after the write, through the block end
+          for (int u = s - p + 1; u < nt; ++u) f *= tok[u * SMT::kTokPer + SMT::kTokSc];
+          dsl[s] = f;
+        } else {
+          dsl[s] *= pre;
+        }
+      }
+    }
+    fac = misc[0];
+    p += nt;
+    t0 += nt;
+    __syncthreads();
+    if (p == Pn) {
+      // ---------- compaction at the window end ----------
+      for (int i = tid; i < R * d.m; i += kNT) A_s[i] *= fac;
+      for (int i = tid; i < R * d.n; i += kNT) B_s[i] *= fac;
+      fac = 1.f;
+      rebuild();                      // Rm = rearrange(U Vb^T), Rs exact again
+      add_kron_rmat(Rm, A_s, B_s, d);
+      __syncthreads();
+      err_acc += compact_core(Rm, A_s, B_s, Gg, work, d);
+      p = 0;
+      __syncthreads();
+    }
+  }
+  // ---------- materialise the state ----------
+  for (int i = tid; i < R * d.m; i += kNT) Ag[i] = A_s[i] * fac;
+  for (int i = tid; i < R * d.n; i += kNT) Bg[i] = B_s[i] * fac;
+  for (int idx = tid; idx < K * Pn; idx += kNT) Vg[idx] *= dsl[idx % Pn];
+  if (tid == 0) {
+    A.slot[n] = p;
+    if (A.comp_err) A.comp_err[n] += err_acc;
+  }
+}
+
+template <int K, int V>
+gdnx_status launch_kr(const KrParams& P, cudaStream_t st) {
+  const CompactDims& d = P.d;
+  const int zper = d.R * d.a_k * d.b_v;
+  const size_t floats = (size_t)d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) + kMaxP +
+                        kTB * KrSmem<K, V>::kTokPer + kTB * 2 * zper + 2 * kTB * V + (V + K) * kCompPT + 32;
+  const size_t smem = floats * sizeof(float);
+  auto fn = kr_scan_kernel<K, V>;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return GDNX_ELAUNCH;
+  const int64_t N = P.a.base.B * P.a.base.H * P.a.base.M;
+  fn<<<(unsigned)N, kNT, smem, st>>>(P);
+  return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+}
+
+}  // namespace
+
+gdnx_status launch_kr_scan(const gdnx_kr_scan_args& a, cudaStream_t st) {
+  KrParams P;
+  P.a = a;
+  P.vec_e = a.base.gate_e.dim > 1;
+  P.vec_w = a.base.gate_w.dim > 1;
+  CompactDims& d = P.d;
+  d.R = a.R; d.a_v = a.a_v; d.a_k = a.a_k; d.b_v = a.b_v; d.b_k = a.b_k;
+  d.m = a.a_v * a.a_k; d.n = a.b_v * a.b_k;
+  d.q = min(a.R + 4, min(d.m, d.n));
+  d.delta = a.slow_decay;
+  if (d.m > kCompMaxM || d.n > kCompMaxN || d.q > kCompMaxQ || d.R > d.q) return GDNX_EUNSUPPORTED;
+  if (a.P > kMaxP) return GDNX_EUNSUPPORTED;
+  const int64_t K = a.base.K, V = a.base.V;
+  if (K == 128 && V == 128) return launch_kr<128, 128>(P, st);
+  if (K == 64 && V == 64) return launch_kr<64, 64>(P, st);
+  return GDNX_EUNSUPPORTED;
+}
+
+}  // namespace gdnx

@@ -1,0 +1,346 @@
+"""Torch-tensor front end of the C ABI (device memory and streams come from torch).
+
+Every function validates on the host, builds the POD argument struct of
+``include/gdnx.h`` from tensor pointers and strides, and enqueues the CUDA
+kernel on ``torch.cuda.current_stream()``.  CPU tensors are rejected; there
+is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+from .prologue import BRAID_RATES, DECAY_CLAMP, LaneRope
+
+_DT = {torch.float32: L.GDNX_F32, torch.bfloat16: L.GDNX_BF16, torch.float16: L.GDNX_F16}
+_DECAY = {"gamma": L.GDNX_DECAY_GAMMA, "log": L.GDNX_DECAY_LOG, "braided": L.GDNX_DECAY_BRAIDED}
+_ALGO = {"auto": L.GDNX_ALGO_AUTO, "recurrent": L.GDNX_ALGO_RECURRENT, "chunked": L.GDNX_ALGO_CHUNKED}
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("gdnx_b200 kernels take CUDA tensors only (no CPU fallback)")
+
+
+def _stream(dev) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _view(t: Optional[torch.Tensor], lanes: bool, slots: bool = False) -> L.View:
+    """View of a [B,T,H,(M,)(S,)D] tensor.  ``lanes`` says whether a lane dim is present."""
+    v = L.View()
+    if t is None:
+        return v
+    if t.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    if t.shape[-1] > 1 and t.stride(-1) != 1:
+        raise ValueError("the last dim of every input must be contiguous")
+    s = t.stride()
+    v.ptr = t.data_ptr()
+    v.dtype = _DT[t.dtype]
+    v.dim = t.shape[-1]
+    v.sb, v.st, v.sh = s[0], s[1], s[2]
+    i = 3
+    if lanes:
+        v.sm = s[i]; i += 1
+    if slots:
+        v.ss = s[i]; i += 1
+    return v
+
+
+def _rope_struct(rope: Optional[LaneRope]) -> L.Rope:
+    r = L.Rope()
+    if rope is None:
+        return r
+    r.enable = 1
+    for i in range(4):
+        r.pairs[i] = rope.pairs[i]
+        r.scale[i] = rope.scale[i]
+        r.den[i] = rope.den[i]
+    r.pos0 = rope.pos0
+    return r
+
+
+def _fill_decay(args, decay, decay_kind, braid_rates, braid_clamp):
+    args.decay_kind = _DECAY[decay_kind]
+    for i in range(4):
+        args.braid_rates[i] = braid_rates[i]
+    args.braid_clamp = braid_clamp
+
+
+def _lanes_expand(x, M):
+    """[B,T,H,D] (lane-shared) -> stride-0 [B,T,H,M,D] view; [B,T,H,M,D] unchanged."""
+    if x.dim() == 4:
+        return x.unsqueeze(3).expand(-1, -1, -1, M, -1)
+    return x
+
+
+def _gate(x, D):
+    """[B,T,H,M] scalar gate -> [B,T,H,M,1]; [B,T,H,M,D] vector gate unchanged."""
+    if x.dim() == 4:
+        return x.unsqueeze(-1)
+    if x.shape[-1] not in (1, D):
+        raise ValueError("gate last dim must be 1 or the feature size")
+    return x
+
+
+# ----------------------------------------------------------------------------
+# dense scan (GDN3 with compaction off; KMD-2)
+# ----------------------------------------------------------------------------
+
+def gdn3_scan(q, k, v, b_gate, w_gate, decay, *, decay_kind="gamma", rope: Optional[LaneRope] = None,
+              state: Optional[torch.Tensor] = None, return_state: bool = False,
+              out_dtype: Optional[torch.dtype] = None, algo: str = "auto",
+              braid_rates=BRAID_RATES, braid_clamp=DECAY_CLAMP, out: Optional[torch.Tensor] = None,
+              workspace: Optional[torch.Tensor] = None):
+    """Dense GDN3 scan.  q, k: [B,T,H,(M,)K]; v: [B,T,H,(M,)V]; b_gate: [B,T,H,M(,K)];
+    w_gate: [B,T,H,M(,V)]; decay: [B,T,H,M] (or [B,T,H,M,4] braided logits).
+
+    Returns y [B,T,H,M,V] (and the final state [B*H*M, V, K] fp32 if asked).
+    """
+    B, T, H = k.shape[:3]
+    M = b_gate.shape[3]
+    K, V = k.shape[-1], v.shape[-1]
+    _require_cuda(q, k, v, b_gate, w_gate, decay, state)
+    qx, kx, vx = _lanes_expand(q, M), _lanes_expand(k, M), _lanes_expand(v, M)
+    bg, wg = _gate(b_gate, K), _gate(w_gate, V)
+    dec = decay if decay_kind == "braided" else decay.unsqueeze(-1)
+    out_dtype = out_dtype or (torch.float32 if q.dtype == torch.float32 else q.dtype)
+    y = out if out is not None else torch.empty(B, T, H, M, V, dtype=out_dtype, device=q.device)
+    a = L.ScanArgs()
+    a.B, a.T, a.H, a.M, a.K, a.V = B, T, H, M, K, V
+    a.mode, a.algo, a.r_out, a.chunk = L.GDNX_MODE_GDN3, _ALGO[algo], 1, 64
+    a.q, a.k, a.v = _view(qx, True), _view(kx, True), _view(vx, True)
+    a.gate_e, a.gate_w, a.decay = _view(bg, True), _view(wg, True), _view(dec, True)
+    _fill_decay(a, dec, decay_kind, braid_rates, braid_clamp)
+    a.rope = _rope_struct(rope)
+    a.y, a.y_dtype = y.data_ptr(), _DT[y.dtype]
+    a.y_sb, a.y_st, a.y_sh, a.y_sm = y.stride()[:4]
+    st_out = None
+    if state is not None:
+        if state.dtype != torch.float32 or not state.is_contiguous() or state.shape != (B * H * M, V, K):
+            raise ValueError("state must be contiguous fp32 [B*H*M, V, K]")
+        a.state_in = state.data_ptr()
+    if return_state:
+        st_out = torch.empty(B * H * M, V, K, dtype=torch.float32, device=q.device)
+        a.state_out = st_out.data_ptr()
+    _run_scan(a, q.device, workspace)
+    return (y, st_out) if return_state else y
+
+
+def _run_scan(a, device, workspace):
+    lib = L.load()
+    need = lib.gdnx_scan_workspace_bytes(C.byref(a))
+    ws = workspace
+    if need:
+        if ws is None or ws.numel() * ws.element_size() < need:
+            ws = torch.empty(need, dtype=torch.uint8, device=device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel() * ws.element_size()
+    with torch.cuda.device(device):
+        L.check(lib.gdnx_scan_fwd(C.byref(a), C.c_void_p(_stream(device))), "gdnx_scan_fwd")
+
+
+def kmd2_scan(q, k, v, g, beta_e, beta_w, out_mix=None, *, scores: bool = False,
+              state: Optional[torch.Tensor] = None, return_state: bool = False,
+              out_dtype: Optional[torch.dtype] = None, algo: str = "auto"):
+    """KMD-2 scan.  q [B,T,H,r,dk], k/g [B,T,H,dk] (g may be [B,T,H] scalar), v [B,T,H,dv],
+    beta_e/beta_w [B,T,H], out_mix [H,r] (r > 1).  Returns y [B,T,H,dv]
+    (+ scores [B,T,H] and/or final state [B*H, dv, dk] fp32)."""
+    B, T, H, r_out, dk = q.shape
+    dv = v.shape[-1]
+    _require_cuda(q, k, v, g, beta_e, beta_w, out_mix, state)
+    out_dtype = out_dtype or torch.float32
+    y = torch.empty(B, T, H, 1, dv, dtype=out_dtype, device=q.device)
+    sc = torch.empty(B, T, H, 1, dtype=torch.float32, device=q.device) if scores else None
+    a = L.ScanArgs()
+    a.B, a.T, a.H, a.M, a.K, a.V = B, T, H, 1, dk, dv
+    a.mode, a.algo, a.r_out, a.chunk = L.GDNX_MODE_KMD2, _ALGO[algo], r_out, 64
+    a.q = _view(q, False, slots=True)
+    a.k, a.v = _view(k, False), _view(v, False)
+    a.gate_e, a.gate_w = _view(beta_e.unsqueeze(-1), False), _view(beta_w.unsqueeze(-1), False)
+    gg = g if g.dim() == 4 else g.unsqueeze(-1)
+    a.decay = _view(gg, False)
+    _fill_decay(a, gg, "gamma", BRAID_RATES, DECAY_CLAMP)
+    mix = None
+    if r_out > 1:
+        if out_mix is None:
+            raise ValueError("out_mix is required when r_out > 1")
+        mix = out_mix.detach().to(torch.float32).contiguous()
+        a.out_mix = mix.data_ptr()
+    a.y, a.y_dtype = y.data_ptr(), _DT[y.dtype]
+    a.y_sb, a.y_st, a.y_sh, a.y_sm = y.stride()[:4]
+    if sc is not None:
+        a.scores = sc.data_ptr()
+    st_out = None
+    if state is not None:
+        if state.dtype != torch.float32 or not state.is_contiguous() or state.shape != (B * H, dv, dk):
+            raise ValueError("state must be contiguous fp32 [B*H, dv, dk]")
+        a.state_in = state.data_ptr()
+    if return_state:
+        st_out = torch.empty(B * H, dv, dk, dtype=torch.float32, device=q.device)
+        a.state_out = st_out.data_ptr()
+    _run_scan(a, q.device, None)
+    outs = [y[:, :, :, 0]]
+    if scores:
+        outs.append(sc[..., 0])
+    if return_state:
+        outs.append(st_out)
+    return outs[0] if len(outs) == 1 else tuple(outs)
+
+
+# ----------------------------------------------------------------------------
+# GDN3 Kronecker-residual scan + compaction
+# ----------------------------------------------------------------------------
+
+@dataclass
+class KRState:
+    """Device state of the GDN3-KR recurrence (reference layouts,
+    gdn3/_reference_recurrence.py:52-55) plus the slot pointer per chain."""
+    A: torch.Tensor      # [N,R,a_v,a_k]
+    Bk: torch.Tensor     # [N,R,b_v,b_k]
+    U: torch.Tensor      # [N,V,P]
+    Vb: torch.Tensor     # [N,K,P]
+    slot: torch.Tensor   # [N] int32
+    err: torch.Tensor    # [N] fp32 accumulated discarded energy
+
+    @staticmethod
+    def zeros(N, R, P, dims, V, K, device):
+        a_v, a_k, b_v, b_k = dims
+        f = dict(dtype=torch.float32, device=device)
+        return KRState(torch.zeros(N, R, a_v, a_k, **f), torch.zeros(N, R, b_v, b_k, **f),
+                       torch.zeros(N, V, P, **f), torch.zeros(N, K, P, **f),
+                       torch.zeros(N, dtype=torch.int32, device=device), torch.zeros(N, **f))
+
+
+def gdn3_kr_scan(q, k, v, b_gate, w_gate, decay, state: KRState, sketch: torch.Tensor, *,
+                 P: int, R: int = 4, dims=(16, 16, 8, 8), slow_decay: float = 0.97,
+                 decay_kind: str = "gamma", rope: Optional[LaneRope] = None,
+                 out_dtype: Optional[torch.dtype] = None, braid_rates=BRAID_RATES,
+                 braid_clamp=DECAY_CLAMP):
+    """GDN3-KR scan continuing ``state`` in place.  Shapes as ``gdn3_scan``;
+    ``sketch`` is the compaction sketch G [N, b_v*b_k, q] (fp32)."""
+    B, T, H = k.shape[:3]
+    M = b_gate.shape[3]
+    K, V = k.shape[-1], v.shape[-1]
+    N = B * H * M
+    _require_cuda(q, k, v, b_gate, w_gate, decay, sketch)
+    for t in (state.A, state.Bk, state.U, state.Vb, state.err, sketch):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("KR state and sketch must be contiguous fp32")
+    if state.U.shape != (N, V, P) or state.Vb.shape != (N, K, P):
+        raise ValueError("state U/Vb shapes do not match [N,V,P]/[N,K,P]")
+    qx, kx, vx = _lanes_expand(q, M), _lanes_expand(k, M), _lanes_expand(v, M)
+    bg, wg = _gate(b_gate, K), _gate(w_gate, V)
+    dec = decay if decay_kind == "braided" else decay.unsqueeze(-1)
+    out_dtype = out_dtype or (torch.float32 if q.dtype == torch.float32 else q.dtype)
+    y = torch.empty(B, T, H, M, V, dtype=out_dtype, device=q.device)
+    ka = L.KrScanArgs()
+    a = ka.base
+    a.B, a.T, a.H, a.M, a.K, a.V = B, T, H, M, K, V
+    a.mode, a.algo, a.r_out, a.chunk = L.GDNX_MODE_GDN3, L.GDNX_ALGO_RECURRENT, 1, 64
+    a.q, a.k, a.v = _view(qx, True), _view(kx, True), _view(vx, True)
+    a.gate_e, a.gate_w, a.decay = _view(bg, True), _view(wg, True), _view(dec, True)
+    _fill_decay(a, dec, decay_kind, braid_rates, braid_clamp)
+    a.rope = _rope_struct(rope)
+    a.y, a.y_dtype = y.data_ptr(), _DT[y.dtype]
+    a.y_sb, a.y_st, a.y_sh, a.y_sm = y.stride()[:4]
+    ka.R, ka.P = R, P
+    ka.a_v, ka.a_k, ka.b_v, ka.b_k = dims
+    ka.slow_decay = slow_decay
+    ka.sketch = sketch.data_ptr()
+    ka.A, ka.Bk, ka.U, ka.Vb = (state.A.data_ptr(), state.Bk.data_ptr(), state.U.data_ptr(),
+                                state.Vb.data_ptr())
+    ka.slot, ka.comp_err = state.slot.data_ptr(), state.err.data_ptr()
+    lib = L.load()
+    with torch.cuda.device(q.device):
+        L.check(lib.gdnx_kr_scan_fwd(C.byref(ka), C.c_void_p(_stream(q.device))), "gdnx_kr_scan_fwd")
+    return y
+
+
+def compact(A, Bk, U, Vb, sketch, *, dims=(16, 16, 8, 8), slow_decay: float = 0.97):
+    """One compaction per chain, in place on A and Bk; returns per-chain discarded energy [N]."""
+    _require_cuda(A, Bk, U, Vb, sketch)
+    N, R = A.shape[:2]
+    V, P = U.shape[1:]
+    K = Vb.shape[1]
+    for t in (A, Bk, U, Vb, sketch):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("compaction operands must be contiguous fp32")
+    err = torch.empty(N, dtype=torch.float32, device=A.device)
+    ca = L.CompactArgs()
+    ca.N, ca.R, ca.P, ca.V, ca.K = N, R, P, V, K
+    ca.a_v, ca.a_k, ca.b_v, ca.b_k = dims
+    ca.slow_decay = slow_decay
+    ca.sketch, ca.A, ca.Bk, ca.U, ca.Vb, ca.err = (sketch.data_ptr(), A.data_ptr(), Bk.data_ptr(),
+                                                  U.data_ptr(), Vb.data_ptr(), err.data_ptr())
+    lib = L.load()
+    with torch.cuda.device(A.device):
+        L.check(lib.gdnx_compact(C.byref(ca), C.c_void_p(_stream(A.device))), "gdnx_compact")
+    return err
+
+
+# ----------------------------------------------------------------------------
+# decode step
+# ----------------------------------------------------------------------------
+
+def decode_step(S, q, k, v, b_gate, w_gate, decay, *, mode: str = "gdn3", decay_kind: str = "gamma",
+                rope: Optional[LaneRope] = None, out_mix=None, out: Optional[torch.Tensor] = None,
+                out_dtype: Optional[torch.dtype] = None):
+    """One token for every chain, updating the dense state S [N, V, K] in place.
+
+    GDN3 (N = B*H*M): q, k [B,H,(M,)K]; v [B,H,(M,)V]; b_gate [B,H,M(,K)];
+    w_gate [B,H,M(,V)]; decay [B,H,M]; returns y [B,H,M,V].
+    KMD-2 (N = B*H): q [B,H,r,K]; k [B,H,K]; v [B,H,V]; beta_e/beta_w [B,H];
+    decay [B,H,K] (per channel) or [B,H]; returns y [B,H,V].
+    ``rope.pos0`` is the absolute position of the token.
+    """
+    _require_cuda(S, q, k, v, b_gate, w_gate, decay)
+    kmd2 = mode == "kmd2"
+    B, H = k.shape[:2]
+    K, V = k.shape[-1], v.shape[-1]
+    if kmd2:
+        M, r_out = 1, q.shape[2]
+        qv = q[:, None, :, None]                  # [B,1,H,1,r,K]
+        kx, vx = k[:, None, :, None], v[:, None, :, None]
+        bg, wg = b_gate[:, None, :, None, None], w_gate[:, None, :, None, None]
+        dec = decay[:, None, :, None] if decay.dim() == 3 else decay[:, None, :, None, None]
+    else:
+        M, r_out = b_gate.shape[2], 1
+        lane = lambda x: x if x.dim() == 4 else x.unsqueeze(2).expand(-1, -1, M, -1)
+        qv, kx, vx = lane(q)[:, None], lane(k)[:, None], lane(v)[:, None]
+        g1 = lambda x: (x.unsqueeze(-1) if x.dim() == 3 else x)[:, None]
+        bg, wg = g1(b_gate), g1(w_gate)
+        dec = decay[:, None, ..., None] if decay.dim() == 3 else decay[:, None]
+    N = B * H * M
+    if S.dtype != torch.float32 or not S.is_contiguous() or S.shape != (N, V, K):
+        raise ValueError("S must be contiguous fp32 [N, V, K]")
+    out_dtype = out_dtype or (torch.float32 if v.dtype == torch.float32 else v.dtype)
+    y = out if out is not None else torch.empty(B, H, M, V, dtype=out_dtype, device=S.device)
+    a = L.DecodeArgs()
+    a.B, a.H, a.M, a.K, a.V = B, H, M, K, V
+    a.mode = L.GDNX_MODE_KMD2 if kmd2 else L.GDNX_MODE_GDN3
+    a.r_out = r_out
+    a.q = _view(qv, True, slots=kmd2)
+    a.k, a.v = _view(kx, True), _view(vx, True)
+    a.gate_e, a.gate_w, a.decay = _view(bg, True), _view(wg, True), _view(dec, True)
+    a.decay_kind = _DECAY[decay_kind]
+    for i in range(4):
+        a.braid_rates[i] = BRAID_RATES[i]
+    a.braid_clamp = DECAY_CLAMP
+    a.rope = _rope_struct(rope)
+    mix = None
+    if r_out > 1:
+        mix = out_mix.detach().to(torch.float32).contiguous()
+        a.out_mix = mix.data_ptr()
+    a.S = S.data_ptr()
+    a.y, a.y_dtype = y.data_ptr(), _DT[y.dtype]
+    a.y_sb, a.y_sh, a.y_sm = y.stride()[:3]
+    lib = L.load()
+    with torch.cuda.device(S.device):
+        L.check(lib.gdnx_decode_step(C.byref(a), C.c_void_p(_stream(S.device))), "gdnx_decode_step")
+    return y[:, :, 0] if kmd2 else y

@@ -1,0 +1,217 @@
+/*
+ * gdnx.h -- C ABI of the B200 (sm_100a) GDN3 / KMD-2 recurrent-scan library.
+ *
+ * Every entry point takes a POD argument struct of device pointers, int64
+ * strides (in ELEMENTS) and scalars, enqueues work on the caller's stream and
+ * returns a gdnx_status.  The library never allocates or frees device memory
+ * on these paths: inputs, outputs, state and any workspace are caller-owned.
+ * There is no host synchronisation and no CPU fallback; host pointers are
+ * rejected with GDNX_EINVAL.
+ *
+ * Chains.  A chain is one independent recurrent state.  Chains are numbered
+ * n = (b*H + h)*M + m  (batch, head, lane -- lane fastest), exactly as the
+ * reference flattens them (gdn3/_reference_recurrence.py:47-50 and
+ * gdn3/gdn3_upgrade.py:427-431).  KMD-2 uses M = 1.
+ *
+ * State layouts (fp32, row-major, caller-owned):
+ *   dense  S  [N, V, K]            operator S with y = S q   (row v, key k)
+ *   GDN3-KR A [N, R, a_v, a_k], Bk [N, R, b_v, b_k], U [N, V, P], Vb [N, K, P]
+ *           -- the reference's own layouts (gdn3/_reference_recurrence.py:52-55).
+ *   The KMD-2 reference keeps S as [N, dk, dv] (research/kernel_ab/ref_scan.py:36);
+ *   this library's dense state is its transpose.
+ */
+#ifndef GDNX_H_
+#define GDNX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GDNX_API __attribute__((visibility("default")))
+#else
+#define GDNX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  GDNX_OK = 0,
+  GDNX_EINVAL = 1,       /* bad shape / stride / dtype / alignment / host pointer */
+  GDNX_ELAUNCH = 2,      /* CUDA launch or attribute error                         */
+  GDNX_ETIMEOUT = 3,     /* a bounded device-side wait ran out (error word set)   */
+  GDNX_EUNSUPPORTED = 4, /* valid request this build has no kernel for            */
+  GDNX_EWORKSPACE = 5    /* workspace missing or too small                        */
+} gdnx_status;
+
+typedef enum { GDNX_F32 = 0, GDNX_BF16 = 1, GDNX_F16 = 2 } gdnx_dtype;
+
+/* Recurrence family. */
+typedef enum {
+  /* GDN3: h = b (.) k, u = w (.) v, a = (1 - e^-(k.h)) / (k.h);
+   * S <- g S;  r = u - S h;  y = S q + a (k.q) r;  S <- S + a r k^T
+   * (gdn3/_reference_recurrence.py:60-84). */
+  GDNX_MODE_GDN3 = 0,
+  /* KMD-2: S <- diag-decay S; m = S k; d = beta_w v - beta_e m;  S <- S + d k^T;
+   * y = sum_slots mix * (q_slot . S)  (research/kernel_ab/ref_scan.py:40-47). */
+  GDNX_MODE_KMD2 = 1
+} gdnx_mode;
+
+/* How the decay view is interpreted. */
+typedef enum {
+  GDNX_DECAY_GAMMA = 0,   /* multiplicative factor, clamped to [0,1] as the reference does */
+  GDNX_DECAY_LOG = 1,     /* log of the factor (g <= 0); factor = exp(g)                   */
+  GDNX_DECAY_BRAIDED = 2  /* 4 logits x per chain-token:
+                             factor = min(mean_i exp(-min(softplus(x_i),5)*rate_i), clamp)
+                             (gdn3/gdn3_upgrade.py:812-822)                              */
+} gdnx_decay_kind;
+
+/* Kernel choice for gdnx_scan_fwd. */
+typedef enum {
+  GDNX_ALGO_AUTO = 0,      /* chunked tensor-core kernel when eligible, else recurrent */
+  GDNX_ALGO_RECURRENT = 1, /* exact token-recurrent CUDA-core kernel (fp32 math)       */
+  GDNX_ALGO_CHUNKED = 2    /* chunked WY/UT tcgen05 kernel (bf16 operands, fp32 acc)   */
+} gdnx_algo;
+
+/*
+ * A strided view of a logical [B, T, H, M, (S,) D] tensor whose last dim is
+ * contiguous.  Any of sb/st/sh/sm/ss may be 0 to broadcast (e.g. q/k/v shared
+ * by the M lanes of a head).  dim = size of the last dim (K, V, 1 for a
+ * scalar gate, 4 for braided logits).  ss is the stride of the query-slot
+ * dim (KMD-2 r_out slots), ignored elsewhere.  ptr == NULL means "absent".
+ */
+typedef struct {
+  const void* ptr;
+  int32_t dtype; /* gdnx_dtype */
+  int32_t dim;
+  int64_t sb, st, sh, sm, ss;
+} gdnx_view;
+
+/* Lane-specific partial RoPE on q and k (gdn3/gdn3_upgrade.py:342-401).
+ * For lane m (m < 4): pairs i < pairs[m] are (x[i], x[i+pairs[m]]); the angle is
+ * ((pos0 + t) * scale[m]) * inv_freq_i with inv_freq_i = 1 / 10000^(i / den[m]);
+ * x1' = x1 cos - x2 sin;  x2' = x1' sin + x2 cos  (the reference's in-place
+ * update, reproduced exactly).  pairs[m] = 0 disables lane m. */
+typedef struct {
+  int32_t enable;
+  int32_t pairs[4];
+  float scale[4];
+  float den[4];
+  int64_t pos0;
+} gdnx_rope;
+
+typedef struct {
+  int64_t B, T, H, M, K, V;
+  int32_t mode;     /* gdnx_mode            */
+  int32_t algo;     /* gdnx_algo            */
+  int32_t r_out;    /* query slots (KMD-2); 1 otherwise */
+  int32_t chunk;    /* chunk length for GDNX_ALGO_CHUNKED (64)  */
+
+  gdnx_view q;      /* [B,T,H,M,(r_out,)K]                                         */
+  gdnx_view k;      /* [B,T,H,M,K]                                                 */
+  gdnx_view v;      /* [B,T,H,M,V]                                                 */
+  gdnx_view gate_e; /* GDN3: erase gate b, dim K or 1.   KMD-2: beta_e, dim 1      */
+  gdnx_view gate_w; /* GDN3: write gate w, dim V or 1.   KMD-2: beta_w, dim 1      */
+  gdnx_view decay;  /* dim 1 (per chain-token), K (per key channel), or 4 (braided) */
+  int32_t decay_kind;         /* gdnx_decay_kind */
+  float braid_rates[4];       /* GDNX_DECAY_BRAIDED */
+  float braid_clamp;
+  gdnx_rope rope;
+
+  const float* out_mix;       /* [H, r_out] fp32 device, KMD-2 r_out > 1 */
+
+  void* y;                    /* output [B,T,H,M,V] with strides below   */
+  int32_t y_dtype;
+  int64_t y_sb, y_st, y_sh, y_sm;
+  float* scores;              /* optional [B,T,H,M] fp32 contiguous: |k| |update| */
+
+  const float* state_in;      /* optional dense S0 [N,V,K]; NULL = zero state      */
+  float* state_out;           /* optional final dense S [N,V,K] (may equal state_in) */
+
+  void* workspace;            /* see gdnx_scan_workspace_bytes */
+  size_t workspace_bytes;
+} gdnx_scan_args;
+
+/* Dense GDN3 / KMD-2 prefill scan.
+ * Replaces GDN3LinearAttn._gdn3_recurrent_state (gdn3/gdn3_upgrade.py:403-531)
+ * when compaction is off, kmd2_fast_scan.scan / scan_with_update_norm
+ * (gdn3/kmd2_fast_scan.py:163-282) and KMD2NativeAttn._scan
+ * (gdn3/kmd2_native.py:97-132). */
+GDNX_API gdnx_status gdnx_scan_fwd(const gdnx_scan_args* args, void* stream);
+
+/* Workspace the chosen kernel of gdnx_scan_fwd needs (0 if none). */
+GDNX_API size_t gdnx_scan_workspace_bytes(const gdnx_scan_args* args);
+
+/* Kronecker-residual (GDN3-KR) scan with periodic compaction. */
+typedef struct {
+  gdnx_scan_args base;        /* mode must be GDN3; state_in/state_out unused      */
+  int32_t R, P, a_v, a_k, b_v, b_k;
+  float slow_decay;           /* delta of the two-timescale blend (0.97)            */
+  const float* sketch;        /* G [N, b_v*b_k, q], q = min(R+4, a_v*a_k, b_v*b_k);
+                                 the reference draws it with torch's CPU generator,
+                                 seed 1234 (gdn3/gdn3_upgrade.py:679-682)           */
+  /* state, updated in place (zero it for a fresh sequence): */
+  float* A;                   /* [N,R,a_v,a_k] */
+  float* Bk;                  /* [N,R,b_v,b_k] */
+  float* U;                   /* [N,V,P]       */
+  float* Vb;                  /* [N,K,P]       */
+  int32_t* slot;              /* [N] slot pointer p (int32)                          */
+  float* comp_err;            /* optional [N] accumulated discarded energy           */
+} gdnx_kr_scan_args;
+
+/* Replaces GDN3LinearAttn._gdn3_recurrent_state with compaction
+ * (gdn3/gdn3_upgrade.py:403-531; semantics of gdn3/_reference_recurrence.py:33-94,
+ * including per-token decay of the Kronecker factors). */
+GDNX_API gdnx_status gdnx_kr_scan_fwd(const gdnx_kr_scan_args* args, void* stream);
+
+/* One rearrangement-SVD compaction per chain, in place on A and Bk.
+ * Replaces GDN3LinearAttn._compact_vec / _compact_fast (gdn3/gdn3_upgrade.py:565-719).
+ * Singular-vector signs are fixed so the largest-|.| entry of each B factor
+ * is positive (the reference inherits LAPACK's arbitrary sign). */
+typedef struct {
+  int64_t N;
+  int32_t R, P, V, K, a_v, a_k, b_v, b_k;
+  float slow_decay;
+  const float* sketch;        /* [N, b_v*b_k, q] */
+  float* A;                   /* [N,R,a_v,a_k] in/out */
+  float* Bk;                  /* [N,R,b_v,b_k] in/out */
+  const float* U;             /* [N,V,P] */
+  const float* Vb;            /* [N,K,P] */
+  float* err;                 /* optional [N]: discarded energy of this call (written) */
+} gdnx_compact_args;
+
+GDNX_API gdnx_status gdnx_compact(const gdnx_compact_args* args, void* stream);
+
+/* Single-token decode step from a supplied dense state, S updated in place.
+ * One iteration of the loop body of gdn3/_reference_recurrence.py:61-84
+ * (GDN3, A = 0) or research/kernel_ab/ref_scan.py:40-47 (KMD-2).  Views use
+ * T = 1 (st ignored); rope.pos0 is the token's absolute position. */
+typedef struct {
+  int64_t B, H, M, K, V;
+  int32_t mode;
+  int32_t r_out;
+  gdnx_view q, k, v, gate_e, gate_w, decay;
+  int32_t decay_kind;
+  float braid_rates[4];
+  float braid_clamp;
+  gdnx_rope rope;
+  const float* out_mix;
+  float* S;                   /* [N,V,K] fp32, in place */
+  void* y;                    /* [B,H,M,V] */
+  int32_t y_dtype;
+  int64_t y_sb, y_sh, y_sm;
+} gdnx_decode_args;
+
+GDNX_API gdnx_status gdnx_decode_step(const gdnx_decode_args* args, void* stream);
+
+GDNX_API const char* gdnx_status_string(gdnx_status s);
+
+/* Library build identification (for load checks). */
+GDNX_API const char* gdnx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDNX_H_ */
