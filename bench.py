@@ -329,7 +329,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, threads, sample, _ = cpu_sample_rate(target_s=10.0)
+        rate, threads, sample, _ = cpu_sample_rate(target_s=10.0, max_T=4096)
         cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
 
     if rank == 0:

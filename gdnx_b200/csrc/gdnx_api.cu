@@ -89,17 +89,12 @@ size_t gdnx_scan_workspace_bytes(const gdnx_scan_args* a) {
 
 gdnx_status gdnx_scan_fwd(const gdnx_scan_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
-  gdnx_status s = check_common(a->B, a->H, a->M, a->K, a->V, a->mode, a->r_out, a->q, a->k, a->v,
-                               a->gate_e, a->gate_w, a->decay, a->decay_kind, a->rope, a->out_mix);
-  if (s != GDNX_OK) return s;
-  if (a->T < 0) return GDNX_EINVAL;
-  if (!is_device_ptr(a->y) || !dtype_ok(a->y_dtype)) return GDNX_EINVAL;
-  if (a->scores && !is_device_ptr(a->scores)) return GDNX_EINVAL;
-  if (a->state_in && !is_device_ptr(a->state_in)) return GDNX_EINVAL;
-  if (a->state_out && !is_device_ptr(a->state_out)) return GDNX_EINVAL;
+  if (a->B < 0 || a->T < 0 || a->H <= 0 || a->M <= 0 || a->K <= 0 || a->V <= 0) return GDNX_EINVAL;
   if (a->B == 0 || a->T == 0) {
-    // nothing to scan: the final state equals the initial one
-    if (a->state_out && a->state_out != a->state_in) {
+    // nothing to scan (zero-size inputs carry no pointers): the final state
+    // equals the initial one
+    if (a->state_out && a->state_out != a->state_in && a->B > 0) {
+      if (!is_device_ptr(a->state_out) || (a->state_in && !is_device_ptr(a->state_in))) return GDNX_EINVAL;
       const size_t bytes = (size_t)(a->B * a->H * a->M * a->V * a->K) * sizeof(float);
       cudaError_t e = a->state_in
           ? cudaMemcpyAsync(a->state_out, a->state_in, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
@@ -108,6 +103,14 @@ gdnx_status gdnx_scan_fwd(const gdnx_scan_args* a, void* stream) {
     }
     return GDNX_OK;
   }
+  gdnx_status s = check_common(a->B, a->H, a->M, a->K, a->V, a->mode, a->r_out, a->q, a->k, a->v,
+                               a->gate_e, a->gate_w, a->decay, a->decay_kind, a->rope, a->out_mix);
+  if (s != GDNX_OK) return s;
+  if (a->T < 0) return GDNX_EINVAL;
+  if (!is_device_ptr(a->y) || !dtype_ok(a->y_dtype)) return GDNX_EINVAL;
+  if (a->scores && !is_device_ptr(a->scores)) return GDNX_EINVAL;
+  if (a->state_in && !is_device_ptr(a->state_in)) return GDNX_EINVAL;
+  if (a->state_out && !is_device_ptr(a->state_out)) return GDNX_EINVAL;
   cudaStream_t st = (cudaStream_t)stream;
   const bool chunk_ok = gdnx::chunked_eligible(*a);
   if (a->algo == GDNX_ALGO_CHUNKED && !chunk_ok) return GDNX_EUNSUPPORTED;
@@ -121,11 +124,11 @@ gdnx_status gdnx_scan_fwd(const gdnx_scan_args* a, void* stream) {
 
 gdnx_status gdnx_decode_step(const gdnx_decode_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
+  if (a->B == 0) return GDNX_OK;
   gdnx_status s = check_common(a->B, a->H, a->M, a->K, a->V, a->mode, a->r_out, a->q, a->k, a->v,
                                a->gate_e, a->gate_w, a->decay, a->decay_kind, a->rope, a->out_mix);
   if (s != GDNX_OK) return s;
   if (!is_device_ptr(a->S) || !is_device_ptr(a->y) || !dtype_ok(a->y_dtype)) return GDNX_EINVAL;
-  if (a->B == 0) return GDNX_OK;
   cudaStream_t st = (cudaStream_t)stream;
   if (a->K == 128 && a->V == 128) return gdnx::launch_decode_128(*a, st);
   // other head sizes: one step of the exact recurrent kernel, state in place
@@ -160,6 +163,7 @@ gdnx_status gdnx_kr_scan_fwd(const gdnx_kr_scan_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
   const gdnx_scan_args& b = a->base;
   if (b.mode != GDNX_MODE_GDN3) return GDNX_EINVAL;
+  if (b.B == 0 || b.T == 0) return GDNX_OK;
   gdnx_status s = check_common(b.B, b.H, b.M, b.K, b.V, b.mode, b.r_out, b.q, b.k, b.v,
                                b.gate_e, b.gate_w, b.decay, b.decay_kind, b.rope, b.out_mix);
   if (s != GDNX_OK) return s;
@@ -170,7 +174,6 @@ gdnx_status gdnx_kr_scan_fwd(const gdnx_kr_scan_args* a, void* stream) {
       !is_device_ptr(a->U) || !is_device_ptr(a->Vb) || !is_device_ptr(a->slot))
     return GDNX_EINVAL;
   if (a->comp_err && !is_device_ptr(a->comp_err)) return GDNX_EINVAL;
-  if (b.B == 0 || b.T == 0) return GDNX_OK;
   return gdnx::launch_kr_scan(*a, (cudaStream_t)stream);
 }
 
