@@ -257,3 +257,64 @@ def test_kr_scan_chunked_calls_equal_one_call():
     parts = [ops.gdn3_kr_scan(*gpu(*[t[:, a:b] for t in ins]), s2, G, P=P) for a, b in ((0, 23), (23, 80))]
     assert rel(torch.cat(parts, 1), y1) < 1e-5
     assert rel(s2.U, s1.U) < 1e-5 and rel(s2.A, s1.A) < 1e-4
+
+
+# ----------------------------------------------------------------- chunked tensor-core path --
+
+@pytest.mark.parametrize("T,rope_rf", [(64, None), (1, None), (100, 0.5), (256, 0.5), (130, 0.25)])
+def test_chunked_vs_oracle(T, rope_rf):
+    inp, rope, Yo, So = _dense_case(2, T, 2, 4, 128, seed=40 + T, dtype=torch.bfloat16, rope_rf=rope_rf)
+    q, k, v, beta, logg = gpu(inp["q"], inp["k"], inp["v"], inp["beta"], inp["logg"])
+    y, S = ops.gdn3_scan(q, k, v, beta, beta, logg, decay_kind="log", rope=rope, return_state=True,
+                         algo="chunked")
+    assert rel(y.float(), Yo) < TOL16 and rel(S, So) < TOL16
+
+
+def test_chunked_state_continuation_and_fp32_out():
+    inp, _, Yo, So = _dense_case(1, 192, 2, 4, 128, seed=50, dtype=torch.bfloat16)
+    q, k, v, beta, logg = gpu(inp["q"], inp["k"], inp["v"], inp["beta"], inp["logg"])
+    a = lambda x, s: x[:, s]
+    s1, s2 = slice(0, 70), slice(70, 192)
+    y1, S1 = ops.gdn3_scan(a(q, s1), a(k, s1), a(v, s1), a(beta, s1), a(beta, s1), a(logg, s1), decay_kind="log",
+                           return_state=True, algo="chunked", out_dtype=torch.float32)
+    y2, S2 = ops.gdn3_scan(a(q, s2), a(k, s2), a(v, s2), a(beta, s2), a(beta, s2), a(logg, s2), decay_kind="log",
+                           state=S1, return_state=True, algo="chunked", out_dtype=torch.float32)
+    assert y1.dtype == torch.float32
+    assert rel(torch.cat([y1, y2], 1), Yo) < TOL16 and rel(S2, So) < TOL16
+
+
+def test_chunked_realistic_decay():
+    inp = scan_inputs(1, 256, 2, 4, 128, 128, seed=51, dtype=torch.bfloat16)
+    inp["logg"] = realistic_logg(inp["logg"].shape, seed=52).to(torch.bfloat16)
+    Yo, So = R.dense_scan(*expand_lanes(inp, 4))
+    q, k, v, beta, logg = gpu(inp["q"], inp["k"], inp["v"], inp["beta"], inp["logg"])
+    y, S = ops.gdn3_scan(q, k, v, beta, beta, logg, decay_kind="log", return_state=True, algo="chunked")
+    assert rel(y.float(), Yo) < TOL16 and rel(S, So) < TOL16
+
+
+def test_chunked_agrees_with_recurrent_on_config1_slice():
+    """Both CUDA paths on the same bf16 inputs (B=8 slice of config 1, T=512)."""
+    inp = scan_inputs(8, 512, 16, 4, 128, 128, seed=1, dtype=torch.bfloat16)
+    q, k, v, beta, logg = gpu(inp["q"], inp["k"], inp["v"], inp["beta"], inp["logg"])
+    rope = lane_rope(4, 128, 128, 0.5)
+    yc, Sc = ops.gdn3_scan(q, k, v, beta, beta, logg, decay_kind="log", rope=rope, return_state=True,
+                           algo="chunked", out_dtype=torch.float32)
+    yr, Sr = ops.gdn3_scan(q, k, v, beta, beta, logg, decay_kind="log", rope=rope, return_state=True,
+                           algo="recurrent", out_dtype=torch.float32)
+    assert rel(yc, yr) < TOL16 and rel(Sc, Sr) < TOL16
+
+
+def test_chunked_kmd2_scalar_decay():
+    g = torch.Generator().manual_seed(53)
+    B, T, H, dk = 2, 150, 3, 128
+    q = (torch.nn.functional.normalize(torch.randn(B, T, H, 1, dk, generator=g), dim=-1) * dk ** -0.5)
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, dk, generator=g), dim=-1)
+    v = torch.randn(B, T, H, dk, generator=g)
+    gd = torch.exp(-torch.nn.functional.softplus(1.2 * torch.randn(B, T, H, generator=g) - 0.6))
+    be = torch.sigmoid(torch.randn(B, T, H, generator=g))
+    bw = torch.sigmoid(torch.randn(B, T, H, generator=g))
+    q, k, v = (x.to(torch.bfloat16).float() for x in (q, k, v))
+    y_ref, _, S_ref = R.kmd2_scan(q, k, v, gd[..., None].expand(-1, -1, -1, dk), be, bw)
+    bf = lambda x: x.to(torch.bfloat16).to(DEV)
+    y, S = ops.kmd2_scan(bf(q), bf(k), bf(v), gd.to(DEV), be.to(DEV), bw.to(DEV), return_state=True, algo="chunked")
+    assert rel(y, y_ref) < TOL16 and rel(S, S_ref.transpose(1, 2)) < TOL16
