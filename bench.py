@@ -200,6 +200,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--prefill-B", type=int, default=None, help="override B (profiling runs only)")
+    ap.add_argument("--prefill-T", type=int, default=None, help="override T (profiling runs only)")
+    ap.add_argument("--decode-layers", type=int, default=None, help="override layers (profiling runs only)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -222,7 +225,11 @@ def main():
     peaks = load_peaks()
 
     # ---------------- prefill (config 1 per rank) ----------------
-    c = CFG1
+    c = dict(CFG1)
+    if args.prefill_B:
+        c["B"] = args.prefill_B
+    if args.prefill_T:
+        c["T"] = args.prefill_T
     inp = make_prefill_inputs(c, dev, seed=1 + rank)
     rope = lane_rope(c["M"], c["K"], c["K"], 0.5)
     y = torch.empty(c["B"], c["T"], c["H"], c["M"], c["V"], dtype=torch.bfloat16, device=dev)
@@ -293,7 +300,9 @@ def main():
     # ---------------- decode (config 3) ----------------
     decode = None
     if not args.no_decode:
-        d = CFG3
+        d = dict(CFG3)
+        if args.decode_layers:
+            d["layers"] = args.decode_layers
         N = d["B"] * d["H"] * d["M"]
         g = torch.Generator(device=dev).manual_seed(3 + rank)
         states = [torch.randn(N, d["V"], d["K"], device=dev, generator=g) * 0.02 for _ in range(d["layers"])]
