@@ -122,6 +122,21 @@ gdnx_status gdnx_scan_fwd(const gdnx_scan_args* a, void* stream) {
   return gdnx::launch_recurrent_scan(*a, st);
 }
 
+gdnx_status gdnx_scan_fwd_noalloc(const gdnx_scan_args* a, void* stream) {
+  if (!a) return GDNX_EINVAL;
+  if (a->B < 0 || a->T < 0 || a->H <= 0 || a->M <= 0 || a->K <= 0 || a->V <= 0) return GDNX_EINVAL;
+  if (a->B == 0 || a->T == 0) return GDNX_EUNSUPPORTED;  // nothing for the kernel to do; use gdnx_scan_fwd
+  gdnx_status s = check_common(a->B, a->H, a->M, a->K, a->V, a->mode, a->r_out, a->q, a->k, a->v,
+                               a->gate_e, a->gate_w, a->decay, a->decay_kind, a->rope, a->out_mix);
+  if (s != GDNX_OK) return s;
+  if (!is_device_ptr(a->y) || !dtype_ok(a->y_dtype)) return GDNX_EINVAL;
+  if (a->scores) return GDNX_EUNSUPPORTED;
+  if (a->state_in && !is_device_ptr(a->state_in)) return GDNX_EINVAL;
+  if (a->state_out && !is_device_ptr(a->state_out)) return GDNX_EINVAL;
+  if (a->algo == GDNX_ALGO_RECURRENT) return GDNX_EUNSUPPORTED;
+  return gdnx::launch_chunked_scan_static_scratch(*a, (cudaStream_t)stream);
+}
+
 gdnx_status gdnx_decode_step(const gdnx_decode_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
   if (a->B == 0) return GDNX_OK;

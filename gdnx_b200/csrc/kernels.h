@@ -14,5 +14,7 @@ gdnx_status launch_kr_scan(const gdnx_kr_scan_args& a, cudaStream_t st);
 bool chunked_eligible(const gdnx_scan_args& a);
 size_t chunked_workspace_bytes(const gdnx_scan_args& a);
 gdnx_status launch_chunked_scan(const gdnx_scan_args& a, cudaStream_t st);
+// Same kernel with its scratch in a library-owned static device array (no allocation).
+gdnx_status launch_chunked_scan_static_scratch(const gdnx_scan_args& a, cudaStream_t st);
 
 }  // namespace gdnx

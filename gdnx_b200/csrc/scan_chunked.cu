@@ -25,6 +25,8 @@
 // fused into the chunk load.  Every mbarrier wait is bounded; on a timeout the
 // kernel records GDNX_ETIMEOUT in the workspace error word, frees its TMEM
 // and exits.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
@@ -511,6 +513,60 @@ gdnx_status launch_chunked_scan(const gdnx_scan_args& a, cudaStream_t st) {
   P.a = a;
   P.kmd2 = a.mode == GDNX_MODE_KMD2;
   P.err = reinterpret_cast<int*>(a.workspace);
+  if (cudaFuncSetAttribute(chunked_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+      cudaSuccess)
+    return GDNX_ELAUNCH;
+  const int64_t N = a.B * a.H * a.M;
+  chunked_scan_kernel<<<(unsigned)N, NT, SMEM_BYTES, st>>>(P);
+  return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the scratch (the kernel's device error word) sits in
+// a file-scope device array instead of a caller-provided workspace.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = 256;  // maximum scratch this variant offers
+static __device__ __align__(256) unsigned char g_chunked_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices] = {};  // device address of g_chunked_scratch, per device
+
+// Looks up the array's device address once per device, with that device current.
+gdnx_status static_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GDNX_ELAUNCH;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_chunked_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return GDNX_ELAUNCH;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return GDNX_OK;
+}
+
+}  // namespace
+
+gdnx_status launch_chunked_scan_static_scratch(const gdnx_scan_args& a, cudaStream_t st) {
+  if (!chunked_eligible(a)) return GDNX_EUNSUPPORTED;
+  if (chunked_workspace_bytes(a) > kStaticScratchBytes) return GDNX_EWORKSPACE;
+  void* scratch = nullptr;
+  const gdnx_status s = static_scratch(&scratch);
+  if (s != GDNX_OK) return s;
+  // the error word must start at zero on every call
+  if (cudaMemsetAsync(scratch, 0, kStaticScratchBytes, st) != cudaSuccess) return GDNX_ELAUNCH;
+  ChunkParams P;
+  P.a = a;
+  P.a.workspace = scratch;
+  P.a.workspace_bytes = kStaticScratchBytes;
+  P.kmd2 = a.mode == GDNX_MODE_KMD2;
+  P.err = reinterpret_cast<int*>(scratch);
   if (cudaFuncSetAttribute(chunked_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
       cudaSuccess)
     return GDNX_ELAUNCH;

@@ -344,3 +344,36 @@ def decode_step(S, q, k, v, b_gate, w_gate, decay, *, mode: str = "gdn3", decay_
     with torch.cuda.device(S.device):
         L.check(lib.gdnx_decode_step(C.byref(a), C.c_void_p(_stream(S.device))), "gdnx_decode_step")
     return y[:, :, 0] if kmd2 else y
+
+
+def gdn3_scan_noalloc(q, k, v, b_gate, w_gate, decay, *, decay_kind="gamma", rope: Optional[LaneRope] = None,
+                      state: Optional[torch.Tensor] = None, out: torch.Tensor,
+                      state_out: Optional[torch.Tensor] = None):
+    """Dense GDN3 scan through ``gdnx_scan_fwd_noalloc``: the library allocates
+    nothing and uses no caller workspace.  ``out`` ([B,T,H,M,V]) and the
+    optional ``state_out`` ([B*H*M, V, K] fp32) must be provided by the caller;
+    shapes otherwise as :func:`gdn3_scan` (chunked-kernel inputs only)."""
+    B, T, H = k.shape[:3]
+    M = b_gate.shape[3]
+    K, V = k.shape[-1], v.shape[-1]
+    _require_cuda(q, k, v, b_gate, w_gate, decay, state, out, state_out)
+    qx, kx, vx = _lanes_expand(q, M), _lanes_expand(k, M), _lanes_expand(v, M)
+    bg, wg = _gate(b_gate, K), _gate(w_gate, V)
+    dec = decay if decay_kind == "braided" else decay.unsqueeze(-1)
+    a = L.ScanArgs()
+    a.B, a.T, a.H, a.M, a.K, a.V = B, T, H, M, K, V
+    a.mode, a.algo, a.r_out, a.chunk = L.GDNX_MODE_GDN3, L.GDNX_ALGO_CHUNKED, 1, 64
+    a.q, a.k, a.v = _view(qx, True), _view(kx, True), _view(vx, True)
+    a.gate_e, a.gate_w, a.decay = _view(bg, True), _view(wg, True), _view(dec, True)
+    _fill_decay(a, dec, decay_kind, BRAID_RATES, DECAY_CLAMP)
+    a.rope = _rope_struct(rope)
+    a.y, a.y_dtype = out.data_ptr(), _DT[out.dtype]
+    a.y_sb, a.y_st, a.y_sh, a.y_sm = out.stride()[:4]
+    if state is not None:
+        a.state_in = state.data_ptr()
+    if state_out is not None:
+        a.state_out = state_out.data_ptr()
+    lib = L.load()
+    with torch.cuda.device(q.device):
+        L.check(lib.gdnx_scan_fwd_noalloc(C.byref(a), C.c_void_p(_stream(q.device))), "gdnx_scan_fwd_noalloc")
+    return out

@@ -143,6 +143,22 @@ GDNX_API gdnx_status gdnx_scan_fwd(const gdnx_scan_args* args, void* stream);
 /* Workspace the chosen kernel of gdnx_scan_fwd needs (0 if none). */
 GDNX_API size_t gdnx_scan_workspace_bytes(const gdnx_scan_args* args);
 
+/* Allocation-free chunked scan.  No counterpart in the reference.
+ * For callers that cannot allocate device memory at call time -- for example
+ * a host runtime that owns a fixed memory pool, or code running where a
+ * cudaMalloc would synchronise the device or fail.  Same arguments and
+ * results as gdnx_scan_fwd with algo = GDNX_ALGO_CHUNKED, but `workspace` /
+ * `workspace_bytes` are ignored: the kernel's scratch (its device error word)
+ * lives in a 256-byte array that the library keeps in every GPU that loads it
+ * until the process exits.  Requests the chunked kernel cannot take return
+ * GDNX_EUNSUPPORTED; a scratch need above the 256-byte maximum returns
+ * GDNX_EWORKSPACE.  The first call on a device looks the array's device
+ * address up (once per device); make that first call before any stream
+ * capture.  Every call shares the array and clears it on the stream before
+ * the kernel, so calls that overlap on the GPU (other streams, other host
+ * threads) race on it.  Nothing is allocated or freed. */
+GDNX_API gdnx_status gdnx_scan_fwd_noalloc(const gdnx_scan_args* args, void* stream);
+
 /* Kronecker-residual (GDN3-KR) scan with periodic compaction. */
 typedef struct {
   gdnx_scan_args base;        /* mode must be GDN3; state_in/state_out unused      */
