@@ -491,6 +491,7 @@ bool chunked_eligible(const gdnx_scan_args& a) {
   if (a.algo == GDNX_ALGO_RECURRENT) return false;
   if (a.K != KD || a.V != VD || (a.chunk != 0 && a.chunk != C)) return false;
   if (a.r_out != 1) return false;
+  if (a.scores) return false;  // update-norm scores are produced by the recurrent kernel only
   if (a.gate_e.dim != 1 || a.gate_w.dim != 1) return false;
   if (a.decay.dim != 1 && a.decay_kind != GDNX_DECAY_BRAIDED) return false;
   if (a.q.dtype != GDNX_BF16 || a.k.dtype != GDNX_BF16) return false;

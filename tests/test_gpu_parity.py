@@ -318,3 +318,20 @@ def test_chunked_kmd2_scalar_decay():
     bf = lambda x: x.to(torch.bfloat16).to(DEV)
     y, S = ops.kmd2_scan(bf(q), bf(k), bf(v), gd.to(DEV), be.to(DEV), bw.to(DEV), return_state=True, algo="chunked")
     assert rel(y, y_ref) < TOL16 and rel(S, S_ref.transpose(1, 2)) < TOL16
+
+
+def test_kmd2_scores_request_takes_a_path_that_writes_them():
+    """Scalar-decay KMD-2 with scores must not route to the chunked kernel (which has no scores)."""
+    g = torch.Generator().manual_seed(54)
+    B, T, H, dk = 1, 70, 2, 128
+    q = torch.randn(B, T, H, 1, dk, generator=g) * dk ** -0.5
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, dk, generator=g), dim=-1)
+    v = torch.randn(B, T, H, dk, generator=g)
+    gd = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, H, generator=g)))
+    be = torch.sigmoid(torch.randn(B, T, H, generator=g))
+    bw = torch.sigmoid(torch.randn(B, T, H, generator=g))
+    q, k, v = (x.to(torch.bfloat16).float() for x in (q, k, v))
+    _, sc_ref, _ = R.kmd2_scan(q, k, v, gd[..., None].expand(-1, -1, -1, dk), be, bw)
+    bf = lambda x: x.to(torch.bfloat16).to(DEV)
+    _, sc = ops.kmd2_scan(bf(q), bf(k), bf(v), gd.to(DEV), be.to(DEV), bw.to(DEV), scores=True)
+    assert rel(sc, sc_ref) < TOL16
