@@ -50,7 +50,10 @@ constexpr int OFF_MQ = OFF_T + 8192;        // [64 rows i][64 j] bf16
 constexpr int OFF_LM = OFF_MQ + 8192;       // fp32 [64][65]  A (strictly lower)
 constexpr int OFF_TM = OFF_LM + 64 * 65 * 4;  // fp32 [64][65]  T (+ upper-block scratch)
 constexpr int OFF_SC = OFF_TM + 64 * 65 * 4;  // fp32 scalars: L, eL, eLC, ce, cw, kn2, inv_freq (7 x 64)
-constexpr int OFF_BAR = OFF_SC + 7 * 64 * 4;
+constexpr int OFF_STQ = OFF_SC + 7 * 64 * 4;  // bf16 [64 tokens][128] raw q of the next chunk (cp.async)
+constexpr int OFF_STK = OFF_STQ + 16384;       // raw k
+constexpr int OFF_STV = OFF_STK + 16384;       // raw v
+constexpr int OFF_BAR = OFF_STV + 16384;
 constexpr int SMEM_BYTES = OFF_BAR + 64 + 1024;  // + alignment slack
 
 struct ChunkParams {
@@ -68,6 +71,23 @@ __device__ __forceinline__ void load8_bf16(const void* base, int64_t off, float*
     x[2 * i] = f.x;
     x[2 * i + 1] = f.y;
   }
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Raw bits of one element (converted later, so a prefetch does not stall on its load).
+__device__ __forceinline__ uint32_t ld_raw(const void* base, int dtype, int64_t off) {
+  if (dtype == GDNX_F32) return reinterpret_cast<const uint32_t*>(base)[off];
+  return reinterpret_cast<const uint16_t*>(base)[off];
+}
+__device__ __forceinline__ float raw_f32(uint32_t r, int dtype) {
+  if (dtype == GDNX_F32) return __uint_as_float(r);
+  if (dtype == GDNX_BF16) return __uint_as_float(r << 16);
+  return __half2float(__ushort_as_half((unsigned short)r));
 }
 
 __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P) {
@@ -88,6 +108,9 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
   float* sCW = sL + 256;
   float* sKN = sL + 320;
   float* sInv = sL + 384;
+  const char* cSTQ = reinterpret_cast<const char*>(sm + OFF_STQ);
+  const char* cSTK = reinterpret_cast<const char*>(sm + OFF_STK);
+  const __nv_bfloat16* hSTV = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_STV);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
   float* s_misc = reinterpret_cast<float*>(sm + OFF_BAR + 16);
@@ -139,40 +162,96 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
   uint32_t phase = 0;
   bool aborted = false;
   const int64_t nchunks = (a.T + C - 1) / C;
+  const bool braided = a.decay_kind == GDNX_DECAY_BRAIDED;
+  const bool y_tile = a.y_dtype == GDNX_BF16 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 &&
+                      a.y_sb % 8 == 0 && a.y_st % 8 == 0 && a.y_sh % 8 == 0 && a.y_sm % 8 == 0;
+  // next-chunk prefetch: q/k/v rows into the staging tiles with cp.async, and the
+  // per-token scalars (raw bits) into warp 0's registers
+  uint32_t pr_be[2], pr_bw[2], pr_dec[2][4];
+  // Fixed per-thread prefetch slots: thread tid moves 16-byte chunk cc = tid % 16 of
+  // token rows j0 + 16 r (r < 4) for each of q, k, v.
+  const int pf_cc = tid & 15, pf_j0 = tid >> 4;
+  const __nv_bfloat16* pf_src[3];
+  int64_t pf_st[3];
+  {
+    const gdnx_view* vw[3] = {&a.q, &a.k, &a.v};
+#pragma unroll
+    for (int w = 0; w < 3; ++w) {
+      pf_src[w] = reinterpret_cast<const __nv_bfloat16*>(vw[w]->ptr) + view_off(*vw[w], b, 0, h, m) + 8 * pf_cc;
+      pf_st[w] = vw[w]->st;
+    }
+  }
+  const uint32_t pf_dst = tc::smem_u32(sm + OFF_STQ) + pf_j0 * 256 + pf_cc * 16;
+  auto prefetch_rows = [&](int64_t chn, int w0, int w1) {
+    const int64_t tb = chn * C;
+    for (int w = w0; w < w1; ++w) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int64_t tt = tb + pf_j0 + 16 * r;
+        const bool valid = tt < a.T;
+        cp_async16(pf_dst + w * 16384 + r * 16 * 256, valid ? pf_src[w] + tt * pf_st[w] : pf_src[w], valid);
+      }
+    }
+    cp_async_commit();
+  };
+  const int64_t sc_e0 = view_off(a.gate_e, b, 0, h, m), sc_w0 = view_off(a.gate_w, b, 0, h, m);
+  const int64_t sc_d0 = view_off(a.decay, b, 0, h, m);
+  auto prefetch_scalars = [&](int64_t chn) {
+    if (warp != 0) return;
+    const int64_t tb = chn * C;
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2) {
+      const int64_t tt = tb + lane + 32 * s2;
+      pr_be[s2] = pr_bw[s2] = 0u;
+#pragma unroll
+      for (int z = 0; z < 4; ++z) pr_dec[s2][z] = 0u;
+      if (tt < a.T) {
+        pr_be[s2] = ld_raw(a.gate_e.ptr, a.gate_e.dtype, sc_e0 + tt * a.gate_e.st);
+        pr_bw[s2] = ld_raw(a.gate_w.ptr, a.gate_w.dtype, sc_w0 + tt * a.gate_w.st);
+#pragma unroll
+        for (int z = 0; z < 4; ++z)
+          if (z == 0 || braided) pr_dec[s2][z] = ld_raw(a.decay.ptr, a.decay.dtype, sc_d0 + tt * a.decay.st + z);
+      }
+    }
+  };
+  prefetch_rows(0, 0, 3);
+  prefetch_scalars(0);
   for (int64_t ch = 0; ch < nchunks && !aborted; ++ch) {
     const int64_t t0 = ch * C;
     const int nt = (int)((a.T - t0) < C ? (a.T - t0) : C);
 
     // ================= Phase A: fused prologue =================
+    cp_async_wait_all();
+    __syncthreads();
+    // RoPE angle table for the chunk (spread evenly over all threads), parked in Tm
+    float* tabC = Tm;
+    float* tabS = Tm + C * 32;
+    if (dpairs > 0) {
+      const float sc = a.rope.scale[lm];
+      for (int idx = tid; idx < C * dpairs; idx += NT) {
+        const int j = idx / dpairs, i = idx - j * dpairs;
+        float sn, cs;
+        sincosf((float)(a.rope.pos0 + t0 + j) * sc * sInv[i], &sn, &cs);
+        tabC[j * 32 + i] = cs;
+        tabS[j * 32 + i] = sn;
+      }
+      __syncthreads();
+    }
     for (int it = tid; it < C * 16; it += NT) {
       const int j = it >> 4, cc = it & 15;
       const bool partner_only = dch > 0 && cc >= dch && cc < 2 * dch;
       float kx[8], qx[8], k2[8], q2[8];
       float nrm = 0.f;
       if (!partner_only) {
-        const bool valid = j < nt;
-        const int64_t tt = t0 + j;
-        if (valid) {
-          load8_bf16(a.k.ptr, view_off(a.k, b, tt, h, m) + 8 * cc, kx);
-          load8_bf16(a.q.ptr, view_off(a.q, b, tt, h, m) + 8 * cc, qx);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) kx[e] = qx[e] = 0.f;
-        }
+        load8_bf16(cSTK, j * 128 + 8 * cc, kx);
+        load8_bf16(cSTQ, j * 128 + 8 * cc, qx);
         if (cc < dch) {
           const int c2 = cc + dch;
-          if (valid) {
-            load8_bf16(a.k.ptr, view_off(a.k, b, tt, h, m) + 8 * c2, k2);
-            load8_bf16(a.q.ptr, view_off(a.q, b, tt, h, m) + 8 * c2, q2);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) k2[e] = q2[e] = 0.f;
-          }
-          const float pos = (float)(a.rope.pos0 + tt) * a.rope.scale[lm];
+          load8_bf16(cSTK, j * 128 + 8 * c2, k2);
+          load8_bf16(cSTQ, j * 128 + 8 * c2, q2);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            float s, c;
-            sincosf(pos * sInv[8 * cc + e], &s, &c);
+            const float s = tabS[j * 32 + 8 * cc + e], c = tabC[j * 32 + 8 * cc + e];
             const float k1n = kx[e] * c - k2[e] * s;
             k2[e] = k1n * s + k2[e] * c;
             kx[e] = k1n;
@@ -205,19 +284,24 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
         const int j = lane + 32 * s;
         lg[s] = 0.f; ce[s] = 0.f; cw[s] = 0.f;
         if (j < nt) {
-          const int64_t tt = t0 + j;
-          const int64_t dof = view_off(a.decay, b, tt, h, m);
           float l;
           if (a.decay_kind == GDNX_DECAY_LOG) {
-            l = ld_as_f32(a.decay.ptr, a.decay.dtype, dof);
+            l = raw_f32(pr_dec[s][0], a.decay.dtype);
             if (!P.kmd2) l = fminf(l, 0.f);
+          } else if (braided) {
+            float acc = 0.f;
+#pragma unroll
+            for (int z = 0; z < 4; ++z)
+              acc += expf(-fminf(softplus_f(raw_f32(pr_dec[s][z], a.decay.dtype)), 5.0f) * a.braid_rates[z]);
+            l = logf(fmaxf(fminf(acc * 0.25f, a.braid_clamp), 1e-30f));
           } else {
-            const float g = decay_factor(a.decay, a.decay_kind, dof, !P.kmd2, a.braid_rates, a.braid_clamp);
+            float g = raw_f32(pr_dec[s][0], a.decay.dtype);
+            if (!P.kmd2) g = fminf(fmaxf(g, 0.f), 1.f);
             l = logf(fmaxf(g, 1e-30f));
           }
-          lg[s] = fmaxf(l, -80.f);
-          const float be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tt, h, m));
-          const float bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tt, h, m));
+          lg[s] = fmaxf(l, -80.f) * 1.4426950408889634f;  // log2 units from here on
+          const float be = raw_f32(pr_be[s], a.gate_e.dtype);
+          const float bw = raw_f32(pr_bw[s], a.gate_w.dtype);
           if (P.kmd2) {
             ce[s] = be; cw[s] = bw;
           } else {
@@ -237,11 +321,11 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
       s1 += __shfl_sync(0xffffffffu, s0, 31);
       const float Lc = __shfl_sync(0xffffffffu, s1, 31);
       sL[lane] = s0; sL[lane + 32] = s1;
-      sE[lane] = expf(s0); sE[lane + 32] = expf(s1);
-      sEC[lane] = expf(Lc - s0); sEC[lane + 32] = expf(Lc - s1);
+      sE[lane] = exp2f(s0); sE[lane + 32] = exp2f(s1);
+      sEC[lane] = exp2f(Lc - s0); sEC[lane + 32] = exp2f(Lc - s1);
       sCE[lane] = ce[0]; sCE[lane + 32] = ce[1];
       sCW[lane] = cw[0]; sCW[lane + 32] = cw[1];
-      if (lane == 0) s_misc[0] = expf(Lc);
+      if (lane == 0) s_misc[0] = exp2f(Lc);
     }
     __syncthreads();
     // S (fp32, TMEM) -> bf16 operand tile S0; TMEM S <- e^{L_C} S
@@ -275,16 +359,6 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
       }
       tc::commit(mbar);
     }
-    // prefetch the values this thread needs for RHS while the MMAs run
-    float vv[32];
-    {
-      const int64_t vo = view_off(a.v, b, 0, h, m) + row;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int j = 32 * hf + e;
-        vv[e] = j < nt ? ld_as_f32(a.v.ptr, a.v.dtype, vo + (t0 + j) * a.v.st) : 0.f;
-      }
-    }
     {
       const bool ok = tc::mbar_wait(mbar, phase & 1);
       ++phase;
@@ -302,7 +376,7 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int l = 32 * hf + e;
-          Lm[j * 65 + l] = (l < j) ? cej * expf(Lj - sL[l]) * d[e] : 0.f;
+          Lm[j * 65 + l] = (l < j) ? cej * exp2f(Lj - sL[l]) * d[e] : 0.f;
         }
       } else {
         const int i = row - 64;
@@ -310,7 +384,7 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int jj = 32 * hf + e;
-          d[e] = (jj <= i) ? expf(Li - sL[jj]) * d[e] : 0.f;
+          d[e] = (jj <= i) ? exp2f(Li - sL[jj]) * d[e] : 0.f;
         }
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(cMQ, tc::sw128(i, 4 * hf + q4, 64), d + 8 * q4);
@@ -319,7 +393,7 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const int j = 32 * hf + e;
-        d[e] = sCW[j] * vv[e] - sCE[j] * sE[j] * d[e];
+        d[e] = sCW[j] * __bfloat162float(hSTV[j * VD + row]) - sCE[j] * sE[j] * d[e];
       }
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(cRHS, tc::sw128(row, 4 * hf + q4, 128), d + 8 * q4);
@@ -341,6 +415,10 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
       }
     }
     __syncthreads();
+    if (ch + 1 < nchunks) {  // this chunk's staged rows and scalars are consumed: fetch the next
+      prefetch_rows(ch + 1, 0, 3);
+      prefetch_scalars(ch + 1);
+    }
     // diagonal 16x16 blocks: warp w < 4 inverts block w, lane c < 16 builds column c
     if (warp < 4 && lane < 16) {
       const int o = 16 * warp, c = lane;
@@ -356,26 +434,36 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
       for (int i = 0; i < 16; ++i) Tm[(o + i) * 65 + o + c] = x[i];
     }
     __syncthreads();
-    // off-diagonal blocks by distance d:  T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj.
-    // The partial sum X_ij is parked in the (unused) upper block (j, i) of Tm.
-    for (int dd = 1; dd < 4; ++dd) {
-      const int nblk = 4 - dd;
-      for (int o = tid; o < nblk * 256; o += NT) {
-        const int bj = o >> 8, bi = bj + dd, rr = (o >> 4) & 15, cc = o & 15;
-        float s = 0.f;
-        for (int bk = bj; bk < bi; ++bk) {
+    // Off-diagonal blocks.  With P_ij = T_ii A_ij (i > j, all six formed in one step and
+    // parked in the unused upper block (j, i)):  T_ij = -sum_{k=j}^{i-1} P_ik T_kj,
+    // evaluated by block distance 1, 2, 3.
+    for (int o = tid; o < 6 * 256; o += NT) {
+      const int pb = o >> 8, rr = (o >> 4) & 15, cc = o & 15;
+      const int bi = pb < 3 ? pb + 1 : (pb < 5 ? pb - 1 : 3);   // (1,0) (2,1) (3,2) (2,0) (3,1) (3,0)
+      const int bj = pb < 3 ? pb : (pb < 5 ? pb - 3 : 0);
+      float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-          for (int t = 0; t < 16; ++t) s += Lm[(16 * bi + rr) * 65 + 16 * bk + t] * Tm[(16 * bk + t) * 65 + 16 * bj + cc];
-        }
-        Tm[(16 * bj + rr) * 65 + 16 * bi + cc] = s;
+      for (int t = 0; t < 16; t += 2) {
+        s0 = fmaf(Tm[(16 * bi + rr) * 65 + 16 * bi + t], Lm[(16 * bi + t) * 65 + 16 * bj + cc], s0);
+        s1 = fmaf(Tm[(16 * bi + rr) * 65 + 16 * bi + t + 1], Lm[(16 * bi + t + 1) * 65 + 16 * bj + cc], s1);
       }
-      __syncthreads();
-      for (int o = tid; o < nblk * 256; o += NT) {
+      Tm[(16 * bj + rr) * 65 + 16 * bi + cc] = s0 + s1;
+    }
+    __syncthreads();
+    for (int dd = 1; dd < 4; ++dd) {
+      for (int o = tid; o < (4 - dd) * 256; o += NT) {
         const int bj = o >> 8, bi = bj + dd, rr = (o >> 4) & 15, cc = o & 15;
-        float s = 0.f;
+        float s0 = 0.f, s1 = 0.f;
+        for (int bk = bj; bk < bi; ++bk) {
+          const float* pr = Tm + (16 * bk + rr) * 65 + 16 * bi;   // P_{i,k}[rr][:]
+          const float* tc_ = Tm + (16 * bk) * 65 + 16 * bj + cc;  // T_{k,j}[:][cc]
 #pragma unroll
-        for (int t = 0; t < 16; ++t) s += Tm[(16 * bi + rr) * 65 + 16 * bi + t] * Tm[(16 * bj + t) * 65 + 16 * bi + cc];
-        Tm[(16 * bi + rr) * 65 + 16 * bj + cc] = -s;
+          for (int t = 0; t < 16; t += 2) {
+            s0 = fmaf(pr[t], tc_[t * 65], s0);
+            s1 = fmaf(pr[t + 1], tc_[(t + 1) * 65], s1);
+          }
+        }
+        Tm[(16 * bi + rr) * 65 + 16 * bj + cc] = -(s0 + s1);
       }
       __syncthreads();
     }
@@ -454,11 +542,27 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
     {
       float yv[32];
       tc::tmem_ld32(tD1 + lbase + 32 * hf, yv);
-      const int64_t yo = b * a.y_sb + h * a.y_sh + m * a.y_sm + row;
+      if (y_tile) {
+        // stage the chunk's outputs as bf16 [token][v] (in the A-matrix scratch), then
+        // write each token's 256-byte row with 16-byte stores
+        __nv_bfloat16* ys = reinterpret_cast<__nv_bfloat16*>(Lm);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int i = 32 * hf + e;
-        if (i < nt) st_from_f32(a.y, a.y_dtype, yo + (t0 + i) * a.y_st, yv[e]);
+        for (int e = 0; e < 32; ++e) ys[(32 * hf + e) * VD + row] = __float2bfloat16_rn(yv[e]);
+        __syncthreads();
+        const int64_t ybase = b * a.y_sb + h * a.y_sh + m * a.y_sm;
+        for (int it = tid; it < C * 16; it += NT) {
+          const int i = it >> 4, cc = it & 15;
+          if (i < nt)
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + ybase + (t0 + i) * a.y_st + 8 * cc) =
+                *reinterpret_cast<const uint4*>(ys + i * VD + 8 * cc);
+        }
+      } else {
+        const int64_t yo = b * a.y_sb + h * a.y_sh + m * a.y_sm + row;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int i = 32 * hf + e;
+          if (i < nt) st_from_f32(a.y, a.y_dtype, yo + (t0 + i) * a.y_st, yv[e]);
+        }
       }
     }
     tc::fence_before();
@@ -495,9 +599,11 @@ bool chunked_eligible(const gdnx_scan_args& a) {
   if (a.gate_e.dim != 1 || a.gate_w.dim != 1) return false;
   if (a.decay.dim != 1 && a.decay_kind != GDNX_DECAY_BRAIDED) return false;
   if (a.q.dtype != GDNX_BF16 || a.k.dtype != GDNX_BF16) return false;
-  if (!aligned16(a.q.ptr) || !aligned16(a.k.ptr)) return false;
-  const int64_t st[8] = {a.q.sb, a.q.st, a.q.sh, a.q.sm, a.k.sb, a.k.st, a.k.sh, a.k.sm};
-  for (int i = 0; i < 8; ++i)
+  if (a.v.dtype != GDNX_BF16) return false;
+  if (!aligned16(a.q.ptr) || !aligned16(a.k.ptr) || !aligned16(a.v.ptr)) return false;
+  const int64_t st[12] = {a.q.sb, a.q.st, a.q.sh, a.q.sm, a.k.sb, a.k.st, a.k.sh, a.k.sm,
+                          a.v.sb, a.v.st, a.v.sh, a.v.sm};
+  for (int i = 0; i < 12; ++i)
     if (st[i] % 8) return false;
   if (a.rope.enable)
     for (int i = 0; i < 4; ++i)
