@@ -145,7 +145,8 @@ gdnx_status gdnx_decode_step(const gdnx_decode_args* a, void* stream) {
   if (s != GDNX_OK) return s;
   if (!is_device_ptr(a->S) || !is_device_ptr(a->y) || !dtype_ok(a->y_dtype)) return GDNX_EINVAL;
   cudaStream_t st = (cudaStream_t)stream;
-  if (a->K == 128 && a->V == 128) return gdnx::launch_decode_128(*a, st);
+  if (a->K == 128 && a->V == 128 && a->r_out == 1 && (reinterpret_cast<uintptr_t>(a->S) & 15) == 0)
+    return gdnx::launch_decode_128(*a, st);
   // other head sizes: one step of the exact recurrent kernel, state in place
   gdnx_scan_args sa = {};
   sa.B = a->B; sa.T = 1; sa.H = a->H; sa.M = a->M; sa.K = a->K; sa.V = a->V;

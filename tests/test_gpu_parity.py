@@ -335,3 +335,47 @@ def test_kmd2_scores_request_takes_a_path_that_writes_them():
     bf = lambda x: x.to(torch.bfloat16).to(DEV)
     _, sc = ops.kmd2_scan(bf(q), bf(k), bf(v), gd.to(DEV), be.to(DEV), bw.to(DEV), scores=True)
     assert rel(sc, sc_ref) < TOL16
+
+
+def test_decode_step_many_chains_per_cta():
+    """More chains than SMs: every persistent CTA cycles its three state stages."""
+    g = torch.Generator().manual_seed(33)
+    B, H, M, K = 64, 4, 4, 128
+    N = B * H * M
+    S0 = torch.randn(N, K, K, generator=g) * 0.02
+    inp = scan_inputs(B, 1, H, M, K, K, seed=34, dtype=torch.bfloat16)
+    q, k, v = (inp[n][:, 0].float() for n in ("q", "k", "v"))
+    beta, logg = inp["beta"][:, 0].float(), inp["logg"][:, 0].float()
+    ex = lambda x: x.unsqueeze(2).expand(-1, -1, M, -1).reshape(N, -1)
+    yo, So = R.dense_decode_step(S0, ex(q), ex(k), ex(v), beta.reshape(N, 1), beta.reshape(N, 1),
+                                 torch.exp(logg).reshape(N))
+    S = S0.to(DEV).contiguous()
+    y = ops.decode_step(S, *(inp[n][:, 0].to(DEV) for n in ("q", "k", "v")), inp["beta"][:, 0].to(DEV),
+                        inp["beta"][:, 0].to(DEV), inp["logg"][:, 0].to(DEV), decay_kind="log")
+    y2 = ops.decode_step(S, *(inp[n][:, 0].to(DEV) for n in ("q", "k", "v")), inp["beta"][:, 0].to(DEV),
+                         inp["beta"][:, 0].to(DEV), inp["logg"][:, 0].to(DEV), decay_kind="log")
+    yo2, So2 = R.dense_decode_step(So, ex(q), ex(k), ex(v), beta.reshape(N, 1), beta.reshape(N, 1),
+                                   torch.exp(logg).reshape(N))
+    assert rel(y.float().reshape(N, K), yo) < TOL16 and rel(y2.float().reshape(N, K), yo2) < TOL16
+    assert rel(S, So2) < TOL32
+
+
+@pytest.mark.parametrize("pos0", [0, 4096])
+def test_decode_step_with_lane_rope(pos0):
+    g = torch.Generator().manual_seed(35)
+    B, H, M, K = 8, 4, 4, 128
+    N = B * H * M
+    S0 = torch.randn(N, K, K, generator=g) * 0.02
+    inp = scan_inputs(B, 1, H, M, K, K, seed=36, dtype=torch.bfloat16)
+    rf = 0.5
+    qx = PR.apply_lane_rope(inp["q"].float().unsqueeze(3).expand(-1, -1, -1, M, -1).contiguous(), K, rf, pos0=pos0)
+    kx = PR.apply_lane_rope(inp["k"].float().unsqueeze(3).expand(-1, -1, -1, M, -1).contiguous(), K, rf, pos0=pos0)
+    v = inp["v"][:, 0].float().unsqueeze(2).expand(-1, -1, M, -1).reshape(N, K)
+    beta, logg = inp["beta"][:, 0].float(), inp["logg"][:, 0].float()
+    yo, So = R.dense_decode_step(S0, qx[:, 0].reshape(N, K), kx[:, 0].reshape(N, K), v, beta.reshape(N, 1),
+                                 beta.reshape(N, 1), torch.exp(logg).reshape(N))
+    S = S0.to(DEV).contiguous()
+    rope = lane_rope(M, K, K, rf, pos0=pos0)
+    y = ops.decode_step(S, *(inp[n][:, 0].to(DEV) for n in ("q", "k", "v")), inp["beta"][:, 0].to(DEV),
+                        inp["beta"][:, 0].to(DEV), inp["logg"][:, 0].to(DEV), decay_kind="log", rope=rope)
+    assert rel(y.float().reshape(N, K), yo) < TOL16 and rel(S, So) < TOL32
