@@ -289,7 +289,7 @@ def main():
     # ---------------- all-gather of per-head outputs (multi-GPU only) ----------------
     gather = None
     if dist:
-        full = torch.empty((world,) + tuple(y.shape), dtype=y.dtype, device=dev)
+        full = torch.empty((world * y.shape[0],) + tuple(y.shape[1:]), dtype=y.dtype, device=dev)
         ms_g = timed(lambda: dist.all_gather_into_tensor(full, y), 3, 1, stream, barrier)
         t = torch.tensor([ms_g], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

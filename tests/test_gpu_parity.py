@@ -379,3 +379,33 @@ def test_decode_step_with_lane_rope(pos0):
     y = ops.decode_step(S, *(inp[n][:, 0].to(DEV) for n in ("q", "k", "v")), inp["beta"][:, 0].to(DEV),
                         inp["beta"][:, 0].to(DEV), inp["logg"][:, 0].to(DEV), decay_kind="log", rope=rope)
     assert rel(y.float().reshape(N, K), yo) < TOL16 and rel(S, So) < TOL32
+
+
+# ----------------------------------------------------------------- drop-in modules --
+
+@pytest.mark.parametrize("case,P", [("parity_B1_T64", 16), ("parity_B2_T48", 16), ("cfg0dist_P80", 80),
+                                     ("cfg0dist_P80", 128)])
+def test_gdn3_dropin_matches_reference_outputs(case, P):
+    import types
+    from gdnx_b200.gdn3_upgrade import patch_layer
+    c = torch.load(GOLD / "gdn3_frozen.pt", weights_only=False)[case]
+    ins = ([t.contiguous() for t in expand_lanes(c["inputs_compact"], 4)] if "inputs_compact" in c
+           else parity_inputs(*c["shape"], c["seed"]))
+    a_v, a_k, b_v, b_k = c["dims"]
+    layer = types.SimpleNamespace(R=4, P=P, a_v=a_v, a_k=a_k, b_v=b_v, b_k=b_k, slow_decay=0.97, compact_mode="svd")
+    patch_layer(layer)
+    y = layer._gdn3_recurrent_state(*gpu(*ins))
+    assert y.dtype == torch.float32 and y.shape == c["Y"].shape
+    assert rel(y, c["Y"]) < TOL32   # P >= T: no compaction reaches the outputs
+
+
+@pytest.mark.parametrize("case", ["r1", "r4"])
+def test_kmd2_fast_scan_dropin(case):
+    from gdnx_b200 import kmd2_fast_scan
+    c = torch.load(GOLD / "kmd2.pt", weights_only=False)[case]
+    q, k, v, g, be, bw, mix = c["inputs"]
+    args = gpu(q, k, v, g, be, bw)
+    mixg = mix.to(DEV) if mix is not None else None
+    y = kmd2_fast_scan.scan(*args, mixg)
+    y2, sc = kmd2_fast_scan.scan_with_update_norm(*args, mixg)
+    assert rel(y, c["y"]) < TOL32 and rel(y2, c["y"]) < TOL32 and rel(sc, c["scores"]) < TOL32
