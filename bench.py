@@ -200,6 +200,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-kr", action="store_true")
+    ap.add_argument("--kr-T", type=int, default=65536)
     ap.add_argument("--prefill-B", type=int, default=None, help="override B (profiling runs only)")
     ap.add_argument("--prefill-T", type=int, default=None, help="override T (profiling runs only)")
     ap.add_argument("--decode-layers", type=int, default=None, help="override layers (profiling runs only)")
@@ -336,6 +338,29 @@ def main():
                   "peak_gbs": peaks["hbm"], "launches_per_step": d["layers"]}
         del states
 
+    # ---------------- Kronecker-residual scan (config 2, per rank) ----------------
+    kr = None
+    if not args.no_kr:
+        kc = dict(B=1, T=args.kr_T, H=16, M=4, K=128, V=128)
+        kin = make_prefill_inputs(kc, dev, seed=2 + rank)
+        N = kc["B"] * kc["H"] * kc["M"]
+        from gdnx_b200.gdn3_upgrade import reference_sketch
+        krs = {}
+        for P in (256, 16):
+            G = reference_sketch(N, 64, 8, dev)
+            st = ops.KRState.zeros(N, 4, P, (16, 16, 8, 8), 128, 128, dev)
+            yk = torch.empty(kc["B"], kc["T"], kc["H"], kc["M"], kc["V"], dtype=torch.bfloat16, device=dev)
+
+            def kstep():
+                st.slot.zero_()
+                ops.gdn3_kr_scan(kin["q"], kin["k"], kin["v"], kin["beta"], kin["beta"], kin["logg"], st, G, P=P,
+                                 decay_kind="log", rope=rope)
+
+            kms = timed(kstep, 2, 3, stream, barrier)
+            krs[f"P{P}"] = {"ms_per_call": kms, "tok_per_s": kc["B"] * kc["T"] * world / (kms * 1e-3)}
+        kr = {"metric": "KR prefill tok/s (config 2)", "B": 1, "T": kc["T"], "H": 16, "M": 4,
+              "state": "A 16x16 (x) B 8x8, R=4, + U,V 128xP, delta=0.97", **krs}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, threads, sample, _ = cpu_sample_rate(target_s=10.0, max_T=4096)
@@ -351,7 +376,7 @@ def main():
                            "l2": "inputs 402 MB + outputs 537 MB > 126 MB L2 (no flush)",
                            "parallelism": f"(batch x head) shards, dp{world}"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
-                "clocks": clocks, "decode": decode, "gather": gather}
+                "clocks": clocks, "decode": decode, "gather": gather, "kr": kr}
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()

@@ -88,4 +88,17 @@ GDNX_DEV void rope_row_warp(float* row, const gdnx_rope& rp, int lane_m, int64_t
   }
 }
 
+// Lane RoPE from a precomputed cos/sin row: x1' = x1 c - x2 s; x2' = x1' s + x2 c
+// (the reference's in-place update), same fp32 values as rope_row_warp when the
+// table holds sincosf(((float)pos * scale) * inv_freq_i).
+GDNX_DEV void rope_row_table(float* row, int d, const float* cs, const float* sn, int lane) {
+  for (int i = lane; i < d; i += 32) {
+    const float c = cs[i], s = sn[i];
+    const float x1 = row[i], x2 = row[i + d];
+    const float n1 = x1 * c - x2 * s;
+    row[i] = n1;
+    row[i + d] = n1 * s + x2 * c;
+  }
+}
+
 }  // namespace gdnx

@@ -10,13 +10,15 @@ constexpr int kPT = kCompPT;
 
 struct CompParams {
   gdnx_compact_args a;
-  CompactDims d;
+  float delta;
 };
 
+template <class CD>
 __global__ void __launch_bounds__(kThreads) compact_kernel(const CompParams P) {
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
-  const CompactDims d = P.d;
+  CD d;
+  d.delta = P.delta;
   const gdnx_compact_args& a = P.a;
   const int64_t n = blockIdx.x;
   const int ld = compact_ld(d.n);
@@ -42,24 +44,27 @@ __global__ void __launch_bounds__(kThreads) compact_kernel(const CompParams P) {
   if (a.err && threadIdx.x == 0) a.err[n] = err;
 }
 
-}  // namespace
-
-gdnx_status launch_compact(const gdnx_compact_args& a, cudaStream_t st) {
+template <class CD>
+gdnx_status launch_compact_t(const gdnx_compact_args& a, cudaStream_t st) {
   CompParams P;
   P.a = a;
-  CompactDims& d = P.d;
-  d.R = a.R; d.a_v = a.a_v; d.a_k = a.a_k; d.b_v = a.b_v; d.b_k = a.b_k;
-  d.m = a.a_v * a.a_k; d.n = a.b_v * a.b_k;
-  d.q = min(a.R + 4, min(d.m, d.n));
-  d.delta = a.slow_decay;
-  if (d.m > kCompMaxM || d.n > kCompMaxN || d.q > kCompMaxQ || d.R > d.q) return GDNX_EUNSUPPORTED;
+  P.delta = a.slow_decay;
+  const CD d{};
   if (a.V > 128 || a.K > 128 || a.V * a.K > 64 * kThreads) return GDNX_EUNSUPPORTED;
   const size_t smem = sizeof(float) * (size_t)(d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) +
                                                (a.V + a.K) * kPT);
-  if (cudaFuncSetAttribute(compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  if (cudaFuncSetAttribute(compact_kernel<CD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GDNX_ELAUNCH;
-  compact_kernel<<<(unsigned)a.N, kThreads, smem, st>>>(P);
+  compact_kernel<CD><<<(unsigned)a.N, kThreads, smem, st>>>(P);
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+}
+
+}  // namespace
+
+gdnx_status launch_compact(const gdnx_compact_args& a, cudaStream_t st) {
+  if (a.R == 4 && a.a_v == 16 && a.a_k == 16 && a.b_v == 8 && a.b_k == 8) return launch_compact_t<Dims16x8>(a, st);
+  if (a.R == 4 && a.a_v == 8 && a.a_k == 8 && a.b_v == 8 && a.b_k == 8) return launch_compact_t<Dims8x8>(a, st);
+  return GDNX_EUNSUPPORTED;
 }
 
 }  // namespace gdnx

@@ -24,11 +24,17 @@ constexpr int kCompMaxM = 256;  // m = a_v * a_k <= 256
 constexpr int kCompThreads = 256;
 constexpr int kCompPT = 16;     // slots per staged tile of U / Vb
 
-struct CompactDims {
-  int R, m, n, q;
-  int a_v, a_k, b_v, b_k;
+// Compile-time Kronecker shape: A_r is a_v x a_k, B_r is b_v x b_k, rank R.
+// Constant dimensions turn every index split in the hot loops into shifts.
+template <int AV, int AK, int BV, int BK, int RR>
+struct KDims {
+  static constexpr int R = RR, a_v = AV, a_k = AK, b_v = BV, b_k = BK;
+  static constexpr int m = AV * AK, n = BV * BK;
+  static constexpr int q = (RR + 4) < (m < n ? m : n) ? (RR + 4) : (m < n ? m : n);
   float delta;
 };
+using Dims16x8 = KDims<16, 16, 8, 8, 4>;  // K = V = 128 (the reference's defaults)
+using Dims8x8 = KDims<8, 8, 8, 8, 4>;     // K = V = 64
 
 // Shared-memory floats the core needs beyond R_mat (which is m x (n+1), padded).
 __host__ __device__ constexpr int compact_work_floats() {
@@ -57,8 +63,9 @@ GDNX_DEV float block_sum(float x, float* red) {
 // Returns err (discarded energy, not clamped) to every thread.  Rm (m x ld)
 // is read only.  A_s [R][m], B_s [R][n] hold the current (true) factors and
 // are overwritten with the blended ones.  G is [n][q] in global memory.
+template <class CD>
 GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float* G,
-                            float* work, const CompactDims d) {
+                            float* work, const CD d) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const int lane = tid % 32, warp = tid / 32;
   const int m = d.m, n = d.n, q = d.q, R = d.R;
@@ -81,28 +88,47 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
 
   for (int idx = tid; idx < n * q; idx += nt) Gs[idx] = G[idx];
   __syncthreads();
-  // Y = R G
-  for (int idx = tid; idx < m * q; idx += nt) {
-    const int i = idx / q, c = idx % q;
-    float acc = 0.f;
-    for (int j = 0; j < n; ++j) acc = fmaf(Rm[i * ld + j], Gs[j * q + c], acc);
-    Y[idx] = acc;
-  }
+  static_assert(CD::q == kCompMaxQ, "register-blocked products assume q = 8");
+  // Y = R X (m x 8) for X = G or Z (n x 8): one thread per row i, X rows broadcast
+  auto row_times = [&](const float* X) {
+    for (int i = tid; i < m; i += nt) {
+      float acc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+      for (int jj = 0; jj < n; ++jj) {
+        const float r = Rm[i * ld + jj];
+        const float4 x0 = *reinterpret_cast<const float4*>(X + jj * 8);
+        const float4 x1 = *reinterpret_cast<const float4*>(X + jj * 8 + 4);
+        acc[0] = fmaf(r, x0.x, acc[0]); acc[1] = fmaf(r, x0.y, acc[1]);
+        acc[2] = fmaf(r, x0.z, acc[2]); acc[3] = fmaf(r, x0.w, acc[3]);
+        acc[4] = fmaf(r, x1.x, acc[4]); acc[5] = fmaf(r, x1.y, acc[5]);
+        acc[6] = fmaf(r, x1.z, acc[6]); acc[7] = fmaf(r, x1.w, acc[7]);
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) Y[i * 8 + c] = acc[c];
+    }
+  };
+  // Out[j][c] = sum_i R[i][j] X[i][c] (n x 8, X = Y or Q): thread -> column j, 2 of the 8 outputs
+  auto col_times = [&](const float* X, float* Out, int out_stride_j, int out_stride_c) {
+    for (int t = tid; t < n * 4; t += nt) {
+      const int jj = t >> 2, c0 = (t & 3) * 2;
+      float a0 = 0.f, a1 = 0.f;
+      for (int i = 0; i < m; ++i) {
+        const float r = Rm[i * ld + jj];
+        const float2 x = *reinterpret_cast<const float2*>(X + i * 8 + c0);
+        a0 = fmaf(r, x.x, a0);
+        a1 = fmaf(r, x.y, a1);
+      }
+      Out[jj * out_stride_j + c0 * out_stride_c] = a0;
+      Out[jj * out_stride_j + (c0 + 1) * out_stride_c] = a1;
+    }
+  };
+  row_times(Gs);
   __syncthreads();
   for (int it = 0; it < 2; ++it) {
-    for (int idx = tid; idx < n * q; idx += nt) {  // Z = R^T Y
-      const int j = idx / q, c = idx % q;
-      float acc = 0.f;
-      for (int i = 0; i < m; ++i) acc = fmaf(Rm[i * ld + j], Y[i * q + c], acc);
-      Z[idx] = acc;
-    }
+    col_times(Y, Z, 8, 1);  // Z = R^T Y
     __syncthreads();
-    for (int idx = tid; idx < m * q; idx += nt) {  // Y = R Z
-      const int i = idx / q, c = idx % q;
-      float acc = 0.f;
-      for (int j = 0; j < n; ++j) acc = fmaf(Rm[i * ld + j], Z[j * q + c], acc);
-      Y[idx] = acc;
-    }
+    row_times(Z);           // Y = R Z
     __syncthreads();
   }
   // Q = orth(Y): one warp, modified Gram-Schmidt with re-orthogonalisation.
@@ -126,13 +152,8 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
     }
   }
   __syncthreads();
-  // Bm = Q^T R   (q x n)
-  for (int idx = tid; idx < q * n; idx += nt) {
-    const int c = idx / n, j = idx % n;
-    float acc = 0.f;
-    for (int i = 0; i < m; ++i) acc = fmaf(Qm[i * q + c], Rm[i * ld + j], acc);
-    Bm[idx] = acc;
-  }
+  // Bm = Q^T R   (q x n), Bm[c][j]
+  col_times(Qm, Bm, 1, n);
   __syncthreads();
   // One-sided Jacobi on W = Bm^T (n x q): lane holds rows lane and lane+32.
   if (warp == 0) {
@@ -147,6 +168,12 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
     float jr[kCompMaxQ];
 #pragma unroll
     for (int c = 0; c < kCompMaxQ; ++c) jr[c] = (lane == c) ? 1.f : 0.f;
+    // Frobenius scale of W: rotations below fp32 resolution of the whole matrix
+    // are skipped, so near-zero (noise) columns cannot keep a sweep alive
+    float fro = 0.f;
+#pragma unroll
+    for (int c = 0; c < kCompMaxQ; ++c) fro += w0[c] * w0[c] + w1[c] * w1[c];
+    fro = warp_sum(fro);
     for (int sweep = 0; sweep < 30; ++sweep) {
       float off = 0.f;
 #pragma unroll
@@ -154,11 +181,17 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
 #pragma unroll
         for (int j = i + 1; j < kCompMaxQ; ++j) {
           if (j >= q) continue;
-          const float al = warp_sum(w0[i] * w0[i] + w1[i] * w1[i]);
-          const float be = warp_sum(w0[j] * w0[j] + w1[j] * w1[j]);
-          const float ga = warp_sum(w0[i] * w0[j] + w1[i] * w1[j]);
+          float al = w0[i] * w0[i] + w1[i] * w1[i];
+          float be = w0[j] * w0[j] + w1[j] * w1[j];
+          float ga = w0[i] * w0[j] + w1[i] * w1[j];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {  // three reductions interleaved
+            al += __shfl_xor_sync(0xffffffffu, al, o);
+            be += __shfl_xor_sync(0xffffffffu, be, o);
+            ga += __shfl_xor_sync(0xffffffffu, ga, o);
+          }
           const float nrm = sqrtf(al * be);
-          if (nrm <= 1e-37f || fabsf(ga) <= 1e-7f * nrm) continue;
+          if (nrm <= 1e-37f || fabsf(ga) <= 1e-6f * nrm || fabsf(ga) <= 1e-9f * fro) continue;
           off = fmaxf(off, fabsf(ga) / nrm);
           const float zeta = (be - al) / (2.f * ga);
           const float t = copysignf(1.f, zeta) / (fabsf(zeta) + sqrtf(1.f + zeta * zeta));
@@ -171,7 +204,7 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
           jr[i] = cs * ja - sn * jb; jr[j] = sn * ja + cs * jb;
         }
       }
-      if (off < 2e-7f) break;
+      if (off < 2e-6f) break;  // columns orthogonal to fp32 working accuracy
     }
     // singular values, descending order (selection; q <= 8)
     float sv[kCompMaxQ];
@@ -234,7 +267,8 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
 }
 
 // Adds sum_r vec(A_r) vec(B_r)^T to Rm (m x ld), A_s [R][m], B_s [R][n].
-GDNX_DEV void add_kron_rmat(float* Rm, const float* A_s, const float* B_s, const CompactDims d) {
+template <class CD>
+GDNX_DEV void add_kron_rmat(float* Rm, const float* A_s, const float* B_s, const CD d) {
   const int ld = compact_ld(d.n);
   for (int idx = threadIdx.x; idx < d.m * d.n; idx += blockDim.x) {
     const int i = idx / d.n, j = idx % d.n;
@@ -246,15 +280,17 @@ GDNX_DEV void add_kron_rmat(float* Rm, const float* A_s, const float* B_s, const
 
 // Rearranged position of dense residual element (v, k):
 // R[(av, ak)][(bv, bk)] = S[av*b_v + bv][ak*b_k + bk].
-GDNX_DEV int rmat_index(int v, int k, const CompactDims d) {
+template <class CD>
+GDNX_DEV int rmat_index(int v, int k, const CD d) {
   const int av = v / d.b_v, bv = v % d.b_v, ak = k / d.b_k, bk = k % d.b_k;
   return (av * d.a_k + ak) * compact_ld(d.n) + bv * d.b_k + bk;
 }
 
 // Rm += rearrange(U diag(dsl) Vb^T) for V*K <= 64*256, built in registers tile by
 // tile (dsl = per-slot scale, nullptr = 1).  Needs blockDim.x == kCompThreads.
+template <class CD>
 GDNX_DEV void add_residual_rmat(float* Rm, const float* U, const float* Vb, const float* dsl, int V, int K, int P,
-                                float* tileU, float* tileV, const CompactDims d) {
+                                float* tileU, float* tileV, const CD d) {
   const int tid = threadIdx.x;
   const int per = (V * K + kCompThreads - 1) / kCompThreads;  // <= 64
   float acc[64];

@@ -127,18 +127,6 @@ GDNX_DEV void load_raw(const DecParams& P, int64_t n, int warp, int lane, ChainR
   r.w = ld_raw(a.gate_w.ptr, a.gate_w.dtype, wo + (P.vec_w ? row : 0));
 }
 
-// Lane RoPE from the per-launch cos/sin table: x1' = x1 c - x2 s; x2' = x1' s + x2 c
-// (the reference's in-place update), same fp32 values as rope_row_warp.
-GDNX_DEV void rope_row_table(float* row, int d, const float* cs, const float* sn, int lane) {
-  for (int i = lane; i < d; i += 32) {
-    const float c = cs[i], s = sn[i];
-    const float x1 = row[i], x2 = row[i + d];
-    const float n1 = x1 * c - x2 * s;
-    row[i] = n1;
-    row[i + d] = n1 * s + x2 * c;
-  }
-}
-
 GDNX_DEV void finish_chain(const DecParams& P, int64_t n, int lane, const ChainRaw& r, float* sk, float* sq,
                            const float* ropeC, const float* ropeS, ChainVals& c) {
   const gdnx_decode_args& a = P.a;

@@ -20,8 +20,9 @@
 //    decays the reference applies;
 //  * A, Bk live in shared memory with one pending scalar decay fac
 //    (true A = fac A_s), folded in before each compaction;
-//  * the Kronecker read uses Z_r = X B_r^T computed cooperatively for the
-//    TB staged tokens, then each row contracts A_r (16 x 16) with Z_r;
+//  * the Kronecker operator sum_r A_r (x) B_r is materialised densely in
+//    registers next to the residual whenever A, Bk change, so its read shares
+//    the residual's loads (its per-token decay is the scalar fac^2);
 //  * compaction runs in-kernel on shared memory (compact.cuh).
 #include "compact.cuh"
 #include "kernels.h"
@@ -35,7 +36,7 @@ constexpr int kMaxP = 1024;
 
 struct KrParams {
   gdnx_kr_scan_args a;
-  CompactDims d;
+  float delta;
   int vec_e, vec_w;
 };
 
@@ -46,8 +47,9 @@ struct KrSmem {
   static constexpr int kTokPer = 4 * K + 2 * V + 8;
 };
 
-template <int K, int V>
+template <class CD>
 __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
+  constexpr int K = CD::a_k * CD::b_k, V = CD::a_v * CD::b_v;
   constexpr int TPR = kNT / V;     // threads per state row
   constexpr int KC = K / 4 / TPR;  // float4 key chunks per thread
   using SMT = KrSmem<K, V>;
@@ -55,9 +57,9 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   float* sm = reinterpret_cast<float*>(smem4);
   const gdnx_kr_scan_args& A = P.a;
   const gdnx_scan_args& a = A.base;
-  const CompactDims d = P.d;
+  CD d;
+  d.delta = P.delta;
   const int R = d.R, Pn = A.P;
-  const int zper = R * d.a_k * d.b_v;  // Z floats per vector
   const int ld = compact_ld(d.n);
 
   // ---- shared memory carve-up ----
@@ -67,12 +69,14 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   float* B_s = A_s + R * d.m;                      // R x n
   float* dsl = B_s + R * d.n;                      // per-slot decay [P]
   float* tok = dsl + kMaxP;                        // kTB x kTokPer
-  float* Zb = tok + kTB * SMT::kTokPer;            // kTB x 2 x zper
-  float* ybuf = Zb + kTB * 2 * zper;               // kTB x V
+  float* ybuf = tok + kTB * SMT::kTokPer;          // kTB x V
   float* nbuf = ybuf + kTB * V;                    // kTB x V (new U columns)
   float* tileU = nbuf + kTB * V;                   // V x kCompPT
   float* tileV = tileU + V * kCompPT;              // K x kCompPT
   float* misc = tileV + K * kCompPT;               // 32 floats
+  float* ropeC = misc + 32;                        // kTB x 64 (cos of this block's angles)
+  float* ropeS = ropeC + kTB * 64;                 // kTB x 64
+  float* sInv = ropeS + kTB * 64;                  // 64 inverse frequencies
 
   const int64_t n = blockIdx.x;
   const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
@@ -90,6 +94,8 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   for (int i = tid; i < R * d.n; i += kNT) B_s[i] = Bg[i];
   for (int i = tid; i < Pn; i += kNT) dsl[i] = 1.f;
   int p = A.slot[n];
+  const int dpairs = (a.rope.enable && m < 4) ? a.rope.pairs[m] : 0;
+  if (tid < 64 && dpairs > 0) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[m]);
   float fac = 1.f, err_acc = 0.f;
 
   float4 Rs[KC];
@@ -108,7 +114,27 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
     }
     __syncthreads();
   };
+  // dense Kronecker operator sum_r A_r (x) B_r (row v, this thread's keys), materialised
+  // whenever A_s / B_s change (start, compaction); its decay is the scalar fac^2
+  float4 Ks[KC];
+  auto build_kron = [&]() {
+#pragma unroll
+    for (int c = 0; c < KC; ++c) {
+      float kv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int kk = 4 * (c * TPR + j) + e;
+        const int ak = kk / CD::b_k, bk = kk % CD::b_k;
+        float acc = 0.f;
+#pragma unroll
+        for (int r = 0; r < CD::R; ++r) acc = fmaf(A_s[r * d.m + av * d.a_k + ak], B_s[r * d.n + bv * d.b_k + bk], acc);
+        kv[e] = acc;
+      }
+      Ks[c] = make_float4(kv[0], kv[1], kv[2], kv[3]);
+    }
+  };
   rebuild();
+  build_kron();
 
   int64_t t0 = 0;
   while (t0 < a.T) {
@@ -116,7 +142,14 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
     if (nt64 > kTB) nt64 = kTB;
     if (nt64 > Pn - p) nt64 = Pn - p;
     const int nt = (int)nt64;
-    // ---------- stage A: per-token vectors (one warp per token) ----------
+    // ---------- stage A: RoPE angles of the block, then per-token vectors (one warp per token) ----------
+    if (dpairs > 0) {
+      for (int idx = tid; idx < nt * dpairs; idx += kNT) {
+        const int tt = idx / dpairs, i = idx - tt * dpairs;
+        sincosf(((float)(a.rope.pos0 + t0 + tt) * a.rope.scale[m]) * sInv[i], &ropeS[tt * 64 + i], &ropeC[tt * 64 + i]);
+      }
+      __syncthreads();
+    }
     for (int tt = warp; tt < nt; tt += kNT / 32) {
       const int64_t t = t0 + tt;
       float* tk = tok + tt * SMT::kTokPer;
@@ -129,20 +162,20 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
         sq[i] = ld_as_f32(a.q.ptr, a.q.dtype, qo + i);
       }
       __syncwarp();
-      rope_row_warp(sk, a.rope, (int)m, a.rope.pos0 + t, lane);
-      rope_row_warp(sq, a.rope, (int)m, a.rope.pos0 + t, lane);
+      if (dpairs > 0) {
+        rope_row_table(sk, dpairs, ropeC + tt * 64, ropeS + tt * 64, lane);
+        rope_row_table(sq, dpairs, ropeC + tt * 64, ropeS + tt * 64, lane);
+      }
       __syncwarp();
       const int64_t eo = view_off(a.gate_e, b, t, h, m), wo = view_off(a.gate_w, b, t, h, m);
       const float be = P.vec_e ? 1.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
       const float bw = P.vec_w ? 1.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo);
       float kh = 0.f, kq = 0.f;
-      const int ps = p + tt;  // slot overwritten by this token
       for (int i = lane; i < K; i += 32) {
         const float hv = (P.vec_e ? ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo + i) : be) * sk[i];
         sh[i] = hv;
         kh += sk[i] * hv;
         kq += sk[i] * sq[i];
-        tk[SMT::kTokKold + i] = Vg[(int64_t)i * Pn + ps];
       }
       kh = warp_sum(kh);
       kq = warp_sum(kq);
@@ -150,7 +183,6 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       for (int i = lane; i < V; i += 32) {
         const float wv = P.vec_w ? ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo + i) : bw;
         tk[SMT::kTokU + i] = wv * ld_as_f32(a.v.ptr, a.v.dtype, vo + i);
-        tk[SMT::kTokUold + i] = Ug[(int64_t)i * Pn + ps];
       }
       if (lane == 0) {
         float* sc = tk + SMT::kTokSc;
@@ -160,8 +192,17 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
         sc[2] = kq;
       }
     }
+    // the slots this block overwrites (p .. p+nt-1): rows of U and Vb, nt contiguous floats each
+    for (int idx = tid; idx < K * nt; idx += kNT) {
+      const int kk = idx / nt, tt = idx - kk * nt;
+      tok[tt * SMT::kTokPer + SMT::kTokKold + kk] = Vg[(int64_t)kk * Pn + p + tt];
+    }
+    for (int idx = tid; idx < V * nt; idx += kNT) {
+      const int vv = idx / nt, tt = idx - vv * nt;
+      tok[tt * SMT::kTokPer + SMT::kTokUold + vv] = Ug[(int64_t)vv * Pn + p + tt];
+    }
     __syncthreads();
-    // ---------- stage B: running decays (thread 0) and Z = X B^T (all) ----------
+    // ---------- stage B: running decays (thread 0) ----------
     if (tid == 0) {
       float f = fac, pre = 1.f;
       for (int tt = 0; tt < nt; ++tt) {
@@ -174,34 +215,13 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       misc[0] = f;
       misc[1] = pre;
     }
-    for (int idx = tid; idx < nt * 2 * zper; idx += kNT) {
-      const int tt = idx / (2 * zper), rem = idx % (2 * zper);
-      const int which = rem / zper, z = rem % zper;    // 0: h, 1: q
-      const int r = z / (d.a_k * d.b_v), ak = (z / d.b_v) % d.a_k, bvv = z % d.b_v;
-      const float* x = tok + tt * SMT::kTokPer + (which ? SMT::kTokQ : SMT::kTokH) + ak * d.b_k;
-      const float* br = B_s + r * d.n + bvv * d.b_k;
-      float acc = 0.f;
-      for (int bk = 0; bk < d.b_k; ++bk) acc = fmaf(x[bk], br[bk], acc);
-      Zb[idx] = acc;
-    }
     __syncthreads();
     // ---------- sequential token updates ----------
     for (int tt = 0; tt < nt; ++tt) {
       const float* tk = tok + tt * SMT::kTokPer;
       const float* sc = tk + SMT::kTokSc;
       const float gam = sc[0], al = sc[1], kq = sc[2], ks = sc[3], ev = sc[4];
-      // Kronecker reads (row v): sum_{r,ak} A_r[av][ak] Z_r[ak][bv], split over j
-      const float* Zh = Zb + tt * 2 * zper;
-      const float* Zq = Zh + zper;
-      float krh = 0.f, krq = 0.f;
-      for (int e = j; e < R * d.a_k; e += TPR) {
-        const int r = e / d.a_k, ak = e % d.a_k;
-        const float aw = A_s[r * d.m + av * d.a_k + ak];
-        const int zi = (r * d.a_k + ak) * d.b_v + bv;
-        krh = fmaf(aw, Zh[zi], krh);
-        krq = fmaf(aw, Zq[zi], krq);
-      }
-      float dh = 0.f, dq = 0.f;
+      float krh = 0.f, krq = 0.f, dh = 0.f, dq = 0.f;
 #pragma unroll
       for (int c = 0; c < KC; ++c) {
         const int k0 = 4 * (c * TPR + j);
@@ -211,6 +231,10 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
         dh = fmaf(Rs[c].z, h4.z, dh); dh = fmaf(Rs[c].w, h4.w, dh);
         dq = fmaf(Rs[c].x, q4.x, dq); dq = fmaf(Rs[c].y, q4.y, dq);
         dq = fmaf(Rs[c].z, q4.z, dq); dq = fmaf(Rs[c].w, q4.w, dq);
+        krh = fmaf(Ks[c].x, h4.x, krh); krh = fmaf(Ks[c].y, h4.y, krh);
+        krh = fmaf(Ks[c].z, h4.z, krh); krh = fmaf(Ks[c].w, h4.w, krh);
+        krq = fmaf(Ks[c].x, q4.x, krq); krq = fmaf(Ks[c].y, q4.y, krq);
+        krq = fmaf(Ks[c].z, q4.z, krq); krq = fmaf(Ks[c].w, q4.w, krq);
       }
 #pragma unroll
       for (int o = 1; o < TPR; o <<= 1) {
@@ -280,6 +304,7 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       err_acc += compact_core(Rm, A_s, B_s, Gg, work, d);
       p = 0;
       __syncthreads();
+      build_kron();
     }
   }
   // ---------- materialise the state ----------
@@ -292,14 +317,14 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   }
 }
 
-template <int K, int V>
+template <class CD>
 gdnx_status launch_kr(const KrParams& P, cudaStream_t st) {
-  const CompactDims& d = P.d;
-  const int zper = d.R * d.a_k * d.b_v;
+  constexpr int K = CD::a_k * CD::b_k, V = CD::a_v * CD::b_v;
+  const CD d{};
   const size_t floats = (size_t)d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) + kMaxP +
-                        kTB * KrSmem<K, V>::kTokPer + kTB * 2 * zper + 2 * kTB * V + (V + K) * kCompPT + 32;
+                        kTB * KrSmem<K, V>::kTokPer + 2 * kTB * V + (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
   const size_t smem = floats * sizeof(float);
-  auto fn = kr_scan_kernel<K, V>;
+  auto fn = kr_scan_kernel<CD>;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GDNX_ELAUNCH;
   const int64_t N = P.a.base.B * P.a.base.H * P.a.base.M;
@@ -314,16 +339,14 @@ gdnx_status launch_kr_scan(const gdnx_kr_scan_args& a, cudaStream_t st) {
   P.a = a;
   P.vec_e = a.base.gate_e.dim > 1;
   P.vec_w = a.base.gate_w.dim > 1;
-  CompactDims& d = P.d;
-  d.R = a.R; d.a_v = a.a_v; d.a_k = a.a_k; d.b_v = a.b_v; d.b_k = a.b_k;
-  d.m = a.a_v * a.a_k; d.n = a.b_v * a.b_k;
-  d.q = min(a.R + 4, min(d.m, d.n));
-  d.delta = a.slow_decay;
-  if (d.m > kCompMaxM || d.n > kCompMaxN || d.q > kCompMaxQ || d.R > d.q) return GDNX_EUNSUPPORTED;
+  P.delta = a.slow_decay;
   if (a.P > kMaxP) return GDNX_EUNSUPPORTED;
   const int64_t K = a.base.K, V = a.base.V;
-  if (K == 128 && V == 128) return launch_kr<128, 128>(P, st);
-  if (K == 64 && V == 64) return launch_kr<64, 64>(P, st);
+  const bool r4 = a.R == 4;
+  if (r4 && K == 128 && V == 128 && a.a_v == 16 && a.a_k == 16 && a.b_v == 8 && a.b_k == 8)
+    return launch_kr<Dims16x8>(P, st);
+  if (r4 && K == 64 && V == 64 && a.a_v == 8 && a.a_k == 8 && a.b_v == 8 && a.b_k == 8)
+    return launch_kr<Dims8x8>(P, st);
   return GDNX_EUNSUPPORTED;
 }
 

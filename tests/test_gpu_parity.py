@@ -409,3 +409,20 @@ def test_kmd2_fast_scan_dropin(case):
     y = kmd2_fast_scan.scan(*args, mixg)
     y2, sc = kmd2_fast_scan.scan_with_update_norm(*args, mixg)
     assert rel(y, c["y"]) < TOL32 and rel(y2, c["y"]) < TOL32 and rel(sc, c["scores"]) < TOL32
+
+
+def test_kr_scan_with_lane_rope_and_log_decay():
+    inp = scan_inputs(1, 40, 2, 4, 128, 128, seed=71)
+    M, K, rf, P = 4, 128, 0.5, 16
+    qx = PR.apply_lane_rope(inp["q"].unsqueeze(3).expand(-1, -1, -1, M, -1).contiguous(), K, rf)
+    kx = PR.apply_lane_rope(inp["k"].unsqueeze(3).expand(-1, -1, -1, M, -1).contiguous(), K, rf)
+    vx = inp["v"].unsqueeze(3).expand(-1, -1, -1, M, -1)
+    bg = inp["beta"].unsqueeze(-1).expand(-1, -1, -1, -1, K)
+    N = 1 * 2 * M
+    G = R.sketch_matrix(N, 64, 8)
+    Yo, st = R.gdn3_kr_scan(qx, kx, vx, bg, bg, torch.exp(inp["logg"]), R=4, P=P, G=G, canon_signs=True)
+    state = ops.KRState.zeros(N, 4, P, (16, 16, 8, 8), K, K, DEV)
+    q, k, v, beta, logg = gpu(inp["q"], inp["k"], inp["v"], inp["beta"], inp["logg"])
+    y = ops.gdn3_kr_scan(q, k, v, beta, beta, logg, state, G.to(DEV), P=P, decay_kind="log",
+                         rope=lane_rope(M, K, K, rf))
+    assert rel(y, Yo) < TOL32 and rel(state.U, st.U) < TOL32
