@@ -37,7 +37,7 @@ namespace {
 constexpr int C = 64;         // chunk length
 constexpr int KD = 128;       // key dim
 constexpr int VD = 128;       // value dim
-constexpr int NT = 256;       // threads
+constexpr int NT = 512;       // threads: 16 warps, four per TMEM lane quadrant
 constexpr int TMEM_COLS = 256;
 
 // shared-memory map (bytes from a 1024-aligned base)
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
 
   const gdnx_scan_args& a = P.a;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, hf = warp >> 2;
+  const int quad = warp & 3, qg = warp >> 2;  // lane quadrant, column group (0..3)
   const int row = quad * 32 + lane;  // TMEM lane owned by this thread
   const int64_t n = blockIdx.x;
   const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
@@ -143,8 +143,8 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
   {
     float vals[32];
 #pragma unroll
-    for (int c2 = 0; c2 < 2; ++c2) {
-      const int col = 64 * hf + 32 * c2;
+    for (int c2 = 0; c2 < 1; ++c2) {
+      const int col = 32 * qg;
       if (a.state_in) {
         const float* src = a.state_in + (n * VD + row) * KD + col;
 #pragma unroll
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
   // per-token scalars (raw bits) into warp 0's registers
   uint32_t pr_be[2], pr_bw[2], pr_dec[2][4];
   // Fixed per-thread prefetch slots: thread tid moves 16-byte chunk cc = tid % 16 of
-  // token rows j0 + 16 r (r < 4) for each of q, k, v.
+  // token rows j0 + 32 r (r < 2) for each of q, k, v.
   const int pf_cc = tid & 15, pf_j0 = tid >> 4;
   const __nv_bfloat16* pf_src[3];
   int64_t pf_st[3];
@@ -186,10 +186,10 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
     const int64_t tb = chn * C;
     for (int w = w0; w < w1; ++w) {
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int64_t tt = tb + pf_j0 + 16 * r;
+      for (int r = 0; r < C / (NT / 16); ++r) {
+        const int64_t tt = tb + pf_j0 + (NT / 16) * r;
         const bool valid = tt < a.T;
-        cp_async16(pf_dst + w * 16384 + r * 16 * 256, valid ? pf_src[w] + tt * pf_st[w] : pf_src[w], valid);
+        cp_async16(pf_dst + w * 16384 + r * (NT / 16) * 256, valid ? pf_src[w] + tt * pf_st[w] : pf_src[w], valid);
       }
     }
     cp_async_commit();
@@ -333,8 +333,8 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
       const float eLC = s_misc[0];
       float vals[32];
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        const int col = 64 * hf + 32 * c2;
+      for (int c2 = 0; c2 < 1; ++c2) {
+        const int col = 32 * qg;
         tc::tmem_ld32(tS + lbase + col, vals);
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(cS0, tc::sw128(row, col / 8 + q4, 128), vals + 8 * q4);
@@ -368,35 +368,35 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
 
     // ================= Phase C: masks, RHS, Qd, T = (I+A)^{-1} =================
     {
-      float d[32];
-      tc::tmem_ld32(tD1 + lbase + 32 * hf, d);
+      float d[16];
+      tc::tmem_ld16(tD1 + lbase + 16 * qg, d);
       if (row < 64) {
         const int j = row;
         const float Lj = sL[j], cej = sCE[j];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int l = 32 * hf + e;
+        for (int e = 0; e < 16; ++e) {
+          const int l = 16 * qg + e;
           Lm[j * 65 + l] = (l < j) ? cej * exp2f(Lj - sL[l]) * d[e] : 0.f;
         }
       } else {
         const int i = row - 64;
         const float Li = sL[i];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int jj = 32 * hf + e;
+        for (int e = 0; e < 16; ++e) {
+          const int jj = 16 * qg + e;
           d[e] = (jj <= i) ? exp2f(Li - sL[jj]) * d[e] : 0.f;
         }
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(cMQ, tc::sw128(i, 4 * hf + q4, 64), d + 8 * q4);
+        for (int q4 = 0; q4 < 2; ++q4) tc::st_chunk_bf16(cMQ, tc::sw128(i, 2 * qg + q4, 64), d + 8 * q4);
       }
-      tc::tmem_ld32(tD2 + lbase + 32 * hf, d);
+      tc::tmem_ld16(tD2 + lbase + 16 * qg, d);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int j = 32 * hf + e;
+      for (int e = 0; e < 16; ++e) {
+        const int j = 16 * qg + e;
         d[e] = sCW[j] * __bfloat162float(hSTV[j * VD + row]) - sCE[j] * sE[j] * d[e];
       }
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(cRHS, tc::sw128(row, 4 * hf + q4, 128), d + 8 * q4);
+      for (int q4 = 0; q4 < 2; ++q4) tc::st_chunk_bf16(cRHS, tc::sw128(row, 2 * qg + q4, 128), d + 8 * q4);
       // Qd = e^{L_i} q_i in place (rows 64..127 of KQ; G1 has consumed them)
       for (int it = tid; it < C * 16; it += NT) {
         const int i = it >> 4, cc = it & 15;
@@ -505,14 +505,14 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
 
     // ================= Phase E: W^T -> bf16 tiles W and W' = W e^{L_C - L_j} =================
     {
-      float w[32], w2[32];
-      tc::tmem_ld32(tD2 + lbase + 32 * hf, w);
+      float w[16], w2[16];
+      tc::tmem_ld16(tD2 + lbase + 16 * qg, w);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) w2[e] = w[e] * sEC[32 * hf + e];
+      for (int e = 0; e < 16; ++e) w2[e] = w[e] * sEC[16 * qg + e];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        tc::st_chunk_bf16(cW, tc::sw128(row, 4 * hf + q4, 128), w + 8 * q4);
-        tc::st_chunk_bf16(cRHS, tc::sw128(row, 4 * hf + q4, 128), w2 + 8 * q4);
+      for (int q4 = 0; q4 < 2; ++q4) {
+        tc::st_chunk_bf16(cW, tc::sw128(row, 2 * qg + q4, 128), w + 8 * q4);
+        tc::st_chunk_bf16(cRHS, tc::sw128(row, 2 * qg + q4, 128), w2 + 8 * q4);
       }
     }
     tc::fence_async_smem();
@@ -540,14 +540,14 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
 
     // ================= Phase G: outputs =================
     {
-      float yv[32];
-      tc::tmem_ld32(tD1 + lbase + 32 * hf, yv);
+      float yv[16];
+      tc::tmem_ld16(tD1 + lbase + 16 * qg, yv);
       if (y_tile) {
         // stage the chunk's outputs as bf16 [token][v] (in the A-matrix scratch), then
         // write each token's 256-byte row with 16-byte stores
         __nv_bfloat16* ys = reinterpret_cast<__nv_bfloat16*>(Lm);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ys[(32 * hf + e) * VD + row] = __float2bfloat16_rn(yv[e]);
+        for (int e = 0; e < 16; ++e) ys[(16 * qg + e) * VD + row] = __float2bfloat16_rn(yv[e]);
         __syncthreads();
         const int64_t ybase = b * a.y_sb + h * a.y_sh + m * a.y_sm;
         for (int it = tid; it < C * 16; it += NT) {
@@ -559,8 +559,8 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
       } else {
         const int64_t yo = b * a.y_sb + h * a.y_sh + m * a.y_sm + row;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int i = 32 * hf + e;
+        for (int e = 0; e < 16; ++e) {
+          const int i = 16 * qg + e;
           if (i < nt) st_from_f32(a.y, a.y_dtype, yo + (t0 + i) * a.y_st, yv[e]);
         }
       }
@@ -573,8 +573,8 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
     tc::fence_after();
     float vals[32];
 #pragma unroll
-    for (int c2 = 0; c2 < 2; ++c2) {
-      const int col = 64 * hf + 32 * c2;
+    for (int c2 = 0; c2 < 1; ++c2) {
+      const int col = 32 * qg;
       tc::tmem_ld32(tS + lbase + col, vals);
       float* dst = a.state_out + (n * VD + row) * KD + col;
 #pragma unroll
