@@ -90,6 +90,27 @@ __device__ __forceinline__ float raw_f32(uint32_t r, int dtype) {
   return __half2float(__ushort_as_half((unsigned short)r));
 }
 
+// sin and cos of an fp32 angle: Cody-Waite reduction by 2*pi (2*pi split into a
+// float head and tail, so the reduced argument is exact to ~1e-10 for |x| up to
+// ~1e5), then the hardware sine/cosine on [-pi, pi] (absolute error ~5e-7).
+__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+  constexpr float kInv2Pi = 0.15915494309189535f;
+  constexpr float k2PiHi = 6.2831854820251465f;    // float(2*pi)
+  constexpr float k2PiLo = -1.7484556000744e-07f;  // 2*pi - float(2*pi)
+  const float k = rintf(x * kInv2Pi);
+  float r = fmaf(-k, k2PiHi, x);
+  r = fmaf(-k, k2PiLo, r);
+  __sincosf(r, s, c);
+}
+
+__device__ __forceinline__ void bulk_row(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(dst), "l"(src), "r"(bytes), "r"(mbar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(mbar), "r"(bytes) : "memory");
+}
+
 __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P) {
   extern __shared__ uint8_t smraw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
@@ -114,6 +135,7 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
   float* s_misc = reinterpret_cast<float*>(sm + OFF_BAR + 16);
+  uint64_t* stage_bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 32);
 
   const gdnx_scan_args& a = P.a;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -126,7 +148,10 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
   const int dch = dpairs / 8;
 
   if (warp == 0) tc::tmem_alloc(s_tmem, TMEM_COLS);
-  if (tid == 0) tc::mbar_init(mbar, 1);
+  if (tid == 0) {
+    tc::mbar_init(mbar, 1);
+    tc::mbar_init(stage_bar, 1);
+  }
   if (dpairs > 0 && tid < 64) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[lm]);
   tc::fence_before();
   __syncthreads();
@@ -168,31 +193,35 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
   // next-chunk prefetch: q/k/v rows into the staging tiles with cp.async, and the
   // per-token scalars (raw bits) into warp 0's registers
   uint32_t pr_be[2], pr_bw[2], pr_dec[2][4];
-  // Fixed per-thread prefetch slots: thread tid moves 16-byte chunk cc = tid % 16 of
-  // token rows j0 + 32 r (r < 2) for each of q, k, v.
-  const int pf_cc = tid & 15, pf_j0 = tid >> 4;
-  const __nv_bfloat16* pf_src[3];
-  int64_t pf_st[3];
-  {
-    const gdnx_view* vw[3] = {&a.q, &a.k, &a.v};
-#pragma unroll
-    for (int w = 0; w < 3; ++w) {
-      pf_src[w] = reinterpret_cast<const __nv_bfloat16*>(vw[w]->ptr) + view_off(*vw[w], b, 0, h, m) + 8 * pf_cc;
-      pf_st[w] = vw[w]->st;
-    }
+  // Next-chunk staging of the raw q/k/v rows: one 256-byte bulk copy per token row
+  // (3 x 64 per chunk, issued by warps 0-5), counted on stage_bar; rows past T are
+  // zero-filled with plain stores instead.
+  const __nv_bfloat16* pf_src = nullptr;
+  int64_t pf_st = 0;
+  if (warp < 6) {
+    const gdnx_view& vw = warp < 2 ? a.q : (warp < 4 ? a.k : a.v);
+    pf_src = reinterpret_cast<const __nv_bfloat16*>(vw.ptr) + view_off(vw, b, 0, h, m);
+    pf_st = vw.st;
   }
-  const uint32_t pf_dst = tc::smem_u32(sm + OFF_STQ) + pf_j0 * 256 + pf_cc * 16;
-  auto prefetch_rows = [&](int64_t chn, int w0, int w1) {
+  const uint32_t sbar = tc::smem_u32(stage_bar);
+  const uint32_t pf_dst = tc::smem_u32(sm + OFF_STQ) + (warp >> 1) * 16384 + ((warp & 1) * 32 + lane) * 256;
+  uint32_t stage_phase = 0;
+  auto prefetch_rows = [&](int64_t chn, int, int) {
     const int64_t tb = chn * C;
-    for (int w = w0; w < w1; ++w) {
+    const int nv = (int)((a.T - tb) < C ? (a.T - tb) : C);
+    if (tid == 0) mbar_expect_tx(sbar, 3u * nv * 256u);
+    __syncwarp();
+    if (warp < 6) {
+      const int j = (warp & 1) * 32 + lane;
+      if (j < nv) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        bulk_row(pf_dst, pf_src + (tb + j) * pf_st, 256, sbar);
+      } else {
+        uint4* z = reinterpret_cast<uint4*>(sm + OFF_STQ + (warp >> 1) * 16384 + j * 256);
 #pragma unroll
-      for (int r = 0; r < C / (NT / 16); ++r) {
-        const int64_t tt = tb + pf_j0 + (NT / 16) * r;
-        const bool valid = tt < a.T;
-        cp_async16(pf_dst + w * 16384 + r * (NT / 16) * 256, valid ? pf_src[w] + tt * pf_st[w] : pf_src[w], valid);
+        for (int c = 0; c < 16; ++c) z[c] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    cp_async_commit();
   };
   const int64_t sc_e0 = view_off(a.gate_e, b, 0, h, m), sc_w0 = view_off(a.gate_w, b, 0, h, m);
   const int64_t sc_d0 = view_off(a.decay, b, 0, h, m);
@@ -221,8 +250,12 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
     const int nt = (int)((a.T - t0) < C ? (a.T - t0) : C);
 
     // ================= Phase A: fused prologue =================
-    cp_async_wait_all();
-    __syncthreads();
+    {
+      // staged rows of this chunk: bulk copies (mbarrier) and zero-filled tails (barrier)
+      const bool ok = tc::mbar_wait(stage_bar, stage_phase & 1);
+      ++stage_phase;
+      if (__syncthreads_or(!ok)) { aborted = true; break; }
+    }
     // RoPE angle table for the chunk (spread evenly over all threads), parked in Tm
     float* tabC = Tm;
     float* tabS = Tm + C * 32;
@@ -231,7 +264,7 @@ __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P
       for (int idx = tid; idx < C * dpairs; idx += NT) {
         const int j = idx / dpairs, i = idx - j * dpairs;
         float sn, cs;
-        sincosf((float)(a.rope.pos0 + t0 + j) * sc * sInv[i], &sn, &cs);
+        sincos_reduced((float)(a.rope.pos0 + t0 + j) * sc * sInv[i], &sn, &cs);
         tabC[j * 32 + i] = cs;
         tabS[j * 32 + i] = sn;
       }
