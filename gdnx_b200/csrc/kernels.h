@@ -14,7 +14,12 @@ gdnx_status launch_kr_scan(const gdnx_kr_scan_args& a, cudaStream_t st);
 bool chunked_eligible(const gdnx_scan_args& a);
 size_t chunked_workspace_bytes(const gdnx_scan_args& a);
 gdnx_status launch_chunked_scan(const gdnx_scan_args& a, cudaStream_t st);
-// Same kernel with its scratch in a library-owned static device array (no allocation).
+// Two-pass WY scan (scan_wy.cu): workspace = error word + per-chunk T tiles and
+// decay prefixes.  Returns GDNX_EUNSUPPORTED when q/k/v cannot be described by
+// TMA tensor maps (the single-pass kernel then runs instead).
+size_t wy_workspace_bytes(const gdnx_scan_args& a);
+gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st);
+// Single-pass kernel with its scratch in a library-owned static device array (no allocation).
 gdnx_status launch_chunked_scan_static_scratch(const gdnx_scan_args& a, cudaStream_t st);
 
 }  // namespace gdnx

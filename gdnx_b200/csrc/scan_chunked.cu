@@ -27,12 +27,15 @@
 // and exits.
 #include <mutex>
 
+#include "chunk_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
 
 namespace gdnx {
 namespace {
+
+using namespace chunk;
 
 constexpr int C = 64;         // chunk length
 constexpr int KD = 128;       // key dim
@@ -62,46 +65,6 @@ struct ChunkParams {
   int* err;
 };
 
-__device__ __forceinline__ void load8_bf16(const void* base, int64_t off, float* x) {
-  const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + off);
-  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(p[i]);
-    x[2 * i] = f.x;
-    x[2 * i + 1] = f.y;
-  }
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-// Raw bits of one element (converted later, so a prefetch does not stall on its load).
-__device__ __forceinline__ uint32_t ld_raw(const void* base, int dtype, int64_t off) {
-  if (dtype == GDNX_F32) return reinterpret_cast<const uint32_t*>(base)[off];
-  return reinterpret_cast<const uint16_t*>(base)[off];
-}
-__device__ __forceinline__ float raw_f32(uint32_t r, int dtype) {
-  if (dtype == GDNX_F32) return __uint_as_float(r);
-  if (dtype == GDNX_BF16) return __uint_as_float(r << 16);
-  return __half2float(__ushort_as_half((unsigned short)r));
-}
-
-// sin and cos of an fp32 angle: Cody-Waite reduction by 2*pi (2*pi split into a
-// float head and tail, so the reduced argument is exact to ~1e-10 for |x| up to
-// ~1e5), then the hardware sine/cosine on [-pi, pi] (absolute error ~5e-7).
-__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
-  constexpr float kInv2Pi = 0.15915494309189535f;
-  constexpr float k2PiHi = 6.2831854820251465f;    // float(2*pi)
-  constexpr float k2PiLo = -1.7484556000744e-07f;  // 2*pi - float(2*pi)
-  const float k = rintf(x * kInv2Pi);
-  float r = fmaf(-k, k2PiHi, x);
-  r = fmaf(-k, k2PiLo, r);
-  __sincosf(r, s, c);
-}
 
 __device__ __forceinline__ void bulk_row(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -646,9 +609,10 @@ bool chunked_eligible(const gdnx_scan_args& a) {
   return true;
 }
 
-size_t chunked_workspace_bytes(const gdnx_scan_args&) { return 256; }  // device error word
+size_t chunked_workspace_bytes(const gdnx_scan_args& a) { return wy_workspace_bytes(a); }
 
-gdnx_status launch_chunked_scan(const gdnx_scan_args& a, cudaStream_t st) {
+// Single-pass kernel: needs only the device error word (the first 256 bytes).
+gdnx_status launch_fused_chunked_scan(const gdnx_scan_args& a, cudaStream_t st) {
   ChunkParams P;
   P.a = a;
   P.kmd2 = a.mode == GDNX_MODE_KMD2;
@@ -659,6 +623,11 @@ gdnx_status launch_chunked_scan(const gdnx_scan_args& a, cudaStream_t st) {
   const int64_t N = a.B * a.H * a.M;
   chunked_scan_kernel<<<(unsigned)N, NT, SMEM_BYTES, st>>>(P);
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+}
+
+gdnx_status launch_chunked_scan(const gdnx_scan_args& a, cudaStream_t st) {
+  const gdnx_status s = launch_wy_scan(a, st);
+  return s == GDNX_EUNSUPPORTED ? launch_fused_chunked_scan(a, st) : s;
 }
 
 // ---------------------------------------------------------------------------
@@ -695,7 +664,6 @@ gdnx_status static_scratch(void** out) {
 
 gdnx_status launch_chunked_scan_static_scratch(const gdnx_scan_args& a, cudaStream_t st) {
   if (!chunked_eligible(a)) return GDNX_EUNSUPPORTED;
-  if (chunked_workspace_bytes(a) > kStaticScratchBytes) return GDNX_EWORKSPACE;
   void* scratch = nullptr;
   const gdnx_status s = static_scratch(&scratch);
   if (s != GDNX_OK) return s;

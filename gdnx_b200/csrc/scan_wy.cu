@@ -1,0 +1,991 @@
+// Two-pass chunked gated-delta scan on sm_100a (dense GDN3 / KMD-2 with
+// per-chain scalar gates and decay, d_k = d_v = 128, C = 64).
+//
+// The delta rule over one chunk of one chain (tokens j = 0..63, log2 decay
+// prefix L_j, erase/write coefficients ce_j, cw_j; gdn3/_reference_recurrence.py:61-84,
+// research/kernel_ab/ref_scan.py:40-47 for the single-token step) is, in the
+// WY/UT form,
+//   A   = strictly-lower( ce_j 2^{L_j - L_l} k_j.k_l )          (64 x 64)
+//   T   = (I + A)^{-1}
+//   W   = T diag(cw) V - T diag(ce 2^L) K S0^T                 (64 x 128)
+//   y_i = 2^{L_i} S0 q_i + sum_{j<=i} 2^{L_i - L_j} (q_i.k_j) W_j
+//   S   = 2^{L_C} S0 + sum_j 2^{L_C - L_j} W_j k_j^T
+// Everything before the first use of S0 is independent of the state, so it is
+// split off:
+//   pass 1 (wy_prep_kernel, one CTA per pair of chunks, all chunks in parallel):
+//     lane RoPE on k, gates (alpha, ce, cw), decay prefix L, the Gram matrix
+//     k k^T on the tensor cores, the masks, T by forward substitution in fp32,
+//     and T_e = T diag(ce 2^L), T_w = T diag(cw) written as bf16 tiles already
+//     in the 128-byte-swizzled UMMA layout, plus L.
+//   pass 2 (wy_scan_kernel, one CTA per chain, chunks in sequence):
+//     TMA loads of q/k/v (two stages ahead), bulk loads of T_e, T_w, L,
+//     lane RoPE of q/k in shared memory, then three tcgen05 groups per chunk:
+//       G1  [K;Q] K^T -> masks, K^T T_e^T -> Wk^T, V^T T_w^T -> W^T (init),
+//           S0 Q^T -> y_S                                    (S0 = bf16 state)
+//       G2  W^T -= S0 Wk^T
+//       G3  y_W = W^T Mq^T,  S += W'^T K                    (K read MN-major)
+//     with the fp32 state in TMEM for the whole sequence.
+// The state is kept as S = 2^{ls} S_tmem with a running log2 scale ls, so the
+// per-chunk decay 2^{L_C} is folded into the bf16 operands instead of a TMEM
+// read-modify-write; when ls + L_C would drop below -40 the scale is applied
+// to TMEM and reset.  Every mbarrier wait is bounded (GDNX_ETIMEOUT in the
+// workspace error word, TMEM freed, kernel returns).
+#include <cuda.h>
+#include <mutex>
+
+#include "chunk_common.cuh"
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace gdnx {
+namespace {
+
+using namespace chunk;
+
+constexpr int C = 64;
+constexpr int KD = 128;
+constexpr int VD = 128;
+constexpr int LDA = 68;                    // fp32 row stride of the A matrices (16-byte rows)
+constexpr int64_t TT_ELEMS = 3 * C * C;    // bf16 elements of T_e, T_w, Mq^T per chain-chunk
+constexpr size_t ERR_BYTES = 256;
+// Chunks whose total log2 decay L_C is at least this take the folded path: pass 1
+// stores Mq'_il = 2^{-L_l} q_i.k_l (j <= i) and pass 2 scales y_i by 2^{L_i} on the
+// way out, so q is used unscaled; below it, pass 1 stores Mq_il = 2^{L_i - L_l} q_i.k_l
+// and pass 2 forms Qd = 2^{L} q in shared memory (2^{-L_l} <= 2^60 on the folded path).
+constexpr float FOLD_MIN_LC = -60.f;
+
+struct WyScanMaps {
+  CUtensorMap q, k, v, y;
+  int use_m[4];  // per map: 1 if the lane coordinate is a real dimension
+  int y_tma;     // y written with TMA stores (bf16, 16-byte strides)
+};
+
+GDNX_DEV void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
+                          uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(mbar)
+      : "memory");
+}
+GDNX_DEV void tma_store_5d(const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4, uint32_t src) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4, %5}], [%6];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(src)
+      : "memory");
+}
+GDNX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+GDNX_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+GDNX_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+GDNX_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(mbar)
+               : "memory");
+}
+GDNX_DEV void expect_tx(uint32_t mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
+}
+
+// ------------------------------- pass 1 ------------------------------------
+constexpr int P_NT = 256;
+constexpr int P_OFF_K = 0;                          // [2 kb][128 rows][128 B] bf16 k (2 chunks)
+constexpr int P_OFF_Q = P_OFF_K + 32768;            // same for q
+constexpr int P_OFF_A = P_OFF_Q + 32768;            // fp32 [2][64][LDA]
+constexpr int P_OFF_SC = P_OFF_A + 2 * C * LDA * 4; // L, ce, cw, kn [2][64] each; inv_freq [64]
+constexpr int P_OFF_BAR = P_OFF_SC + (8 * 64 + 64) * 4;
+constexpr int P_SMEM = P_OFF_BAR + 64 + 1024;
+
+struct WyParams {
+  gdnx_scan_args a;
+  int kmd2;
+  int64_t nchunks;
+  __nv_bfloat16* tt;  // [N][nchunks][3][64*64] bf16 (T_e, T_w, Mq^T; swizzled tiles)
+  float* lsum;        // [N][nchunks][64] log2 decay prefix
+  int* err;
+};
+
+// Forward substitution for one 32 x 32 diagonal block of T = (I + A)^{-1}:
+// lane c owns column I0 + c, rows I0..I0+31.  A rows are read as broadcast
+// float4s; four partial sums per row shorten the dependency chain.  The block
+// is written back over A's block (its strictly-lower part is consumed).
+template <int I0>
+GDNX_DEV void subst_block(float* A, int lane) {
+  float x[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float s0 = (i == lane) ? 1.f : 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int l = 0; l < i; l += 4) {
+      const float4 a4 = *reinterpret_cast<const float4*>(A + (I0 + i) * LDA + I0 + l);
+      s0 = fmaf(-a4.x, x[l], s0);
+      if (l + 1 < i) s1 = fmaf(-a4.y, x[l + 1], s1);
+      if (l + 2 < i) s2 = fmaf(-a4.z, x[l + 2], s2);
+      if (l + 3 < i) s3 = fmaf(-a4.w, x[l + 3], s3);
+    }
+    x[i] = (s0 + s1) + (s2 + s3);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) A[(I0 + i) * LDA + I0 + lane] = x[i];
+}
+
+// out[r][lane] = sum_l X[rows r][cols X0 + l] * Y[l][lane] for the 8 rows of
+// this warp, Y's column held in registers (32 x 32 blocks of the 64 x 64 matrix).
+GDNX_DEV void rows8_times_col(const float* A, int r0, int X0, const float* ycol, float* out) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int l = 0; l < 32; l += 4) {
+      const float4 a4 = *reinterpret_cast<const float4*>(A + (r0 + r) * LDA + X0 + l);
+      s0 = fmaf(a4.x, ycol[l], s0);
+      s1 = fmaf(a4.y, ycol[l + 1], s1);
+      s0 = fmaf(a4.z, ycol[l + 2], s0);
+      s1 = fmaf(a4.w, ycol[l + 3], s1);
+    }
+    out[r] = s0 + s1;
+  }
+}
+
+__global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
+  extern __shared__ uint8_t smraw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  char* cK = reinterpret_cast<char*>(sm + P_OFF_K);
+  char* cQ = reinterpret_cast<char*>(sm + P_OFF_Q);
+  float* sA = reinterpret_cast<float*>(sm + P_OFF_A);
+  float* sL = reinterpret_cast<float*>(sm + P_OFF_SC);  // [2][64]
+  float* sCE = sL + 128;                                // ce, later the T_e column factor ce 2^L
+  float* sCW = sL + 256;
+  float* sKN = sL + 384;
+  float* sInv = sL + 512;
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_OFF_BAR);
+  uint64_t* tbar = mbar + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + P_OFF_BAR + 16);
+
+  const gdnx_scan_args& a = P.a;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t npairs = (P.nchunks + 1) / 2;
+  const int64_t n = blockIdx.x / npairs, pair = blockIdx.x % npairs;
+  const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
+  const int lm = (int)m;
+  const int dpairs = (a.rope.enable && lm < 4) ? a.rope.pairs[lm] : 0;
+  const int dch = dpairs / 8;
+  const int64_t tbase = pair * 2 * C;  // first token of the pair
+  const uint32_t sK = tc::smem_u32(cK), sQ = tc::smem_u32(cQ);
+
+  if (tid == 0) {
+    tc::mbar_init(mbar, 1);
+    tc::mbar_init(tbar, 1);
+    // k and q rows of both chunks (TMA zero-fills tokens past T): [kb][rows 0-63 chunk a, 64-127 chunk b]
+    const uint32_t bar = tc::smem_u32(tbar);
+    expect_tx(bar, 8 * 8192);
+    const int ck_m = maps.use_m[1] ? lm : 0, cq_m = maps.use_m[0] ? lm : 0;
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+      for (int ci = 0; ci < 2; ++ci) {
+        tma_load_5d(sK + kb * 16384 + ci * 8192, &maps.k, 64 * kb, ck_m, (int)h, (int)(tbase + ci * C), (int)b, bar);
+        tma_load_5d(sQ + kb * 16384 + ci * 8192, &maps.q, 64 * kb, cq_m, (int)h, (int)(tbase + ci * C), (int)b, bar);
+      }
+  }
+  if (warp == 0) tc::tmem_alloc(s_tmem, 256);
+  if (dpairs > 0 && tid < 64) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[lm]);
+  // warps 0, 1: raw per-token scalars of chunk `warp` (in flight during the TMA wait)
+  uint32_t pr_be[2] = {0, 0}, pr_bw[2] = {0, 0}, pr_dec[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  const bool braided = a.decay_kind == GDNX_DECAY_BRAIDED;
+  if (warp < 2) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int64_t t = tbase + warp * C + lane + 32 * s;
+      if (t < a.T) {
+        pr_be[s] = ld_raw(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m));
+        pr_bw[s] = ld_raw(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m));
+        const int64_t od = view_off(a.decay, b, t, h, m);
+#pragma unroll
+        for (int z = 0; z < 4; ++z)
+          if (z == 0 || braided) pr_dec[s][z] = ld_raw(a.decay.ptr, a.decay.dtype, od + z);
+      }
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *s_tmem;
+  bool ok = tc::mbar_wait(tbar, 0);
+  ok = !__syncthreads_or(!ok);
+
+  // lane RoPE of k and q in place (one set of angles per token) and squared k
+  // norms (16 consecutive lanes per row)
+  if (ok) {
+    const float sc = dpairs > 0 ? a.rope.scale[lm] : 0.f;
+    for (int it = tid; it < 2 * C * 16; it += P_NT) {
+      const int r = it >> 4, cc = it & 15;
+      const bool partner_only = dch > 0 && cc >= dch && cc < 2 * dch;
+      float nrm = 0.f;
+      if (!partner_only) {
+        float x1[8], x2[8];
+        const uint32_t o1 = tc::sw128(r, cc, 128);
+        load8_bf16(cK + o1, 0, x1);
+        if (cc < dch) {
+          float y1[8], y2[8];
+          const uint32_t o2 = tc::sw128(r, cc + dch, 128);
+          load8_bf16(cK + o2, 0, x2);
+          load8_bf16(cQ + o1, 0, y1);
+          load8_bf16(cQ + o2, 0, y2);
+          const float pos = (float)(a.rope.pos0 + tbase + r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float sn, cs;
+            sincos_reduced(pos * sc * sInv[8 * cc + e], &sn, &cs);
+            const float a1 = x1[e] * cs - x2[e] * sn;
+            x2[e] = a1 * sn + x2[e] * cs;
+            x1[e] = a1;
+            const float b1 = y1[e] * cs - y2[e] * sn;
+            y2[e] = b1 * sn + y2[e] * cs;
+            y1[e] = b1;
+          }
+          tc::st_chunk_bf16(cK, o1, x1);
+          tc::st_chunk_bf16(cK, o2, x2);
+          tc::st_chunk_bf16(cQ, o1, y1);
+          tc::st_chunk_bf16(cQ, o2, y2);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) nrm += x2[e] * x2[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) nrm += x1[e] * x1[e];
+      }
+      nrm += __shfl_xor_sync(0xffffffffu, nrm, 8);
+      nrm += __shfl_xor_sync(0xffffffffu, nrm, 4);
+      nrm += __shfl_xor_sync(0xffffffffu, nrm, 2);
+      nrm += __shfl_xor_sync(0xffffffffu, nrm, 1);
+      if (cc == 0) sKN[r] = nrm;
+    }
+  }
+  tc::fence_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  // Gram matrices on the tensor cores: D1 = [Ka;Kb] Ka^T, D2 = [Ka;Kb] Kb^T,
+  // D3 = [Qa;Qb] Ka^T, D4 = [Qa;Qb] Kb^T (N = 128 over [Ka;Kb] per A)
+  if (ok && tid == 0) {
+    tc::fence_after();
+    constexpr uint32_t ID = tc::idesc_bf16(128, 128, false, false);
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      const uint32_t ko = (s >> 2) * 16384 + (s & 3) * 32;
+      const uint64_t dbk = tc::smem_desc(sK + ko, 16, 1024);
+      tc::mma_bf16(tmem, tc::smem_desc(sK + ko, 16, 1024), dbk, ID, s > 0);
+      tc::mma_bf16(tmem + 128, tc::smem_desc(sQ + ko, 16, 1024), dbk, ID, s > 0);
+    }
+    tc::commit(mbar);
+  }
+  // per-token scalars (warp w < 2: chunk w), overlapping the MMAs
+  if (ok && warp < 2) {
+    float lg[2], ce[2], cw[2];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int j = lane + 32 * s;
+      lg[s] = ce[s] = cw[s] = 0.f;
+      if (tbase + warp * C + j < a.T) {
+        float l;
+        if (a.decay_kind == GDNX_DECAY_LOG) {
+          l = raw_f32(pr_dec[s][0], a.decay.dtype);
+          if (!P.kmd2) l = fminf(l, 0.f);
+        } else if (braided) {
+          float acc = 0.f;
+#pragma unroll
+          for (int z = 0; z < 4; ++z)
+            acc += expf(-fminf(softplus_f(raw_f32(pr_dec[s][z], a.decay.dtype)), 5.0f) * a.braid_rates[z]);
+          l = logf(fmaxf(fminf(acc * 0.25f, a.braid_clamp), 1e-30f));
+        } else {
+          float g = raw_f32(pr_dec[s][0], a.decay.dtype);
+          if (!P.kmd2) g = fminf(fmaxf(g, 0.f), 1.f);
+          l = logf(fmaxf(g, 1e-30f));
+        }
+        lg[s] = fmaxf(l, -80.f) * 1.4426950408889634f;  // log2 units
+        const float be = raw_f32(pr_be[s], a.gate_e.dtype), bw = raw_f32(pr_bw[s], a.gate_w.dtype);
+        if (P.kmd2) {
+          ce[s] = be;
+          cw[s] = bw;
+        } else {
+          const float al = stable_alpha(be * sKN[warp * C + j]);
+          ce[s] = al * be;
+          cw[s] = al * bw;
+        }
+      }
+    }
+    float s0 = lg[0], s1 = lg[1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float u0 = __shfl_up_sync(0xffffffffu, s0, o);
+      const float u1 = __shfl_up_sync(0xffffffffu, s1, o);
+      if (lane >= o) { s0 += u0; s1 += u1; }
+    }
+    s1 += __shfl_sync(0xffffffffu, s0, 31);
+    float* L = sL + warp * C;
+    L[lane] = s0;
+    L[lane + 32] = s1;
+    sCE[warp * C + lane] = ce[0];
+    sCE[warp * C + lane + 32] = ce[1];
+    sCW[warp * C + lane] = cw[0];
+    sCW[warp * C + lane + 32] = cw[1];
+  }
+  if (ok) ok = tc::mbar_wait(mbar, 0);
+  ok = !__syncthreads_or(!ok);
+  tc::fence_after();
+  if (ok) {
+    // masks: A[j][l] = ce_j 2^{L_j - L_l} (k_j.k_l) for l < j
+    const int quad = warp & 3, cg = warp >> 2;
+    const int r = quad * 32 + lane, ci = r >> 6, j = r & 63;
+    float d[32];
+    tc::tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(ci * 64 + 32 * cg), d);
+    const float* L = sL + ci * C;
+    const float Lj = L[j], cej = sCE[ci * C + j];
+    const bool fold = L[C - 1] >= FOLD_MIN_LC;
+    float* Arow = sA + (ci * C + j) * LDA + 32 * cg;
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) {
+      float4 o;
+      const int l = 32 * cg + e;
+      o.x = (l + 0 < j) ? cej * exp2f(Lj - L[l + 0]) * d[e + 0] : 0.f;
+      o.y = (l + 1 < j) ? cej * exp2f(Lj - L[l + 1]) * d[e + 1] : 0.f;
+      o.z = (l + 2 < j) ? cej * exp2f(Lj - L[l + 2]) * d[e + 2] : 0.f;
+      o.w = (l + 3 < j) ? cej * exp2f(Lj - L[l + 3]) * d[e + 3] : 0.f;
+      *reinterpret_cast<float4*>(Arow + e) = o;
+    }
+    // Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for l <= i, stored transposed (rows l, 64 i:
+    // the MN-major B operand of y += W^T Mq^T) over the q tile (its MMAs have completed)
+    tc::tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(128 + ci * 64 + 32 * cg), d);
+    char* mqt = cQ + ci * 8192;
+    const uint32_t cb = (uint32_t)(j & 7) * 2;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int l = 32 * cg + e;
+      const float v = (l <= j) ? exp2f(fold ? -L[l] : Lj - L[l]) * d[e] : 0.f;
+      *reinterpret_cast<__nv_bfloat16*>(mqt + tc::sw128(l, j >> 3, C) + cb) = __float2bfloat16_rn(v);
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, 256);
+  }
+  if (!ok) {
+    if (tid == 0 && P.err) atomicExch(P.err, (int)GDNX_ETIMEOUT);
+    return;
+  }
+  // T = (I + A)^{-1} by 32 x 32 blocks: T11, T22 by substitution (warps 0-3),
+  // then R = A21 T11 and T21 = -T22 R (all warps, 8 rows each).
+  if (tid < 2 * C) sCE[tid] *= exp2f(sL[tid]);  // T_e column factor ce_l 2^{L_l}
+  if (warp < 4) {
+    float* A = sA + (warp >> 1) * C * LDA;
+    if (warp & 1) subst_block<32>(A, lane);
+    else subst_block<0>(A, lane);
+  }
+  __syncthreads();
+  float* A = sA + (warp >> 2) * C * LDA;
+  const int r0 = 32 + 8 * (warp & 3);
+  {
+    float col[32], out[8];
+#pragma unroll
+    for (int l = 0; l < 32; ++l) col[l] = A[l * LDA + lane];  // T11[:, lane]
+    rows8_times_col(A, r0, 0, col, out);                      // A21 rows
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < 8; ++r) A[(r0 + r) * LDA + lane] = out[r];  // R over A21
+  }
+  __syncthreads();
+  {
+    float col[32], out[8];
+#pragma unroll
+    for (int l = 0; l < 32; ++l) col[l] = A[(32 + l) * LDA + lane];  // R[:, lane]
+    rows8_times_col(A, r0, 32, col, out);                            // T22 rows
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 8; ++r) A[(r0 + r) * LDA + lane] = -out[r];  // T21
+  }
+  __syncthreads();
+  // T_e = T diag(ce 2^L), T_w = T diag(cw) -> bf16 swizzled tiles over the k tile;
+  // T's upper block T12 is zero
+  for (int it = tid; it < 2 * C * 8; it += P_NT) {
+    const int ci = it >> 9, j = (it >> 3) & 63, c8 = it & 7;
+    float te[8], tw[8];
+    if (c8 >= 4 && j < 32) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) te[e] = tw[e] = 0.f;
+    } else {
+      const float* src = sA + (ci * C + j) * LDA + 8 * c8;
+      const float4 u0 = *reinterpret_cast<const float4*>(src), u1 = *reinterpret_cast<const float4*>(src + 4);
+      const float t8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        te[e] = t8[e] * sCE[ci * C + 8 * c8 + e];
+        tw[e] = t8[e] * sCW[ci * C + 8 * c8 + e];
+      }
+    }
+    const uint32_t off = tc::sw128(j, c8, C);
+    tc::st_chunk_bf16(cK + ci * 16384, off, te);
+    tc::st_chunk_bf16(cK + ci * 16384 + 8192, off, tw);
+  }
+  __syncthreads();
+  // write out: [n][chunk][T_e | T_w | Mq^T] (24 KB per chunk) and L
+  for (int ci = 0; ci < 2; ++ci) {
+    const int64_t chn = pair * 2 + ci;
+    if (chn >= P.nchunks) break;
+    uint4* dst = reinterpret_cast<uint4*>(P.tt + (n * P.nchunks + chn) * TT_ELEMS);
+    const uint4* src = reinterpret_cast<const uint4*>(cK + ci * 16384);
+    const uint4* srcm = reinterpret_cast<const uint4*>(cQ + ci * 8192);
+    for (int it = tid; it < 1024; it += P_NT) dst[it] = src[it];
+    for (int it = tid; it < 512; it += P_NT) dst[1024 + it] = srcm[it];
+    if (tid < 64) P.lsum[(n * P.nchunks + chn) * C + tid] = sL[ci * C + tid];
+  }
+}
+
+// ------------------------------- pass 2 ------------------------------------
+constexpr int S_NT = 512;  // warps 0-7: state group, warps 8-15: prologue / output group
+constexpr int G_NT = 256;  // threads per group
+// Shared memory.  Each stage's q/k tile has 192 rows per 64-wide K block:
+//   stage 0: rows 0-63 k, 64-127 -Wk (G2 B rows [Wk; Q]), 128-191 q
+//   stage 1: rows 0-63 k, 64-127 q,  128-191 -Wk      (G2 B rows [Q; Wk])
+// and Mq^T sits one block-stride before (stage 0) or two after (stage 1) the
+// k rows, so that G3's MN-major B operand [Mq^T | K'] / [K' | Mq^T] is one
+// descriptor with LBO = the block stride.
+constexpr int KB = 24576;                        // K-block stride of a q/k tile
+constexpr int S_OFF_MQ0 = 0;                     // Mq^T stage 0 [64 j][64 i]
+constexpr int S_OFF_WT = 8192;                   // W^T [128 v][64 j]
+constexpr int S_OFF_KQ0 = S_OFF_MQ0 + KB;        // stage 0 tile (2 blocks)
+constexpr int S_OFF_KQ1 = S_OFF_KQ0 + 2 * KB;    // stage 1 tile
+constexpr int S_OFF_MQ1 = S_OFF_KQ1 + 2 * KB;    // Mq^T stage 1
+constexpr int S_OFF_V = S_OFF_MQ1 + 8192;        // 2 stages x [2 vb][64 tokens][128 B]
+constexpr int S_OFF_TT = S_OFF_V + 2 * 16384;    // 2 stages x (T_e 8 KB | T_w 8 KB)
+constexpr int S_OFF_SB = S_OFF_TT + 2 * 16384;   // bf16 state [2 kb][128 v][128 B]
+constexpr int S_OFF_L = S_OFF_SB + 32768;        // 2 stages x L[64]
+constexpr int S_OFF_PSC = S_OFF_L + 512;         // 2 x 2^L, 2 x K' factor: 4 x 64 fp32
+constexpr int S_OFF_SF = S_OFF_PSC + 1024;       // 2 x {2^ls, rescale factor, rescale flag, -}
+constexpr int S_OFF_INV = S_OFF_SF + 32;         // inv_freq[64]
+constexpr int S_OFF_BAR = S_OFF_INV + 256;       // 8 mbarriers, TMEM base, abort flag, final ls
+constexpr int S_SMEM = S_OFF_BAR + 128 + 1024;
+static_assert(S_OFF_MQ1 == S_OFF_KQ1 + 2 * KB, "stage-1 Mq^T position");
+static_assert(S_OFF_KQ0 - KB == S_OFF_MQ0, "stage-0 Mq^T position");
+static_assert(S_SMEM <= 232448, "shared memory");
+constexpr uint32_t STAGE_TX = 6 * 8192 + 3 * 8192 + 256;
+
+// TMEM columns: W^T0 | y0 | state (128) | y1 | W^T1 | Wk^T, so that G2 writes
+// [W^T0 | y0] / [y1 | W^T1] and G3 writes [y0 | S] / [S | y1] with one MMA each.
+constexpr uint32_t T_W0 = 0, T_Y0 = 64, T_S = 128, T_Y1 = 256, T_W1 = 320, T_WK = 384;
+
+GDNX_DEV bool try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait that also gives up when the other group has raised the abort flag.
+GDNX_DEV bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t a = tc::smem_u32(bar);
+  for (uint32_t it = 0; it < (1u << 22); ++it) {
+    if (try_wait(a, parity)) return true;
+    if (*abort_flag) return false;
+  }
+  *abort_flag = 1;
+  return false;
+}
+GDNX_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
+}
+GDNX_DEV void group_sync(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(G_NT) : "memory"); }
+// Group barrier that returns the OR of `v` over the group (the same value in every thread).
+GDNX_DEV bool group_any(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(G_NT)
+      : "memory");
+  return r != 0;
+}
+
+__global__ void __launch_bounds__(S_NT, 1)
+    wy_scan_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
+  extern __shared__ uint8_t smraw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  float* sEL = reinterpret_cast<float*>(sm + S_OFF_PSC);  // [2][64] 2^{L_j}
+  float* sFK = sEL + 128;                                  // [2][64] K' factors
+  float4* sSF = reinterpret_cast<float4*>(sm + S_OFF_SF);
+  float* sInv = reinterpret_cast<float*>(sm + S_OFF_INV);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S_OFF_BAR);
+  uint64_t* full = bars;       // [2] stage loaded (TMA + bulk, tx-counted)
+  uint64_t* g1 = bars + 2;     // G1 complete (prologue group's MMAs)
+  uint64_t* g2 = bars + 3;     // G2 complete
+  uint64_t* g3 = bars + 4;     // [2] G3 complete (per stage / y buffer)
+  uint64_t* ready = bars + 6;  // [2] prologue of the chunk done (operands in place)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + S_OFF_BAR + 68);
+  float* s_lsfin = reinterpret_cast<float*>(sm + S_OFF_BAR + 72);
+
+  const gdnx_scan_args& a = P.a;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3;
+  const int row = quad * 32 + lane;
+  const uint32_t lbase = (uint32_t)(quad * 32) << 16;
+  const int64_t n = blockIdx.x;
+  const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
+  const int lm = (int)m;
+  const int dpairs = (a.rope.enable && lm < 4) ? a.rope.pairs[lm] : 0;
+  const int dch = dpairs / 8;
+  const float rsc = dpairs > 0 ? a.rope.scale[lm] : 0.f;
+  const int64_t nchunks = P.nchunks;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const uint32_t sV = sbase + S_OFF_V, sTT = sbase + S_OFF_TT, sSB = sbase + S_OFF_SB;
+  const uint32_t sWT = sbase + S_OFF_WT, sLst = sbase + S_OFF_L;
+  const __nv_bfloat16* ttg = P.tt + n * nchunks * TT_ELEMS;
+  const float* lsg = P.lsum + n * nchunks * C;
+  // per-stage geometry (rows within a 192-row K block)
+  auto kq_off = [](int s) { return s ? S_OFF_KQ1 : S_OFF_KQ0; };
+  auto q_row = [](int s) { return s ? 64 : 128; };
+  auto wk_row = [](int s) { return s ? 128 : 64; };
+  auto mq_off = [](int s) { return s ? S_OFF_MQ1 : S_OFF_MQ0; };
+
+  if (warp == 0) tc::tmem_alloc(s_tmem, 512);
+  if (tid == 0) {
+    for (int i = 0; i < 8; ++i) tc::mbar_init(bars + i, 1);
+    *s_abort = 0;
+    *s_lsfin = 0.f;
+  }
+  if (dpairs > 0 && tid < 64) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[lm]);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  // TMA coordinates: {x (dim), lane, head, token, batch}
+  const int cq_m = maps.use_m[0] ? lm : 0, ck_m = maps.use_m[1] ? lm : 0, cv_m = maps.use_m[2] ? lm : 0;
+  auto issue_stage = [&](int64_t chn) {  // one thread
+    const int s = (int)(chn & 1);
+    const uint32_t bar = tc::smem_u32(full + s);
+    const int t0 = (int)(chn * C);
+    tc::fence_async_smem();
+    expect_tx(bar, STAGE_TX);
+    const uint32_t kq = sbase + kq_off(s);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+      tma_load_5d(kq + kb * KB, &maps.k, 64 * kb, ck_m, (int)h, t0, (int)b, bar);
+      tma_load_5d(kq + kb * KB + q_row(s) * 128, &maps.q, 64 * kb, cq_m, (int)h, t0, (int)b, bar);
+      tma_load_5d(sV + s * 16384 + kb * 8192, &maps.v, 64 * kb, cv_m, (int)h, t0, (int)b, bar);
+    }
+    bulk_load(sTT + s * 16384, ttg + chn * TT_ELEMS, 16384, bar);
+    bulk_load(sbase + mq_off(s), ttg + chn * TT_ELEMS + 2 * C * C, 8192, bar);
+    bulk_load(sLst + s * 256, lsg + chn * C, 256, bar);
+  };
+  if (tid == 0) {
+    issue_stage(0);
+    if (nchunks > 1) issue_stage(1);
+  }
+
+  // initial state into TMEM (all 16 warps, 32 columns each)
+  {
+    float vals[32];
+    const int col = 32 * (warp >> 2);
+    if (a.state_in) {
+      const float* src = a.state_in + (n * VD + row) * KD + col;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(src + e);
+        vals[e] = f.x; vals[e + 1] = f.y; vals[e + 2] = f.z; vals[e + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) vals[e] = 0.f;
+    }
+    tc::tmem_st32(tmem + T_S + lbase + col, vals);
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+
+  constexpr uint32_t ID_MN_K = tc::idesc_bf16(128, 64, true, false);
+  constexpr uint32_t ID_G2 = tc::idesc_bf16(128, 128, false, false);
+  constexpr uint32_t ID_G3 = tc::idesc_bf16(128, 192, false, true);
+
+  if (warp < 8) {
+    // ======================= state group: S0 -> G2 -> W -> G3 =======================
+    const int half = warp >> 2;
+    for (int64_t ch = 0; ch < nchunks; ++ch) {
+      const int s = (int)(ch & 1);
+      bool ok = wait_or_abort(ready + s, (uint32_t)((ch >> 1) & 1), s_abort);
+      if (group_any(2, !ok)) break;
+      // state -> bf16 operand (true scale); rescale TMEM when due
+      {
+        const float4 sf = sSF[s];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int col = 64 * half + 32 * hh;
+          float vals[32], o[8];
+          tc::tmem_ld32(tmem + T_S + lbase + col, vals);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = vals[8 * q4 + e] * sf.x;
+            tc::st_chunk_bf16(reinterpret_cast<char*>(sm + S_OFF_SB), tc::sw128(row, col / 8 + q4, 128), o);
+          }
+          if (sf.z != 0.f) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) vals[e] *= sf.y;
+            tc::tmem_st32(tmem + T_S + lbase + col, vals);
+          }
+        }
+      }
+      tc::fence_async_smem();
+      tc::fence_before();
+      if (group_any(2, *s_abort != 0)) break;
+      // G2: [W^T | y] += S0 [-Wk; Qd]^T  (W^T holds V^T T_w^T from G1, y was zeroed)
+      const uint32_t kq = sbase + kq_off(s);
+      if (tid == 0) {
+        tc::fence_after();
+        const uint32_t d = tmem + (s ? T_Y1 : T_W0);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t ko = (k >> 2) * KB + (k & 3) * 32;
+          tc::mma_bf16(d, tc::smem_desc(sSB + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                       tc::smem_desc(kq + ko + 64 * 128, 16, 1024), ID_G2, 1);
+        }
+        tc::commit(g2);
+      }
+      // while G2 runs: K' = diag(f) K in place (rows 0-63; G1 has consumed K)
+      {
+        char* kqp = reinterpret_cast<char*>(sm + kq_off(s));
+        const float* f = sFK + 64 * s;
+        for (int it = tid; it < C * 16; it += G_NT) {
+          const int r = it >> 4, cc = it & 15;
+          const uint32_t off = tc::sw128(r, cc, 192);
+          float x[8];
+          load8_bf16(kqp + off, 0, x);
+          const float fr = f[r];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] *= fr;
+          tc::st_chunk_bf16(kqp, off, x);
+        }
+      }
+      tc::fence_async_smem();
+      ok = wait_or_abort(g2, (uint32_t)(ch & 1), s_abort);
+      tc::fence_after();
+      if (group_any(2, !ok)) break;
+      // W^T -> bf16 A operand
+      {
+        float w[32];
+        tc::tmem_ld32(tmem + (s ? T_W1 : T_W0) + lbase + 32 * half, w);
+        char* wt = reinterpret_cast<char*>(sm + S_OFF_WT);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(wt, tc::sw128(row, 4 * half + q4, 128), w + 8 * q4);
+      }
+      tc::fence_async_smem();
+      tc::fence_before();
+      if (group_any(2, *s_abort != 0)) break;
+      // G3: [y | S] or [S | y] += W^T [Mq^T | K'] / [K' | Mq^T]   (B MN-major)
+      if (tid == 0) {
+        tc::fence_after();
+        const uint32_t d = tmem + (s ? T_S : T_Y0);
+        const uint32_t bb = s ? kq : sbase + S_OFF_MQ0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(d, tc::smem_desc(sWT + k * 32, 16, 1024), tc::smem_desc(bb + k * 2048, KB, 1024), ID_G3, 1);
+        tc::commit(g3 + s);
+      }
+      ok = wait_or_abort(g3 + s, (uint32_t)((ch >> 1) & 1), s_abort);
+      tc::fence_after();
+      // stage s is consumed: fetch chunk ch + 2 into it
+      if (tid == 0 && ok && ch + 2 < nchunks) issue_stage(ch + 2);
+      if (group_any(2, !ok)) break;
+    }
+  } else {
+    // ========== prologue / output group: RoPE, G1, -Wk, Qd, y zero, y out ==========
+    const int ptid = tid - G_NT, half = (warp - 8) >> 2;
+    const int64_t ybase = b * a.y_sb + h * a.y_sh + m * a.y_sm;
+    float ls = 0.f;  // state = 2^ls * S_tmem at the start of the chunk being prepared
+    const int cy_m = maps.use_m[3] ? lm : 0;
+    // y of chunk `c` (its G3 complete) -> global.  With TMA: staged as two
+    // swizzled [64 tokens][64 v] boxes in the -Wk rows of the chunk's stage (G2 has
+    // consumed them; the next writer waits for the stores' reads).
+    auto y_out = [&](int64_t c) -> bool {
+      const int sp = (int)(c & 1);
+      const bool ok = wait_or_abort(g3 + sp, (uint32_t)((c >> 1) & 1), s_abort);
+      tc::fence_after();
+      if (group_any(1, !ok)) return false;
+      float yv[32];
+      tc::tmem_ld32(tmem + (sp ? T_Y1 : T_Y0) + lbase + 32 * half, yv);
+      if (sSF[sp].w != 0.f) {  // folded chunk: y_i = 2^{L_i} (S0 q_i + sum_l Mq'_il W_l)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) yv[e] *= sEL[64 * sp + 32 * half + e];
+      }
+      if (maps.y_tma) {
+        char* stg = reinterpret_cast<char*>(sm + kq_off(sp) + wk_row(sp) * 128 + (row >> 6) * KB);
+        const int vv = row & 63;
+        const uint32_t cb = (uint32_t)(vv & 7) * 2;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int i = 32 * half + e;
+          *reinterpret_cast<__nv_bfloat16*>(stg + i * 128 + (((vv >> 3) ^ (i & 7)) << 4) + cb) =
+              __float2bfloat16_rn(yv[e]);
+        }
+        tc::fence_async_smem();
+        group_sync(1);
+        if (ptid == 0) {
+          const uint32_t src = sbase + kq_off(sp) + wk_row(sp) * 128;
+          tma_store_5d(&maps.y, 0, cy_m, (int)h, (int)(c * C), (int)b, src);
+          tma_store_5d(&maps.y, 64, cy_m, (int)h, (int)(c * C), (int)b, src + KB);
+          bulk_commit();
+        }
+      } else {
+        const int nt = (int)((a.T - c * C) < C ? (a.T - c * C) : C);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int i = 32 * half + e;
+          if (i < nt) st_from_f32(a.y, a.y_dtype, ybase + row + (c * C + i) * a.y_st, yv[e]);
+        }
+      }
+      return true;
+    };
+    bool alive = true;
+    for (int64_t ch = 0; ch < nchunks; ++ch) {
+      const int s = (int)(ch & 1);
+      const int64_t t0 = ch * C;
+      char* kq = reinterpret_cast<char*>(sm + kq_off(s));
+      const int qr = q_row(s), wr = wk_row(s);
+      bool ok = wait_or_abort(full + s, (uint32_t)((ch >> 1) & 1), s_abort);
+      if (group_any(1, !ok)) { alive = false; break; }
+      const float* Lst = reinterpret_cast<const float*>(sm + S_OFF_L + s * 256);
+      const float Lc = Lst[C - 1];
+      const bool rescale = ls + Lc < -40.f;
+      const bool fold = Lc >= FOLD_MIN_LC;
+      if (ptid < 64) {  // K' = f K (the S update's operand); 2^L for Qd or for y
+        const float Lj = Lst[ptid];
+        sEL[64 * s + ptid] = exp2f(Lj);
+        sFK[64 * s + ptid] = rescale ? exp2f(Lc - Lj) : exp2f(-Lj - ls);
+      }
+      if (ptid == 0) sSF[s] = make_float4(exp2f(ls), exp2f(ls + Lc), rescale ? 1.f : 0.f, fold ? 1.f : 0.f);
+      ls = rescale ? 0.f : ls + Lc;
+      // lane RoPE of token j's k (row j) and q (row qr + j) in place, one set of angles
+      for (int it = ptid; it < C * dch; it += G_NT) {
+        const int j = it / dch, cc = it - j * dch;
+        float k1[8], k2[8], q1[8], q2[8];
+        const uint32_t o1 = tc::sw128(j, cc, 192), o2 = tc::sw128(j, cc + dch, 192);
+        const uint32_t p1 = tc::sw128(qr + j, cc, 192), p2 = tc::sw128(qr + j, cc + dch, 192);
+        load8_bf16(kq + o1, 0, k1);
+        load8_bf16(kq + o2, 0, k2);
+        load8_bf16(kq + p1, 0, q1);
+        load8_bf16(kq + p2, 0, q2);
+        const float pos = (float)(a.rope.pos0 + t0 + j);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float sn, cs;
+          sincos_reduced(pos * rsc * sInv[8 * cc + e], &sn, &cs);
+          const float a1 = k1[e] * cs - k2[e] * sn;
+          k2[e] = a1 * sn + k2[e] * cs;
+          k1[e] = a1;
+          const float b1 = q1[e] * cs - q2[e] * sn;
+          q2[e] = b1 * sn + q2[e] * cs;
+          q1[e] = b1;
+        }
+        tc::st_chunk_bf16(kq, o1, k1);
+        tc::st_chunk_bf16(kq, o2, k2);
+        tc::st_chunk_bf16(kq, p1, q1);
+        tc::st_chunk_bf16(kq, p2, q2);
+      }
+      tc::fence_async_smem();
+      tc::fence_before();
+      group_sync(1);
+      // G1 (state-independent): Wk^T = K^T T_e^T, W^T = V^T T_w^T
+      const uint32_t skq = sbase + kq_off(s), stt = sTT + s * 16384, sv = sV + s * 16384;
+      if (ptid == 0) {
+        tc::fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(tmem + T_WK, tc::smem_desc(skq + k * 2048, KB, 1024), tc::smem_desc(stt + k * 32, 16, 1024),
+                       ID_MN_K, k > 0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(tmem + (s ? T_W1 : T_W0), tc::smem_desc(sv + k * 2048, 8192, 1024),
+                       tc::smem_desc(stt + 8192 + k * 32, 16, 1024), ID_MN_K, k > 0);
+        tc::commit(g1);
+      }
+      // while G1 runs: y buffer of this stage to zero (its chunk two back is written out)
+      {
+        float z[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) z[e] = 0.f;
+        tc::tmem_st32(tmem + (s ? T_Y1 : T_Y0) + lbase + 32 * half, z);
+      }
+      ok = wait_or_abort(g1, (uint32_t)(ch & 1), s_abort);
+      tc::fence_after();
+      if (ptid == 0) bulk_wait_read();  // y stores of chunk ch - 2 have read the -Wk rows
+      if (group_any(1, !ok)) { alive = false; break; }
+      if (!fold) {  // exact path: Qd = 2^{L_i} q_i in place
+        for (int it = ptid; it < C * 16; it += G_NT) {
+          const int r = it >> 4, cc = it & 15;
+          const uint32_t off = tc::sw128(qr + r, cc, 192);
+          float x[8];
+          load8_bf16(kq + off, 0, x);
+          const float f = sEL[64 * s + r];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] *= f;
+          tc::st_chunk_bf16(kq, off, x);
+        }
+      }
+      // -Wk as rows of the G2 B operand (K-major [j][k]): this thread holds Wk^T[k = row][j]
+      {
+        float d[32];
+        tc::tmem_ld32(tmem + T_WK + lbase + 32 * half, d);
+        char* base = kq + (row >> 6) * KB;
+        const int kk = row & 63;
+        const uint32_t cb = (uint32_t)(kk & 7) * 2;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = 32 * half + e;
+          *reinterpret_cast<__nv_bfloat16*>(base + (wr + j) * 128 + (((kk >> 3) ^ ((wr + j) & 7)) << 4) + cb) =
+              __float2bfloat16_rn(-d[e]);
+        }
+      }
+      tc::fence_async_smem();
+      tc::fence_before();
+      group_sync(1);
+      if (ptid == 0) mbar_arrive(ready + s);
+      // outputs of the previous chunk (its G3 overlaps this chunk's prologue)
+      if (ch > 0 && !y_out(ch - 1)) { alive = false; break; }
+    }
+    if (alive && nchunks > 0) y_out(nchunks - 1);
+    if (ptid == 0) {
+      *s_lsfin = ls;
+      bulk_wait_all();
+    }
+  }
+
+  __syncthreads();
+  tc::fence_after();
+  const bool aborted = *s_abort != 0;
+  if (!aborted && a.state_out) {
+    float vals[32];
+    const int col = 32 * (warp >> 2);
+    tc::tmem_ld32(tmem + T_S + lbase + col, vals);
+    const float f = exp2f(*s_lsfin);
+    float* dst = a.state_out + (n * VD + row) * KD + col;
+#pragma unroll
+    for (int e = 0; e < 32; e += 4)
+      *reinterpret_cast<float4*>(dst + e) = make_float4(vals[e] * f, vals[e + 1] * f, vals[e + 2] * f, vals[e + 3] * f);
+  }
+  if (aborted && tid == 0) {
+    if (P.err) atomicExch(P.err, (int)GDNX_ETIMEOUT);
+    // let loads still in flight land before the CTA's shared memory is released
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_wait(full + s, 0, 1u << 16);
+      tc::mbar_wait(full + s, 1, 1u << 16);
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------- host side ----------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+std::mutex g_encode_mu;
+EncodeTiledFn g_encode = nullptr;
+
+EncodeTiledFn encode_fn() {
+  std::lock_guard<std::mutex> lk(g_encode_mu);
+  if (!g_encode) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<EncodeTiledFn>(f);
+    else
+      cudaGetLastError();
+  }
+  return g_encode;
+}
+
+// 5-D map {dim, lane, head, token, batch} over a [B,T,H,M,128] bf16 view, box
+// {64, 1, 1, 64, 1}, 128-byte swizzle.  A lane stride of 0 (shared q/k/v) or a
+// single lane drops the lane coordinate (size 1).
+bool make_map(const gdnx_view& v, const gdnx_scan_args& a, CUtensorMap* map, int* use_m) {
+  if (v.dtype != GDNX_BF16 || (reinterpret_cast<uintptr_t>(v.ptr) & 15)) return false;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  *use_m = (v.sm != 0 && a.M > 1) ? 1 : 0;
+  const cuuint64_t kb = 2;  // bytes per element
+  cuuint64_t dims[5] = {(cuuint64_t)KD, (cuuint64_t)(*use_m ? a.M : 1), (cuuint64_t)a.H, (cuuint64_t)a.T,
+                        (cuuint64_t)a.B};
+  cuuint64_t strides[4] = {(cuuint64_t)(*use_m ? v.sm : KD) * kb, (cuuint64_t)v.sh * kb, (cuuint64_t)v.st * kb,
+                           (cuuint64_t)v.sb * kb};
+  // size-1 dimensions may carry any stride; give them a valid one
+  if (a.H == 1) strides[1] = strides[0];
+  if (a.T == 1) strides[2] = strides[1];
+  if (a.B == 1) strides[3] = strides[2];
+  for (int i = 0; i < 4; ++i)
+    if (strides[i] == 0 || strides[i] % 16 || strides[i] >= (1ull << 40)) return false;
+  cuuint32_t box[5] = {64, 1, 1, (cuuint32_t)C, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(v.ptr), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t wy_workspace_bytes(const gdnx_scan_args& a) {
+  const int64_t N = a.B * a.H * a.M, nch = (a.T + C - 1) / C;
+  return ERR_BYTES + (size_t)N * nch * (TT_ELEMS * 2 + C * 4);
+}
+
+gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st) {
+  WyScanMaps maps;
+  if (!make_map(a.q, a, &maps.q, &maps.use_m[0]) || !make_map(a.k, a, &maps.k, &maps.use_m[1]) ||
+      !make_map(a.v, a, &maps.v, &maps.use_m[2]))
+    return GDNX_EUNSUPPORTED;
+  gdnx_view yv;
+  yv.ptr = a.y;
+  yv.dtype = a.y_dtype;
+  yv.dim = VD;
+  yv.sb = a.y_sb;
+  yv.st = a.y_st;
+  yv.sh = a.y_sh;
+  yv.sm = a.y_sm;
+  yv.ss = 0;
+  maps.y_tma = make_map(yv, a, &maps.y, &maps.use_m[3]) ? 1 : 0;
+  const int64_t N = a.B * a.H * a.M, nch = (a.T + C - 1) / C;
+  WyParams P;
+  P.a = a;
+  P.kmd2 = a.mode == GDNX_MODE_KMD2;
+  P.nchunks = nch;
+  char* ws = reinterpret_cast<char*>(a.workspace);
+  P.err = reinterpret_cast<int*>(ws);
+  P.tt = reinterpret_cast<__nv_bfloat16*>(ws + ERR_BYTES);
+  P.lsum = reinterpret_cast<float*>(ws + ERR_BYTES + (size_t)N * nch * TT_ELEMS * 2);
+  if (cudaMemsetAsync(ws, 0, ERR_BYTES, st) != cudaSuccess) return GDNX_ELAUNCH;
+  if (cudaFuncSetAttribute(wy_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM) != cudaSuccess ||
+      cudaFuncSetAttribute(wy_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess ||
+      cudaFuncSetAttribute(wy_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_SMEM) != cudaSuccess)
+    return GDNX_ELAUNCH;
+  const int64_t npairs = (nch + 1) / 2;
+  wy_prep_kernel<<<(unsigned)(N * npairs), P_NT, P_SMEM, st>>>(P, maps);
+  wy_scan_kernel<<<(unsigned)N, S_NT, S_SMEM, st>>>(P, maps);
+  return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+}
+
+}  // namespace gdnx
