@@ -41,5 +41,14 @@ GDNX_DEV void sincos_reduced(float x, float* s, float* c) {
   __sincosf(r, s, c);
 }
 
+// 2^x with the hardware base-2 exponential (ex2.approx.ftz: relative error about
+// 2^-22, subnormal results flushed to zero); used where a decay factor feeds a
+// bf16 operand or an fp32 accumulation with looser tolerance than that.
+GDNX_DEV float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 }  // namespace chunk
 }  // namespace gdnx

@@ -92,10 +92,11 @@ GDNX_DEV void expect_tx(uint32_t mbar, uint32_t bytes) {
 constexpr int P_NT = 256;
 constexpr int P_OFF_K = 0;                          // [2 kb][128 rows][128 B] bf16 k (2 chunks)
 constexpr int P_OFF_Q = P_OFF_K + 32768;            // same for q
-constexpr int P_OFF_A = P_OFF_Q + 32768;            // fp32 [2][64][LDA]
-constexpr int P_OFF_SC = P_OFF_A + 2 * C * LDA * 4; // L, ce, cw, kn [2][64] each; inv_freq [64]
-constexpr int P_OFF_BAR = P_OFF_SC + (8 * 64 + 64) * 4;
+constexpr int P_OFF_A = 0;                          // fp32 [2][64][LDA] over k, q after the MMAs
+constexpr int P_OFF_SC = P_OFF_Q + 32768;           // L, ce, cw, kn, 2^-L [2][64] each; inv_freq [64]
+constexpr int P_OFF_BAR = P_OFF_SC + (10 * 64 + 64) * 4;
 constexpr int P_SMEM = P_OFF_BAR + 64 + 1024;
+static_assert(2 * C * LDA * 4 <= 65536, "A over the k/q tiles");
 
 struct WyParams {
   gdnx_scan_args a;
@@ -149,17 +150,18 @@ GDNX_DEV void rows8_times_col(const float* A, int r0, int X0, const float* ycol,
   }
 }
 
-__global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
+__global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
   extern __shared__ uint8_t smraw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   char* cK = reinterpret_cast<char*>(sm + P_OFF_K);
   char* cQ = reinterpret_cast<char*>(sm + P_OFF_Q);
   float* sA = reinterpret_cast<float*>(sm + P_OFF_A);
-  float* sL = reinterpret_cast<float*>(sm + P_OFF_SC);  // [2][64]
-  float* sCE = sL + 128;                                // ce, later the T_e column factor ce 2^L
+  float* sL = reinterpret_cast<float*>(sm + P_OFF_SC);  // [2][64] log2 decay prefix
+  float* sCE = sL + 128;                                // ce_l, then the T_e factor ce_l 2^{L_l}
   float* sCW = sL + 256;
-  float* sKN = sL + 384;
+  float* sKN = sL + 384;  // |k|^2
   float* sInv = sL + 512;
+  float* sNE = sL + 576;  // [2][64] 2^{-L_l}
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_OFF_BAR);
   uint64_t* tbar = mbar + 1;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(sm + P_OFF_BAR + 16);
@@ -174,6 +176,7 @@ __global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const _
   const int dch = dpairs / 8;
   const int64_t tbase = pair * 2 * C;  // first token of the pair
   const uint32_t sK = tc::smem_u32(cK), sQ = tc::smem_u32(cQ);
+  const bool braided = a.decay_kind == GDNX_DECAY_BRAIDED;
 
   if (tid == 0) {
     tc::mbar_init(mbar, 1);
@@ -192,22 +195,54 @@ __global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const _
   }
   if (warp == 0) tc::tmem_alloc(s_tmem, 256);
   if (dpairs > 0 && tid < 64) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[lm]);
-  // warps 0, 1: raw per-token scalars of chunk `warp` (in flight during the TMA wait)
-  uint32_t pr_be[2] = {0, 0}, pr_bw[2] = {0, 0}, pr_dec[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-  const bool braided = a.decay_kind == GDNX_DECAY_BRAIDED;
+  // warps 0, 1: log2 decay prefix of chunk `warp` (independent of k)
   if (warp < 2) {
+    float lg[2];
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       const int64_t t = tbase + warp * C + lane + 32 * s;
+      lg[s] = 0.f;
       if (t < a.T) {
-        pr_be[s] = ld_raw(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m));
-        pr_bw[s] = ld_raw(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m));
         const int64_t od = view_off(a.decay, b, t, h, m);
+        float l;
+        if (a.decay_kind == GDNX_DECAY_LOG) {
+          l = ld_as_f32(a.decay.ptr, a.decay.dtype, od);
+          if (!P.kmd2) l = fminf(l, 0.f);
+        } else if (braided) {
+          float acc = 0.f;
 #pragma unroll
-        for (int z = 0; z < 4; ++z)
-          if (z == 0 || braided) pr_dec[s][z] = ld_raw(a.decay.ptr, a.decay.dtype, od + z);
+          for (int z = 0; z < 4; ++z)
+            acc += expf(-fminf(softplus_f(ld_as_f32(a.decay.ptr, a.decay.dtype, od + z)), 5.0f) * a.braid_rates[z]);
+          l = logf(fmaxf(fminf(acc * 0.25f, a.braid_clamp), 1e-30f));
+        } else {
+          float g = ld_as_f32(a.decay.ptr, a.decay.dtype, od);
+          if (!P.kmd2) g = fminf(fmaxf(g, 0.f), 1.f);
+          l = logf(fmaxf(g, 1e-30f));
+        }
+        lg[s] = fmaxf(l, -80.f) * 1.4426950408889634f;  // log2 units
       }
     }
+    float s0 = lg[0], s1 = lg[1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float u0 = __shfl_up_sync(0xffffffffu, s0, o);
+      const float u1 = __shfl_up_sync(0xffffffffu, s1, o);
+      if (lane >= o) { s0 += u0; s1 += u1; }
+    }
+    s1 += __shfl_sync(0xffffffffu, s0, 31);
+    sL[warp * C + lane] = s0;
+    sL[warp * C + lane + 32] = s1;
+    sNE[warp * C + lane] = fast_exp2(-s0);
+    sNE[warp * C + lane + 32] = fast_exp2(-s1);
+  }
+  // this thread's token (row of the masks): raw gates, in flight during the TMA wait
+  const int quad = warp & 3, cg = warp >> 2;
+  const int r = quad * 32 + lane, ci = r >> 6, j = r & 63;
+  const int64_t tj = tbase + r;
+  float be = 0.f, bw = 0.f;
+  if (tj < a.T) {
+    be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tj, h, m));
+    bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tj, h, m));
   }
   tc::fence_before();
   __syncthreads();
@@ -216,58 +251,39 @@ __global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const _
   bool ok = tc::mbar_wait(tbar, 0);
   ok = !__syncthreads_or(!ok);
 
-  // lane RoPE of k and q in place (one set of angles per token) and squared k
-  // norms (16 consecutive lanes per row)
+  // lane RoPE of k and q in place (rotated chunk pairs only; one set of angles per token)
   if (ok) {
     const float sc = dpairs > 0 ? a.rope.scale[lm] : 0.f;
-    for (int it = tid; it < 2 * C * 16; it += P_NT) {
-      const int r = it >> 4, cc = it & 15;
-      const bool partner_only = dch > 0 && cc >= dch && cc < 2 * dch;
-      float nrm = 0.f;
-      if (!partner_only) {
-        float x1[8], x2[8];
-        const uint32_t o1 = tc::sw128(r, cc, 128);
-        load8_bf16(cK + o1, 0, x1);
-        if (cc < dch) {
-          float y1[8], y2[8];
-          const uint32_t o2 = tc::sw128(r, cc + dch, 128);
-          load8_bf16(cK + o2, 0, x2);
-          load8_bf16(cQ + o1, 0, y1);
-          load8_bf16(cQ + o2, 0, y2);
-          const float pos = (float)(a.rope.pos0 + tbase + r);
+    for (int it = tid; it < 2 * C * dch; it += P_NT) {
+      const int rr = it / dch, cc = it - rr * dch;
+      float x1[8], x2[8], y1[8], y2[8];
+      const uint32_t o1 = tc::sw128(rr, cc, 128), o2 = tc::sw128(rr, cc + dch, 128);
+      load8_bf16(cK + o1, 0, x1);
+      load8_bf16(cK + o2, 0, x2);
+      load8_bf16(cQ + o1, 0, y1);
+      load8_bf16(cQ + o2, 0, y2);
+      const float pos = (float)(a.rope.pos0 + tbase + rr);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float sn, cs;
-            sincos_reduced(pos * sc * sInv[8 * cc + e], &sn, &cs);
-            const float a1 = x1[e] * cs - x2[e] * sn;
-            x2[e] = a1 * sn + x2[e] * cs;
-            x1[e] = a1;
-            const float b1 = y1[e] * cs - y2[e] * sn;
-            y2[e] = b1 * sn + y2[e] * cs;
-            y1[e] = b1;
-          }
-          tc::st_chunk_bf16(cK, o1, x1);
-          tc::st_chunk_bf16(cK, o2, x2);
-          tc::st_chunk_bf16(cQ, o1, y1);
-          tc::st_chunk_bf16(cQ, o2, y2);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) nrm += x2[e] * x2[e];
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) nrm += x1[e] * x1[e];
+      for (int e = 0; e < 8; ++e) {
+        float sn, cs;
+        sincos_reduced(pos * sc * sInv[8 * cc + e], &sn, &cs);
+        const float a1 = x1[e] * cs - x2[e] * sn;
+        x2[e] = a1 * sn + x2[e] * cs;
+        x1[e] = a1;
+        const float b1 = y1[e] * cs - y2[e] * sn;
+        y2[e] = b1 * sn + y2[e] * cs;
+        y1[e] = b1;
       }
-      nrm += __shfl_xor_sync(0xffffffffu, nrm, 8);
-      nrm += __shfl_xor_sync(0xffffffffu, nrm, 4);
-      nrm += __shfl_xor_sync(0xffffffffu, nrm, 2);
-      nrm += __shfl_xor_sync(0xffffffffu, nrm, 1);
-      if (cc == 0) sKN[r] = nrm;
+      tc::st_chunk_bf16(cK, o1, x1);
+      tc::st_chunk_bf16(cK, o2, x2);
+      tc::st_chunk_bf16(cQ, o1, y1);
+      tc::st_chunk_bf16(cQ, o2, y2);
     }
   }
   tc::fence_async_smem();
   tc::fence_before();
   __syncthreads();
-  // Gram matrices on the tensor cores: D1 = [Ka;Kb] Ka^T, D2 = [Ka;Kb] Kb^T,
-  // D3 = [Qa;Qb] Ka^T, D4 = [Qa;Qb] Kb^T (N = 128 over [Ka;Kb] per A)
+  // Gram matrices on the tensor cores: [Ka;Kb] [Ka;Kb]^T and [Qa;Qb] [Ka;Kb]^T (N = 128)
   if (ok && tid == 0) {
     tc::fence_after();
     constexpr uint32_t ID = tc::idesc_bf16(128, 128, false, false);
@@ -280,90 +296,65 @@ __global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const _
     }
     tc::commit(mbar);
   }
-  // per-token scalars (warp w < 2: chunk w), overlapping the MMAs
-  if (ok && warp < 2) {
-    float lg[2], ce[2], cw[2];
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      const int j = lane + 32 * s;
-      lg[s] = ce[s] = cw[s] = 0.f;
-      if (tbase + warp * C + j < a.T) {
-        float l;
-        if (a.decay_kind == GDNX_DECAY_LOG) {
-          l = raw_f32(pr_dec[s][0], a.decay.dtype);
-          if (!P.kmd2) l = fminf(l, 0.f);
-        } else if (braided) {
-          float acc = 0.f;
-#pragma unroll
-          for (int z = 0; z < 4; ++z)
-            acc += expf(-fminf(softplus_f(raw_f32(pr_dec[s][z], a.decay.dtype)), 5.0f) * a.braid_rates[z]);
-          l = logf(fmaxf(fminf(acc * 0.25f, a.braid_clamp), 1e-30f));
-        } else {
-          float g = raw_f32(pr_dec[s][0], a.decay.dtype);
-          if (!P.kmd2) g = fminf(fmaxf(g, 0.f), 1.f);
-          l = logf(fmaxf(g, 1e-30f));
-        }
-        lg[s] = fmaxf(l, -80.f) * 1.4426950408889634f;  // log2 units
-        const float be = raw_f32(pr_be[s], a.gate_e.dtype), bw = raw_f32(pr_bw[s], a.gate_w.dtype);
-        if (P.kmd2) {
-          ce[s] = be;
-          cw[s] = bw;
-        } else {
-          const float al = stable_alpha(be * sKN[warp * C + j]);
-          ce[s] = al * be;
-          cw[s] = al * bw;
-        }
-      }
-    }
-    float s0 = lg[0], s1 = lg[1];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float u0 = __shfl_up_sync(0xffffffffu, s0, o);
-      const float u1 = __shfl_up_sync(0xffffffffu, s1, o);
-      if (lane >= o) { s0 += u0; s1 += u1; }
-    }
-    s1 += __shfl_sync(0xffffffffu, s0, 31);
-    float* L = sL + warp * C;
-    L[lane] = s0;
-    L[lane + 32] = s1;
-    sCE[warp * C + lane] = ce[0];
-    sCE[warp * C + lane + 32] = ce[1];
-    sCW[warp * C + lane] = cw[0];
-    sCW[warp * C + lane + 32] = cw[1];
-  }
   if (ok) ok = tc::mbar_wait(mbar, 0);
   ok = !__syncthreads_or(!ok);
   tc::fence_after();
+  // this thread: row r of [Ka;Kb] K^T, columns 32 cg .. 32 cg + 31 of its chunk's block
+  float d[32];
+  const uint32_t lrow = (uint32_t)(quad * 32) << 16;
   if (ok) {
-    // masks: A[j][l] = ce_j 2^{L_j - L_l} (k_j.k_l) for l < j
-    const int quad = warp & 3, cg = warp >> 2;
-    const int r = quad * 32 + lane, ci = r >> 6, j = r & 63;
-    float d[32];
-    tc::tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(ci * 64 + 32 * cg), d);
+    tc::tmem_ld32(tmem + lrow + (uint32_t)(ci * 64 + 32 * cg), d);
+    if ((j >> 5) == cg) sKN[r] = d[j & 31];  // |k_j|^2 from the diagonal
+  }
+  __syncthreads();
+  if (ok) {
     const float* L = sL + ci * C;
-    const float Lj = L[j], cej = sCE[ci * C + j];
-    const bool fold = L[C - 1] >= FOLD_MIN_LC;
-    float* Arow = sA + (ci * C + j) * LDA + 32 * cg;
-#pragma unroll
-    for (int e = 0; e < 32; e += 4) {
-      float4 o;
-      const int l = 32 * cg + e;
-      o.x = (l + 0 < j) ? cej * exp2f(Lj - L[l + 0]) * d[e + 0] : 0.f;
-      o.y = (l + 1 < j) ? cej * exp2f(Lj - L[l + 1]) * d[e + 1] : 0.f;
-      o.z = (l + 2 < j) ? cej * exp2f(Lj - L[l + 2]) * d[e + 2] : 0.f;
-      o.w = (l + 3 < j) ? cej * exp2f(Lj - L[l + 3]) * d[e + 3] : 0.f;
-      *reinterpret_cast<float4*>(Arow + e) = o;
+    const float Lj = L[j];
+    float cej = 0.f, cwj = 0.f;
+    if (tj < a.T) {
+      if (P.kmd2) {
+        cej = be;
+        cwj = bw;
+      } else {
+        const float al = stable_alpha(be * sKN[r]);
+        cej = al * be;
+        cwj = al * bw;
+      }
     }
-    // Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for l <= i, stored transposed (rows l, 64 i:
-    // the MN-major B operand of y += W^T Mq^T) over the q tile (its MMAs have completed)
-    tc::tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(128 + ci * 64 + 32 * cg), d);
-    char* mqt = cQ + ci * 8192;
-    const uint32_t cb = (uint32_t)(j & 7) * 2;
+    if (cg == 0) {
+      sCE[r] = cej * fast_exp2(Lj);  // T_e column factor ce_l 2^{L_l}
+      sCW[r] = cwj;
+    }
+    // masks: A[j][l] = ce_j 2^{L_j - L_l} (k_j.k_l) for l < j
+    const bool fold = L[C - 1] >= FOLD_MIN_LC;  // uniform per chunk, i.e. per warp
+    const float* NE = sNE + ci * C;
+    float* Arow = sA + (ci * C + j) * LDA + 32 * cg;
+    // 2^{L_j - L_l} as (2^{L_j}) (2^{-L_l}) where both stay in range (folded chunks)
+    const float rj = cej * fast_exp2(Lj);
+    float g[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
       const int l = 32 * cg + e;
-      const float v = (l <= j) ? exp2f(fold ? -L[l] : Lj - L[l]) * d[e] : 0.f;
-      *reinterpret_cast<__nv_bfloat16*>(mqt + tc::sw128(l, j >> 3, C) + cb) = __float2bfloat16_rn(v);
+      const float w = fold ? rj * NE[l] : cej * fast_exp2(Lj - L[l]);
+      g[e] = (l < j) ? w * d[e] : 0.f;
+    }
+    // Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for l <= i (2^{-L_l} q_i.k_l on folded chunks),
+    // written straight to the chunk's tile transposed (rows l, 64 i: the MN-major B
+    // operand of y += W^T Mq^T)
+    tc::tmem_ld32(tmem + lrow + (uint32_t)(128 + ci * 64 + 32 * cg), d);
+#pragma unroll
+    for (int e = 0; e < 32; e += 4)
+      *reinterpret_cast<float4*>(Arow + e) = make_float4(g[e], g[e + 1], g[e + 2], g[e + 3]);
+    const int64_t chn = pair * 2 + ci;
+    if (chn < P.nchunks) {
+      char* mqt = reinterpret_cast<char*>(P.tt + (n * P.nchunks + chn) * TT_ELEMS + 2 * C * C);
+      const uint32_t cb = (uint32_t)(j & 7) * 2;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int l = 32 * cg + e;
+        const float v = (l <= j) ? (fold ? NE[l] : fast_exp2(Lj - L[l])) * d[e] : 0.f;
+        *reinterpret_cast<__nv_bfloat16*>(mqt + tc::sw128(l, j >> 3, C) + cb) = __float2bfloat16_rn(v);
+      }
     }
   }
   tc::fence_before();
@@ -378,7 +369,6 @@ __global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const _
   }
   // T = (I + A)^{-1} by 32 x 32 blocks: T11, T22 by substitution (warps 0-3),
   // then R = A21 T11 and T21 = -T22 R (all warps, 8 rows each).
-  if (tid < 2 * C) sCE[tid] *= exp2f(sL[tid]);  // T_e column factor ce_l 2^{L_l}
   if (warp < 4) {
     float* A = sA + (warp >> 1) * C * LDA;
     if (warp & 1) subst_block<32>(A, lane);
@@ -394,7 +384,7 @@ __global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const _
     rows8_times_col(A, r0, 0, col, out);                      // A21 rows
     __syncwarp();
 #pragma unroll
-    for (int r = 0; r < 8; ++r) A[(r0 + r) * LDA + lane] = out[r];  // R over A21
+    for (int q = 0; q < 8; ++q) A[(r0 + q) * LDA + lane] = out[q];  // R over A21
   }
   __syncthreads();
   {
@@ -404,42 +394,37 @@ __global__ void __launch_bounds__(P_NT) wy_prep_kernel(const WyParams P, const _
     rows8_times_col(A, r0, 32, col, out);                            // T22 rows
     __syncthreads();
 #pragma unroll
-    for (int r = 0; r < 8; ++r) A[(r0 + r) * LDA + lane] = -out[r];  // T21
+    for (int q = 0; q < 8; ++q) A[(r0 + q) * LDA + lane] = -out[q];  // T21
   }
   __syncthreads();
-  // T_e = T diag(ce 2^L), T_w = T diag(cw) -> bf16 swizzled tiles over the k tile;
-  // T's upper block T12 is zero
+  // T_e = T diag(ce 2^L), T_w = T diag(cw) as bf16 tiles in the swizzled UMMA layout,
+  // straight to global (T's upper block T12 is zero); then L
   for (int it = tid; it < 2 * C * 8; it += P_NT) {
-    const int ci = it >> 9, j = (it >> 3) & 63, c8 = it & 7;
+    const int cj = it >> 9, jj = (it >> 3) & 63, c8 = it & 7;
+    const int64_t chn = pair * 2 + cj;
+    if (chn >= P.nchunks) continue;
     float te[8], tw[8];
-    if (c8 >= 4 && j < 32) {
+    if (c8 >= 4 && jj < 32) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) te[e] = tw[e] = 0.f;
     } else {
-      const float* src = sA + (ci * C + j) * LDA + 8 * c8;
+      const float* src = sA + (cj * C + jj) * LDA + 8 * c8;
       const float4 u0 = *reinterpret_cast<const float4*>(src), u1 = *reinterpret_cast<const float4*>(src + 4);
       const float t8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        te[e] = t8[e] * sCE[ci * C + 8 * c8 + e];
-        tw[e] = t8[e] * sCW[ci * C + 8 * c8 + e];
+        te[e] = t8[e] * sCE[cj * C + 8 * c8 + e];
+        tw[e] = t8[e] * sCW[cj * C + 8 * c8 + e];
       }
     }
-    const uint32_t off = tc::sw128(j, c8, C);
-    tc::st_chunk_bf16(cK + ci * 16384, off, te);
-    tc::st_chunk_bf16(cK + ci * 16384 + 8192, off, tw);
+    char* dst = reinterpret_cast<char*>(P.tt + (n * P.nchunks + chn) * TT_ELEMS);
+    const uint32_t off = tc::sw128(jj, c8, C);
+    tc::st_chunk_bf16(dst, off, te);
+    tc::st_chunk_bf16(dst + 8192, off, tw);
   }
-  __syncthreads();
-  // write out: [n][chunk][T_e | T_w | Mq^T] (24 KB per chunk) and L
-  for (int ci = 0; ci < 2; ++ci) {
-    const int64_t chn = pair * 2 + ci;
-    if (chn >= P.nchunks) break;
-    uint4* dst = reinterpret_cast<uint4*>(P.tt + (n * P.nchunks + chn) * TT_ELEMS);
-    const uint4* src = reinterpret_cast<const uint4*>(cK + ci * 16384);
-    const uint4* srcm = reinterpret_cast<const uint4*>(cQ + ci * 8192);
-    for (int it = tid; it < 1024; it += P_NT) dst[it] = src[it];
-    for (int it = tid; it < 512; it += P_NT) dst[1024 + it] = srcm[it];
-    if (tid < 64) P.lsum[(n * P.nchunks + chn) * C + tid] = sL[ci * C + tid];
+  if (tid < 2 * C) {
+    const int64_t chn = pair * 2 + (tid >> 6);
+    if (chn < P.nchunks) P.lsum[(n * P.nchunks + chn) * C + (tid & 63)] = sL[tid];
   }
 }
 
