@@ -79,6 +79,10 @@ GDNX_DEV void tma_store_5d(const CUtensorMap* map, int c0, int c1, int c2, int c
 GDNX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 GDNX_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 GDNX_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+GDNX_DEV void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
 GDNX_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(mbar)
@@ -93,10 +97,11 @@ constexpr int P_NT = 256;
 constexpr int P_OFF_K = 0;                          // [2 kb][128 rows][128 B] bf16 k (2 chunks)
 constexpr int P_OFF_Q = P_OFF_K + 32768;            // same for q
 constexpr int P_OFF_A = 0;                          // fp32 [2][64][LDA] over k, q after the MMAs
+constexpr int P_OFF_MQS = 36864;                    // Mq^T staging [2][64 l][64 i] bf16 over q
 constexpr int P_OFF_SC = P_OFF_Q + 32768;           // L, ce, cw, kn, 2^-L [2][64] each; inv_freq [64]
 constexpr int P_OFF_BAR = P_OFF_SC + (10 * 64 + 64) * 4;
 constexpr int P_SMEM = P_OFF_BAR + 64 + 1024;
-static_assert(2 * C * LDA * 4 <= 65536, "A over the k/q tiles");
+static_assert(2 * C * LDA * 4 <= P_OFF_MQS && P_OFF_MQS + 16384 <= 65536, "A and Mq^T over the k/q tiles");
 
 struct WyParams {
   gdnx_scan_args a;
@@ -345,20 +350,26 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
 #pragma unroll
     for (int e = 0; e < 32; e += 4)
       *reinterpret_cast<float4*>(Arow + e) = make_float4(g[e], g[e + 1], g[e + 2], g[e + 3]);
-    const int64_t chn = pair * 2 + ci;
-    if (chn < P.nchunks) {
-      char* mqt = reinterpret_cast<char*>(P.tt + (n * P.nchunks + chn) * TT_ELEMS + 2 * C * C);
-      const uint32_t cb = (uint32_t)(j & 7) * 2;
+    char* mqt = reinterpret_cast<char*>(sm + P_OFF_MQS + ci * 8192);
+    const uint32_t cb = (uint32_t)(j & 7) * 2;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int l = 32 * cg + e;
-        const float v = (l <= j) ? (fold ? NE[l] : fast_exp2(Lj - L[l])) * d[e] : 0.f;
-        *reinterpret_cast<__nv_bfloat16*>(mqt + tc::sw128(l, j >> 3, C) + cb) = __float2bfloat16_rn(v);
-      }
+    for (int e = 0; e < 32; ++e) {
+      const int l = 32 * cg + e;
+      const float v = (l <= j) ? (fold ? NE[l] : fast_exp2(Lj - L[l])) * d[e] : 0.f;
+      *reinterpret_cast<__nv_bfloat16*>(mqt + tc::sw128(l, j >> 3, C) + cb) = __float2bfloat16_rn(v);
     }
   }
+  tc::fence_async_smem();
   tc::fence_before();
   __syncthreads();
+  if (ok && tid == 0) {  // staged Mq^T tiles -> global with bulk copies
+    for (int c2 = 0; c2 < 2; ++c2) {
+      const int64_t chn = pair * 2 + c2;
+      if (chn < P.nchunks)
+        bulk_store(P.tt + (n * P.nchunks + chn) * TT_ELEMS + 2 * C * C, tc::smem_u32(sm + P_OFF_MQS + c2 * 8192), 8192);
+    }
+    bulk_commit();
+  }
   if (warp == 0) {
     tc::fence_after();
     tc::tmem_dealloc(tmem, 256);
@@ -426,6 +437,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     const int64_t chn = pair * 2 + (tid >> 6);
     if (chn < P.nchunks) P.lsum[(n * P.nchunks + chn) * C + (tid & 63)] = sL[tid];
   }
+  if (tid == 0) bulk_wait_read();  // the Mq^T stores have read shared memory
 }
 
 // ------------------------------- pass 2 ------------------------------------
