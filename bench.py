@@ -235,7 +235,7 @@ def main():
     inp = make_prefill_inputs(c, dev, seed=1 + rank)
     rope = lane_rope(c["M"], c["K"], c["K"], 0.5)
     y = torch.empty(c["B"], c["T"], c["H"], c["M"], c["V"], dtype=torch.bfloat16, device=dev)
-    ws = torch.empty(1 << 20, dtype=torch.uint8, device=dev)
+    ws = None  # the library's per-stream workspace (T_e, T_w, Mq tiles of the parallel pass)
 
     def step():
         ops.gdn3_scan(inp["q"], inp["k"], inp["v"], inp["beta"], inp["beta"], inp["logg"], decay_kind="log",
@@ -257,7 +257,8 @@ def main():
     tp = ROOT / "profiles" / "traffic.json"
     if tp.exists():
         traffic = json.loads(tp.read_text()).get("prefill_config1_bytes_per_launch")
-    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
+    roofline = {"bound": "tensor", "scope": "whole prefill step: wy_prep_kernel + wy_scan_kernel",
+                "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16"], "traffic": traffic,
                 "peak_source": f"{peaks['source']} bf16 burst", "flops_per_launch": flops,
                 "alg_bytes_per_launch": prefill_bytes(c),
@@ -375,7 +376,7 @@ def main():
                            "state": "fp32", "io": "bf16", "algo": args.algo,
                            "l2": "inputs 402 MB + outputs 537 MB > 126 MB L2 (no flush)",
                            "parallelism": f"(batch x head) shards, dp{world}"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
                 "clocks": clocks, "decode": decode, "gather": gather, "kr": kr}
         print(json.dumps(line), flush=True)
     if dist:

@@ -133,13 +133,28 @@ def gdn3_scan(q, k, v, b_gate, w_gate, decay, *, decay_kind="gamma", rope: Optio
     return (y, st_out) if return_state else y
 
 
+# Scan workspaces owned by this module, one per (device, stream): grown on demand and
+# reused, so repeated calls allocate nothing.  Calls on one stream are ordered, so
+# they can share it; pass `workspace=` to manage the memory yourself.
+_WORKSPACES = {}
+
+
+def _cached_workspace(device, need):
+    key = (device.index, _stream(device))
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def _run_scan(a, device, workspace):
     lib = L.load()
     need = lib.gdnx_scan_workspace_bytes(C.byref(a))
     ws = workspace
     if need:
         if ws is None or ws.numel() * ws.element_size() < need:
-            ws = torch.empty(need, dtype=torch.uint8, device=device)
+            ws = _cached_workspace(device, need)
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel() * ws.element_size()
     with torch.cuda.device(device):
         L.check(lib.gdnx_scan_fwd(C.byref(a), C.c_void_p(_stream(device))), "gdnx_scan_fwd")
