@@ -94,11 +94,10 @@ GDNX_DEV void expect_tx(uint32_t mbar, uint32_t bytes) {
 
 // ------------------------------- pass 1 ------------------------------------
 constexpr int P_NT = 256;
-constexpr int P_OFF_K = 0;                          // [2 kb][128 rows][128 B] bf16 k (2 chunks)
-constexpr int P_OFF_Q = P_OFF_K + 32768;            // same for q
-constexpr int P_OFF_A = 0;                          // fp32 [2][64][LDA] over k, q after the MMAs
-constexpr int P_OFF_MQS = 36864;                    // Mq^T staging [2][64 l][64 i] bf16 over q
-constexpr int P_OFF_SC = P_OFF_Q + 32768;           // L, ce, cw, kn, 2^-L [2][64] each; inv_freq [64]
+constexpr int P_OFF_KQ = 0;                         // 2 chunks x [2 kb][rows 0-63 k, 64-127 q][128 B] bf16
+constexpr int P_OFF_A = 0;                          // fp32 [2][64][LDA] over the tiles after the MMAs
+constexpr int P_OFF_MQS = 36864;                    // Mq^T staging [2][64 l][64 i] bf16 over the tiles
+constexpr int P_OFF_SC = P_OFF_KQ + 65536;          // L, ce, cw, kn, 2^-L [2][64] each; inv_freq [64]
 constexpr int P_OFF_BAR = P_OFF_SC + (10 * 64 + 64) * 4;
 constexpr int P_SMEM = P_OFF_BAR + 64 + 1024;
 static_assert(2 * C * LDA * 4 <= P_OFF_MQS && P_OFF_MQS + 16384 <= 65536, "A and Mq^T over the k/q tiles");
@@ -158,13 +157,11 @@ GDNX_DEV void rows8_times_col(const float* A, int r0, int X0, const float* ycol,
 __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
   extern __shared__ uint8_t smraw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
-  char* cK = reinterpret_cast<char*>(sm + P_OFF_K);
-  char* cQ = reinterpret_cast<char*>(sm + P_OFF_Q);
+  char* cKQ = reinterpret_cast<char*>(sm + P_OFF_KQ);
   float* sA = reinterpret_cast<float*>(sm + P_OFF_A);
   float* sL = reinterpret_cast<float*>(sm + P_OFF_SC);  // [2][64] log2 decay prefix
-  float* sCE = sL + 128;                                // ce_l, then the T_e factor ce_l 2^{L_l}
+  float* sCE = sL + 128;                                // T_e column factor ce_l 2^{L_l}
   float* sCW = sL + 256;
-  float* sKN = sL + 384;  // |k|^2
   float* sInv = sL + 512;
   float* sNE = sL + 576;  // [2][64] 2^{-L_l}
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_OFF_BAR);
@@ -180,25 +177,26 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   const int dpairs = (a.rope.enable && lm < 4) ? a.rope.pairs[lm] : 0;
   const int dch = dpairs / 8;
   const int64_t tbase = pair * 2 * C;  // first token of the pair
-  const uint32_t sK = tc::smem_u32(cK), sQ = tc::smem_u32(cQ);
+  const uint32_t sKQ = tc::smem_u32(cKQ);
   const bool braided = a.decay_kind == GDNX_DECAY_BRAIDED;
 
   if (tid == 0) {
     tc::mbar_init(mbar, 1);
     tc::mbar_init(tbar, 1);
-    // k and q rows of both chunks (TMA zero-fills tokens past T): [kb][rows 0-63 chunk a, 64-127 chunk b]
+    // per chunk: k rows 0-63 and q rows 64-127 of each K block (TMA zero-fills tokens past T)
     const uint32_t bar = tc::smem_u32(tbar);
     expect_tx(bar, 8 * 8192);
     const int ck_m = maps.use_m[1] ? lm : 0, cq_m = maps.use_m[0] ? lm : 0;
 #pragma unroll
-    for (int kb = 0; kb < 2; ++kb)
+    for (int ci = 0; ci < 2; ++ci)
 #pragma unroll
-      for (int ci = 0; ci < 2; ++ci) {
-        tma_load_5d(sK + kb * 16384 + ci * 8192, &maps.k, 64 * kb, ck_m, (int)h, (int)(tbase + ci * C), (int)b, bar);
-        tma_load_5d(sQ + kb * 16384 + ci * 8192, &maps.q, 64 * kb, cq_m, (int)h, (int)(tbase + ci * C), (int)b, bar);
+      for (int kb = 0; kb < 2; ++kb) {
+        const uint32_t dst = sKQ + ci * 32768 + kb * 16384;
+        tma_load_5d(dst, &maps.k, 64 * kb, ck_m, (int)h, (int)(tbase + ci * C), (int)b, bar);
+        tma_load_5d(dst + 8192, &maps.q, 64 * kb, cq_m, (int)h, (int)(tbase + ci * C), (int)b, bar);
       }
   }
-  if (warp == 0) tc::tmem_alloc(s_tmem, 256);
+  if (warp == 0) tc::tmem_alloc(s_tmem, 128);
   if (dpairs > 0 && tid < 64) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[lm]);
   // warps 0, 1: log2 decay prefix of chunk `warp` (independent of k)
   if (warp < 2) {
@@ -240,12 +238,14 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     sNE[warp * C + lane] = fast_exp2(-s0);
     sNE[warp * C + lane + 32] = fast_exp2(-s1);
   }
-  // this thread's token (row of the masks): raw gates, in flight during the TMA wait
-  const int quad = warp & 3, cg = warp >> 2;
-  const int r = quad * 32 + lane, ci = r >> 6, j = r & 63;
-  const int64_t tj = tbase + r;
+  // this thread's row: TMEM lane r of chunk ci's block ([K;Q] K^T): rows 0-63 give the
+  // masks row j = r, rows 64-127 the Mq row i = r - 64
+  const int quad = warp & 3, ci = warp >> 2;
+  const int r = quad * 32 + lane, j = r & 63;
+  const bool arow = r < C;
+  const int64_t tj = tbase + ci * C + j;
   float be = 0.f, bw = 0.f;
-  if (tj < a.T) {
+  if (arow && tj < a.T) {
     be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tj, h, m));
     bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tj, h, m));
   }
@@ -256,17 +256,20 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   bool ok = tc::mbar_wait(tbar, 0);
   ok = !__syncthreads_or(!ok);
 
-  // lane RoPE of k and q in place (rotated chunk pairs only; one set of angles per token)
+  // lane RoPE of token t's k and q in place (rotated chunk pairs only; one set of angles)
   if (ok) {
     const float sc = dpairs > 0 ? a.rope.scale[lm] : 0.f;
     for (int it = tid; it < 2 * C * dch; it += P_NT) {
-      const int rr = it / dch, cc = it - rr * dch;
+      const int rr = it / dch, cc = it - rr * dch;  // rr: token of the pair
+      char* tile = cKQ + (rr >> 6) * 32768;
+      const int jj = rr & 63;
       float x1[8], x2[8], y1[8], y2[8];
-      const uint32_t o1 = tc::sw128(rr, cc, 128), o2 = tc::sw128(rr, cc + dch, 128);
-      load8_bf16(cK + o1, 0, x1);
-      load8_bf16(cK + o2, 0, x2);
-      load8_bf16(cQ + o1, 0, y1);
-      load8_bf16(cQ + o2, 0, y2);
+      const uint32_t o1 = tc::sw128(jj, cc, 128), o2 = tc::sw128(jj, cc + dch, 128);
+      const uint32_t p1 = tc::sw128(C + jj, cc, 128), p2 = tc::sw128(C + jj, cc + dch, 128);
+      load8_bf16(tile + o1, 0, x1);
+      load8_bf16(tile + o2, 0, x2);
+      load8_bf16(tile + p1, 0, y1);
+      load8_bf16(tile + p2, 0, y2);
       const float pos = (float)(a.rope.pos0 + tbase + rr);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -279,104 +282,105 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
         y2[e] = b1 * sn + y2[e] * cs;
         y1[e] = b1;
       }
-      tc::st_chunk_bf16(cK, o1, x1);
-      tc::st_chunk_bf16(cK, o2, x2);
-      tc::st_chunk_bf16(cQ, o1, y1);
-      tc::st_chunk_bf16(cQ, o2, y2);
+      tc::st_chunk_bf16(tile, o1, x1);
+      tc::st_chunk_bf16(tile, o2, x2);
+      tc::st_chunk_bf16(tile, p1, y1);
+      tc::st_chunk_bf16(tile, p2, y2);
     }
   }
   tc::fence_async_smem();
   tc::fence_before();
   __syncthreads();
-  // Gram matrices on the tensor cores: [Ka;Kb] [Ka;Kb]^T and [Qa;Qb] [Ka;Kb]^T (N = 128)
+  // Gram matrices on the tensor cores: per chunk [K;Q] K^T (M = 128, N = 64)
   if (ok && tid == 0) {
     tc::fence_after();
-    constexpr uint32_t ID = tc::idesc_bf16(128, 128, false, false);
+    constexpr uint32_t ID = tc::idesc_bf16(128, 64, false, false);
 #pragma unroll
-    for (int s = 0; s < 8; ++s) {
-      const uint32_t ko = (s >> 2) * 16384 + (s & 3) * 32;
-      const uint64_t dbk = tc::smem_desc(sK + ko, 16, 1024);
-      tc::mma_bf16(tmem, tc::smem_desc(sK + ko, 16, 1024), dbk, ID, s > 0);
-      tc::mma_bf16(tmem + 128, tc::smem_desc(sQ + ko, 16, 1024), dbk, ID, s > 0);
-    }
+    for (int c2 = 0; c2 < 2; ++c2)
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const uint32_t ko = sKQ + c2 * 32768 + (s >> 2) * 16384 + (s & 3) * 32;
+        tc::mma_bf16(tmem + 64 * c2, tc::smem_desc(ko, 16, 1024), tc::smem_desc(ko, 16, 1024), ID, s > 0);
+      }
     tc::commit(mbar);
   }
   if (ok) ok = tc::mbar_wait(mbar, 0);
   ok = !__syncthreads_or(!ok);
   tc::fence_after();
-  // this thread: row r of [Ka;Kb] K^T, columns 32 cg .. 32 cg + 31 of its chunk's block
-  float d[32];
-  const uint32_t lrow = (uint32_t)(quad * 32) << 16;
+  float d[64];
   if (ok) {
-    tc::tmem_ld32(tmem + lrow + (uint32_t)(ci * 64 + 32 * cg), d);
-    if ((j >> 5) == cg) sKN[r] = d[j & 31];  // |k_j|^2 from the diagonal
+    const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(64 * ci);
+    tc::tmem_ld32(ta, d);
+    tc::tmem_ld32(ta + 32, d + 32);
   }
-  __syncthreads();
+  tc::fence_before();
+  __syncthreads();  // the tiles are free from here: A and the Mq^T staging go over them
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, 128);
+  }
   if (ok) {
     const float* L = sL + ci * C;
-    const float Lj = L[j];
-    float cej = 0.f, cwj = 0.f;
-    if (tj < a.T) {
-      if (P.kmd2) {
-        cej = be;
-        cwj = bw;
-      } else {
-        const float al = stable_alpha(be * sKN[r]);
-        cej = al * be;
-        cwj = al * bw;
-      }
-    }
-    if (cg == 0) {
-      sCE[r] = cej * fast_exp2(Lj);  // T_e column factor ce_l 2^{L_l}
-      sCW[r] = cwj;
-    }
-    // masks: A[j][l] = ce_j 2^{L_j - L_l} (k_j.k_l) for l < j
-    const bool fold = L[C - 1] >= FOLD_MIN_LC;  // uniform per chunk, i.e. per warp
     const float* NE = sNE + ci * C;
-    float* Arow = sA + (ci * C + j) * LDA + 32 * cg;
-    // 2^{L_j - L_l} as (2^{L_j}) (2^{-L_l}) where both stay in range (folded chunks)
-    const float rj = cej * fast_exp2(Lj);
-    float g[32];
+    const bool fold = L[C - 1] >= FOLD_MIN_LC;  // uniform per chunk, i.e. per warp
+    const float Lj = L[j];
+    if (arow) {
+      // masks: A[j][l] = ce_j 2^{L_j - L_l} (k_j.k_l) for l < j; |k_j|^2 is the diagonal
+      float cej = 0.f, cwj = 0.f;
+      if (tj < a.T) {
+        if (P.kmd2) {
+          cej = be;
+          cwj = bw;
+        } else {
+          float kn = 0.f;  // |k_j|^2 = d[j] (selected without a dynamic register index)
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const int l = 32 * cg + e;
-      const float w = fold ? rj * NE[l] : cej * fast_exp2(Lj - L[l]);
-      g[e] = (l < j) ? w * d[e] : 0.f;
-    }
-    // Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for l <= i (2^{-L_l} q_i.k_l on folded chunks),
-    // written straight to the chunk's tile transposed (rows l, 64 i: the MN-major B
-    // operand of y += W^T Mq^T)
-    tc::tmem_ld32(tmem + lrow + (uint32_t)(128 + ci * 64 + 32 * cg), d);
+          for (int e = 0; e < 64; ++e) kn = (e == j) ? d[e] : kn;
+          const float al = stable_alpha(be * kn);
+          cej = al * be;
+          cwj = al * bw;
+        }
+      }
+      const float ej = fast_exp2(Lj);
+      sCE[ci * C + j] = cej * ej;
+      sCW[ci * C + j] = cwj;
+      const float rj = cej * ej;  // 2^{L_j - L_l} as 2^{L_j} 2^{-L_l} on folded chunks
+      float* Arow = sA + (ci * C + j) * LDA;
 #pragma unroll
-    for (int e = 0; e < 32; e += 4)
-      *reinterpret_cast<float4*>(Arow + e) = make_float4(g[e], g[e + 1], g[e + 2], g[e + 3]);
-    char* mqt = reinterpret_cast<char*>(sm + P_OFF_MQS + ci * 8192);
-    const uint32_t cb = (uint32_t)(j & 7) * 2;
+      for (int e = 0; e < 64; e += 4) {
+        float g[4];
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const int l = 32 * cg + e;
-      const float v = (l <= j) ? (fold ? NE[l] : fast_exp2(Lj - L[l])) * d[e] : 0.f;
-      *reinterpret_cast<__nv_bfloat16*>(mqt + tc::sw128(l, j >> 3, C) + cb) = __float2bfloat16_rn(v);
+        for (int u = 0; u < 4; ++u) {
+          const int l = e + u;
+          const float w = fold ? rj * NE[l] : cej * fast_exp2(Lj - L[l]);
+          g[u] = (l < j) ? w * d[l] : 0.f;
+        }
+        *reinterpret_cast<float4*>(Arow + e) = make_float4(g[0], g[1], g[2], g[3]);
+      }
+    } else {
+      // Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for l <= i (2^{-L_l} q_i.k_l on folded chunks),
+      // staged transposed (rows l, 64 i: the MN-major B operand of y += W^T Mq^T)
+      char* mqt = reinterpret_cast<char*>(sm + P_OFF_MQS + ci * 8192);
+      const uint32_t cb = (uint32_t)(j & 7) * 2;
+#pragma unroll
+      for (int l = 0; l < 64; ++l) {
+        const float v = (l <= j) ? (fold ? NE[l] : fast_exp2(Lj - L[l])) * d[l] : 0.f;
+        *reinterpret_cast<__nv_bfloat16*>(mqt + tc::sw128(l, j >> 3, C) + cb) = __float2bfloat16_rn(v);
+      }
     }
   }
   tc::fence_async_smem();
-  tc::fence_before();
   __syncthreads();
-  if (ok && tid == 0) {  // staged Mq^T tiles -> global with bulk copies
+  if (!ok) {
+    if (tid == 0 && P.err) atomicExch(P.err, (int)GDNX_ETIMEOUT);
+    return;
+  }
+  if (tid == 0) {  // staged Mq^T tiles -> global with bulk copies
     for (int c2 = 0; c2 < 2; ++c2) {
       const int64_t chn = pair * 2 + c2;
       if (chn < P.nchunks)
         bulk_store(P.tt + (n * P.nchunks + chn) * TT_ELEMS + 2 * C * C, tc::smem_u32(sm + P_OFF_MQS + c2 * 8192), 8192);
     }
     bulk_commit();
-  }
-  if (warp == 0) {
-    tc::fence_after();
-    tc::tmem_dealloc(tmem, 256);
-  }
-  if (!ok) {
-    if (tid == 0 && P.err) atomicExch(P.err, (int)GDNX_ETIMEOUT);
-    return;
   }
   // T = (I + A)^{-1} by 32 x 32 blocks: T11, T22 by substitution (warps 0-3),
   // then R = A21 T11 and T21 = -T22 R (all warps, 8 rows each).
