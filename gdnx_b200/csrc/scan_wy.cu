@@ -94,7 +94,9 @@ GDNX_DEV void expect_tx(uint32_t mbar, uint32_t bytes) {
 
 // ------------------------------- pass 1 ------------------------------------
 constexpr int P_NT = 256;
-constexpr int P_OFF_KQ = 0;                         // 2 chunks x [2 kb][rows 0-63 k, 64-127 q][128 B] bf16
+// [2 kb][256 rows][128 B] bf16, rows: Qa | Ka | Kb | Qb (a, b: the pair's chunks), so that
+// [Ka;Kb] (rows 64-191) is the A operand and [Qa;Ka] / [Kb;Qb] (rows 0-127 / 128-255) the B operands
+constexpr int P_OFF_KQ = 0;
 constexpr int P_OFF_A = 0;                          // fp32 [2][64][LDA] over the tiles after the MMAs
 constexpr int P_OFF_MQS = 36864;                    // Mq^T staging [2][64 l][64 i] bf16 over the tiles
 constexpr int P_OFF_SC = P_OFF_KQ + 65536;          // L, ce, cw, kn, 2^-L [2][64] each; inv_freq [64]
@@ -183,20 +185,20 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   if (tid == 0) {
     tc::mbar_init(mbar, 1);
     tc::mbar_init(tbar, 1);
-    // per chunk: k rows 0-63 and q rows 64-127 of each K block (TMA zero-fills tokens past T)
+    // rows Qa | Ka | Kb | Qb of each K block (TMA zero-fills tokens past T)
     const uint32_t bar = tc::smem_u32(tbar);
     expect_tx(bar, 8 * 8192);
     const int ck_m = maps.use_m[1] ? lm : 0, cq_m = maps.use_m[0] ? lm : 0;
 #pragma unroll
-    for (int ci = 0; ci < 2; ++ci)
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb) {
-        const uint32_t dst = sKQ + ci * 32768 + kb * 16384;
-        tma_load_5d(dst, &maps.k, 64 * kb, ck_m, (int)h, (int)(tbase + ci * C), (int)b, bar);
-        tma_load_5d(dst + 8192, &maps.q, 64 * kb, cq_m, (int)h, (int)(tbase + ci * C), (int)b, bar);
-      }
+    for (int kb = 0; kb < 2; ++kb) {
+      const uint32_t blk = sKQ + kb * 32768;
+      tma_load_5d(blk, &maps.q, 64 * kb, cq_m, (int)h, (int)tbase, (int)b, bar);
+      tma_load_5d(blk + 8192, &maps.k, 64 * kb, ck_m, (int)h, (int)tbase, (int)b, bar);
+      tma_load_5d(blk + 16384, &maps.k, 64 * kb, ck_m, (int)h, (int)(tbase + C), (int)b, bar);
+      tma_load_5d(blk + 24576, &maps.q, 64 * kb, cq_m, (int)h, (int)(tbase + C), (int)b, bar);
+    }
   }
-  if (warp == 0) tc::tmem_alloc(s_tmem, 128);
+  if (warp == 0) tc::tmem_alloc(s_tmem, 256);
   if (dpairs > 0 && tid < 64) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[lm]);
   // warps 0, 1: log2 decay prefix of chunk `warp` (independent of k)
   if (warp < 2) {
@@ -238,11 +240,12 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     sNE[warp * C + lane] = fast_exp2(-s0);
     sNE[warp * C + lane + 32] = fast_exp2(-s1);
   }
-  // this thread's row: TMEM lane r of chunk ci's block ([K;Q] K^T): rows 0-63 give the
-  // masks row j = r, rows 64-127 the Mq row i = r - 64
-  const int quad = warp & 3, ci = warp >> 2;
-  const int r = quad * 32 + lane, j = r & 63;
-  const bool arow = r < C;
+  // this thread: TMEM lane r = token j of chunk ci (k_j against the chunk's k or q);
+  // warps 0-3 / 4-7 take the two 64-column halves: the masks row (k_j.k_l) or the
+  // Mq^T row (k_j.q_i)
+  const int quad = warp & 3, half = warp >> 2;
+  const int r = quad * 32 + lane, ci = r >> 6, j = r & 63;
+  const bool arow = half == (ci == 0 ? 1 : 0);
   const int64_t tj = tbase + ci * C + j;
   float be = 0.f, bw = 0.f;
   if (arow && tj < a.T) {
@@ -261,15 +264,16 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     const float sc = dpairs > 0 ? a.rope.scale[lm] : 0.f;
     for (int it = tid; it < 2 * C * dch; it += P_NT) {
       const int rr = it / dch, cc = it - rr * dch;  // rr: token of the pair
-      char* tile = cKQ + (rr >> 6) * 32768;
       const int jj = rr & 63;
+      const int kr = C + rr;                         // Ka rows 64-127, Kb rows 128-191
+      const int qr = rr < C ? jj : 3 * C + jj;       // Qa rows 0-63, Qb rows 192-255
       float x1[8], x2[8], y1[8], y2[8];
-      const uint32_t o1 = tc::sw128(jj, cc, 128), o2 = tc::sw128(jj, cc + dch, 128);
-      const uint32_t p1 = tc::sw128(C + jj, cc, 128), p2 = tc::sw128(C + jj, cc + dch, 128);
-      load8_bf16(tile + o1, 0, x1);
-      load8_bf16(tile + o2, 0, x2);
-      load8_bf16(tile + p1, 0, y1);
-      load8_bf16(tile + p2, 0, y2);
+      const uint32_t o1 = tc::sw128(kr, cc, 256), o2 = tc::sw128(kr, cc + dch, 256);
+      const uint32_t p1 = tc::sw128(qr, cc, 256), p2 = tc::sw128(qr, cc + dch, 256);
+      load8_bf16(cKQ + o1, 0, x1);
+      load8_bf16(cKQ + o2, 0, x2);
+      load8_bf16(cKQ + p1, 0, y1);
+      load8_bf16(cKQ + p2, 0, y2);
       const float pos = (float)(a.rope.pos0 + tbase + rr);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -282,26 +286,27 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
         y2[e] = b1 * sn + y2[e] * cs;
         y1[e] = b1;
       }
-      tc::st_chunk_bf16(tile, o1, x1);
-      tc::st_chunk_bf16(tile, o2, x2);
-      tc::st_chunk_bf16(tile, p1, y1);
-      tc::st_chunk_bf16(tile, p2, y2);
+      tc::st_chunk_bf16(cKQ, o1, x1);
+      tc::st_chunk_bf16(cKQ, o2, x2);
+      tc::st_chunk_bf16(cKQ, p1, y1);
+      tc::st_chunk_bf16(cKQ, p2, y2);
     }
   }
   tc::fence_async_smem();
   tc::fence_before();
   __syncthreads();
-  // Gram matrices on the tensor cores: per chunk [K;Q] K^T (M = 128, N = 64)
+  // on the tensor cores, A = [Ka;Kb] (M = 128): D_a = A [Qa;Ka]^T (cols 0-127),
+  // D_b = A [Kb;Qb]^T (cols 128-255); rows 0-63 of D_a and 64-127 of D_b are used
   if (ok && tid == 0) {
     tc::fence_after();
-    constexpr uint32_t ID = tc::idesc_bf16(128, 64, false, false);
+    constexpr uint32_t ID = tc::idesc_bf16(128, 128, false, false);
 #pragma unroll
-    for (int c2 = 0; c2 < 2; ++c2)
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint32_t ko = sKQ + c2 * 32768 + (s >> 2) * 16384 + (s & 3) * 32;
-        tc::mma_bf16(tmem + 64 * c2, tc::smem_desc(ko, 16, 1024), tc::smem_desc(ko, 16, 1024), ID, s > 0);
-      }
+    for (int s = 0; s < 8; ++s) {
+      const uint32_t ko = sKQ + (s >> 2) * 32768 + (s & 3) * 32;
+      const uint64_t da = tc::smem_desc(ko + 64 * 128, 16, 1024);
+      tc::mma_bf16(tmem, da, tc::smem_desc(ko, 16, 1024), ID, s > 0);
+      tc::mma_bf16(tmem + 128, da, tc::smem_desc(ko + 128 * 128, 16, 1024), ID, s > 0);
+    }
     tc::commit(mbar);
   }
   if (ok) ok = tc::mbar_wait(mbar, 0);
@@ -309,7 +314,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   tc::fence_after();
   float d[64];
   if (ok) {
-    const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(64 * ci);
+    const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(128 * ci + 64 * half);
     tc::tmem_ld32(ta, d);
     tc::tmem_ld32(ta + 32, d + 32);
   }
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   __syncthreads();  // the tiles are free from here: A and the Mq^T staging go over them
   if (warp == 0) {
     tc::fence_after();
-    tc::tmem_dealloc(tmem, 128);
+    tc::tmem_dealloc(tmem, 256);
   }
   if (ok) {
     const float* L = sL + ci * C;
@@ -357,14 +362,19 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
         *reinterpret_cast<float4*>(Arow + e) = make_float4(g[0], g[1], g[2], g[3]);
       }
     } else {
-      // Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for l <= i (2^{-L_l} q_i.k_l on folded chunks),
-      // staged transposed (rows l, 64 i: the MN-major B operand of y += W^T Mq^T)
+      // Mq^T row l = j: Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for i >= l (2^{-L_l} q_i.k_l on
+      // folded chunks); rows l, 64 i: the MN-major B operand of y += W^T Mq^T
       char* mqt = reinterpret_cast<char*>(sm + P_OFF_MQS + ci * 8192);
-      const uint32_t cb = (uint32_t)(j & 7) * 2;
+      const float nej = NE[j];
 #pragma unroll
-      for (int l = 0; l < 64; ++l) {
-        const float v = (l <= j) ? (fold ? NE[l] : fast_exp2(Lj - L[l])) * d[l] : 0.f;
-        *reinterpret_cast<__nv_bfloat16*>(mqt + tc::sw128(l, j >> 3, C) + cb) = __float2bfloat16_rn(v);
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = 8 * c8 + e;
+          v[e] = (i >= j) ? (fold ? nej : fast_exp2(L[i] - Lj)) * d[i] : 0.f;
+        }
+        tc::st_chunk_bf16(mqt, tc::sw128(j, c8, C), v);
       }
     }
   }
