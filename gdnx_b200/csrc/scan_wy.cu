@@ -483,7 +483,7 @@ static_assert(S_OFF_KQ0 - KB == S_OFF_MQ0, "stage-0 Mq^T position");
 static_assert(S_SMEM <= 232448, "shared memory");
 constexpr uint32_t STAGE_TX = 6 * 8192 + 3 * 8192 + 256;
 
-// TMEM columns: W^T0 | y0 | state (128) | y1 | W^T1 | Wk^T, so that G2 writes
+// TMEM columns: W^T0 | y0 | state (128) | y1 | W^T1 | [Wk; T_w K] (128), so that G2 writes
 // [W^T0 | y0] / [y1 | W^T1] and G3 writes [y0 | S] / [S | y1] with one MMA each.
 constexpr uint32_t T_W0 = 0, T_Y0 = 64, T_S = 128, T_Y1 = 256, T_W1 = 320, T_WK = 384;
 
@@ -625,6 +625,7 @@ __global__ void __launch_bounds__(S_NT, 1)
   tc::fence_after();
 
   constexpr uint32_t ID_MN_K = tc::idesc_bf16(128, 64, true, false);
+  constexpr uint32_t ID_WK = tc::idesc_bf16(128, 128, false, true);
   constexpr uint32_t ID_G2 = tc::idesc_bf16(128, 128, false, false);
   constexpr uint32_t ID_G3 = tc::idesc_bf16(128, 192, false, true);
 
@@ -821,8 +822,8 @@ __global__ void __launch_bounds__(S_NT, 1)
         tc::fence_after();
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(tmem + T_WK, tc::smem_desc(skq + k * 2048, KB, 1024), tc::smem_desc(stt + k * 32, 16, 1024),
-                       ID_MN_K, k > 0);
+          tc::mma_bf16(tmem + T_WK, tc::smem_desc(stt + k * 32, 16, 1024), tc::smem_desc(skq + k * 2048, KB, 1024),
+                       ID_WK, k > 0);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           tc::mma_bf16(tmem + (s ? T_W1 : T_W0), tc::smem_desc(sv + k * 2048, 8192, 1024),
@@ -852,18 +853,18 @@ __global__ void __launch_bounds__(S_NT, 1)
           tc::st_chunk_bf16(kq, off, x);
         }
       }
-      // -Wk as rows of the G2 B operand (K-major [j][k]): this thread holds Wk^T[k = row][j]
-      {
+      // -Wk as rows of the G2 B operand (K-major [j][k]): TMEM rows 0-63 hold Wk[j][k]
+      // (the product [T_e; T_w] K, whose rows 64-127 are not needed); half h writes k block h
+      if (quad < 2) {
         float d[32];
-        tc::tmem_ld32(tmem + T_WK + lbase + 32 * half, d);
-        char* base = kq + (row >> 6) * KB;
-        const int kk = row & 63;
-        const uint32_t cb = (uint32_t)(kk & 7) * 2;
+        char* base = kq + half * KB;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int j = 32 * half + e;
-          *reinterpret_cast<__nv_bfloat16*>(base + (wr + j) * 128 + (((kk >> 3) ^ ((wr + j) & 7)) << 4) + cb) =
-              __float2bfloat16_rn(-d[e]);
+        for (int hh = 0; hh < 2; ++hh) {
+          tc::tmem_ld32(tmem + T_WK + lbase + 64 * half + 32 * hh, d);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) d[e] = -d[e];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(base, tc::sw128(wr + row, 4 * hh + q4, 192), d + 8 * q4);
         }
       }
       tc::fence_async_smem();
