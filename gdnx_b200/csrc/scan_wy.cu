@@ -487,6 +487,32 @@ constexpr uint32_t STAGE_TX = 6 * 8192 + 3 * 8192 + 256;
 // [W^T0 | y0] / [y1 | W^T1] and G3 writes [y0 | S] / [S | y1] with one MMA each.
 constexpr uint32_t T_W0 = 0, T_Y0 = 64, T_S = 128, T_Y1 = 256, T_W1 = 320, T_WK = 384;
 
+// 16 TMEM lanes x 32 consecutive 32-bit columns in the 16x256b fragment layout:
+// for each 8-column group p, registers 4p..4p+3 hold (lane g, column 2(t%4)),
+// (lane g, column 2(t%4)+1), (lane g+8, column 2(t%4)), (lane g+8, column 2(t%4)+1),
+// with g = t/4 (t = thread of the warp): the layout of an m16n8 accumulator, which
+// stmatrix stores 8x8 at a time.  The completion wait is in the same asm statement.
+GDNX_DEV void tmem_ld_16x256b_x4(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// Four 8x8 bf16 matrices (fragment: thread t holds row t/4, columns 2(t%4), +1 of
+// each) stored transposed: thread t gives the address of stored row t%8 of matrix t/8.
+GDNX_DEV void stmatrix_x4_trans(uint32_t saddr, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a0),
+               "r"(a1), "r"(a2), "r"(a3)
+               : "memory");
+}
+
 GDNX_DEV bool try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -733,21 +759,31 @@ __global__ void __launch_bounds__(S_NT, 1)
       const bool ok = wait_or_abort(g3 + sp, (uint32_t)((c >> 1) & 1), s_abort);
       tc::fence_after();
       if (group_any(1, !ok)) return false;
-      float yv[32];
-      tc::tmem_ld32(tmem + (sp ? T_Y1 : T_Y0) + lbase + 32 * half, yv);
-      if (sSF[sp].w != 0.f) {  // folded chunk: y_i = 2^{L_i} (S0 q_i + sum_l Mq'_il W_l)
-#pragma unroll
-        for (int e = 0; e < 32; ++e) yv[e] *= sEL[64 * sp + 32 * half + e];
-      }
+      const bool folded = sSF[sp].w != 0.f;  // y_i = 2^{L_i} (S0 q_i + sum_l Mq'_il W_l)
+      const uint32_t ty = tmem + (sp ? T_Y1 : T_Y0);
       if (maps.y_tma) {
-        char* stg = reinterpret_cast<char*>(sm + kq_off(sp) + wk_row(sp) * 128 + (row >> 6) * KB);
-        const int vv = row & 63;
-        const uint32_t cb = (uint32_t)(vv & 7) * 2;
+        // rows v (TMEM lanes) x tokens i -> [token][v] swizzled tiles: 16x256b loads give
+        // 8x8 fragments, stored transposed by stmatrix
+        float ya[16], yb[16];
+        tmem_ld_16x256b_x4(ty + lbase + 32 * half, ya);                       // lanes 32q + 0..15
+        tmem_ld_16x256b_x4(ty + lbase + (16u << 16) + 32 * half, yb);         // lanes 32q + 16..31
+        const int t4 = lane & 3, mi = lane >> 3, jr = lane & 7;
+        const uint32_t stg = sbase + kq_off(sp) + wk_row(sp) * 128;
+        const int v0 = 32 * quad + 8 * mi;  // this thread's address: matrix mi, stored row jr
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int i = 32 * half + e;
-          *reinterpret_cast<__nv_bfloat16*>(stg + i * 128 + (((vv >> 3) ^ (i & 7)) << 4) + cb) =
-              __float2bfloat16_rn(yv[e]);
+        for (int p = 0; p < 4; ++p) {
+          float f0 = 1.f, f1 = 1.f;
+          if (folded) {
+            f0 = sEL[64 * sp + 32 * half + 8 * p + 2 * t4];
+            f1 = sEL[64 * sp + 32 * half + 8 * p + 2 * t4 + 1];
+          }
+          const uint32_t m0 = tc::pack_bf16(ya[4 * p] * f0, ya[4 * p + 1] * f1);
+          const uint32_t m1 = tc::pack_bf16(ya[4 * p + 2] * f0, ya[4 * p + 3] * f1);
+          const uint32_t m2 = tc::pack_bf16(yb[4 * p] * f0, yb[4 * p + 1] * f1);
+          const uint32_t m3 = tc::pack_bf16(yb[4 * p + 2] * f0, yb[4 * p + 3] * f1);
+          const int i = 32 * half + 8 * p + jr;
+          const uint32_t addr = stg + (uint32_t)((v0 >> 6) * KB + i * 128 + ((((v0 & 63) >> 3) ^ (i & 7)) << 4));
+          stmatrix_x4_trans(addr, m0, m1, m2, m3);
         }
         tc::fence_async_smem();
         group_sync(1);
@@ -758,11 +794,14 @@ __global__ void __launch_bounds__(S_NT, 1)
           bulk_commit();
         }
       } else {
+        float yv[32];
+        tc::tmem_ld32(ty + lbase + 32 * half, yv);
         const int nt = (int)((a.T - c * C) < C ? (a.T - c * C) : C);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int i = 32 * half + e;
-          if (i < nt) st_from_f32(a.y, a.y_dtype, ybase + row + (c * C + i) * a.y_st, yv[e]);
+          const float f = folded ? sEL[64 * sp + i] : 1.f;
+          if (i < nt) st_from_f32(a.y, a.y_dtype, ybase + row + (c * C + i) * a.y_st, yv[e] * f);
         }
       }
       return true;
