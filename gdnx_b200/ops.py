@@ -139,6 +139,83 @@ def gdn3_scan(q, k, v, b_gate, w_gate, decay, *, decay_kind="gamma", rope: Optio
 _WORKSPACES = {}
 
 
+# ----------------------------------------------------------------------------
+# host-to-host scan with copy / compute overlap
+# ----------------------------------------------------------------------------
+
+_HOST_BUFS = {}
+
+
+def _host_pipeline_buffers(device, shapes_dtypes):
+    """Two device buffer sets (double buffering) for the sliced host scan, cached by shape."""
+    key = (device.index,) + tuple(shapes_dtypes)
+    bufs = _HOST_BUFS.get(key)
+    if bufs is None:
+        bufs = [[torch.empty(shp, dtype=dt, device=device) for shp, dt in shapes_dtypes] for _ in range(2)]
+        _HOST_BUFS.clear()  # keep one configuration resident
+        _HOST_BUFS[key] = bufs
+    return bufs
+
+
+def gdn3_scan_host(q, k, v, b_gate, w_gate, decay, *, out: torch.Tensor, device=None, slices: Optional[int] = None,
+                   decay_kind="gamma", rope: Optional[LaneRope] = None, algo: str = "auto",
+                   braid_rates=BRAID_RATES, braid_clamp=DECAY_CLAMP):
+    """Dense GDN3 scan from host memory to host memory.
+
+    Inputs and ``out`` are CPU tensors (pinned for asynchronous copies) shaped as for
+    :func:`gdn3_scan`.  Chains never interact across batch rows, so the batch is cut
+    into ``slices`` (default: one row each, at most 16); each slice's host->device
+    copies, scan and device->host copy run on three CUDA streams ordered by events,
+    so copies in both directions overlap the scans of neighbouring slices.  Device
+    buffers are double-buffered and cached.  Returns ``out`` once the last copy has
+    been enqueued on the current stream's timeline (synchronise before reading it).
+    """
+    device = torch.device(device) if device is not None else torch.device("cuda")
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    ins = [q, k, v, b_gate, w_gate, decay]
+    if any(t.is_cuda for t in ins + [out]):
+        raise ValueError("gdn3_scan_host takes host tensors; use gdn3_scan for device tensors")
+    B = k.shape[0]
+    nsl = slices or min(B, 16)
+    bounds = [(B * i) // nsl for i in range(nsl + 1)]
+    rows = max(bounds[i + 1] - bounds[i] for i in range(nsl))
+    shapes = [((rows,) + tuple(t.shape[1:]), t.dtype) for t in ins] + [((rows,) + tuple(out.shape[1:]), out.dtype)]
+    bufs = _host_pipeline_buffers(device, shapes)
+    with torch.cuda.device(device):
+        main = torch.cuda.current_stream(device)
+        h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        h2d.wait_stream(main)
+        d2h.wait_stream(main)
+        done_in = [torch.cuda.Event() for _ in range(nsl)]
+        done_scan = [torch.cuda.Event() for _ in range(nsl)]
+        done_out = [torch.cuda.Event() for _ in range(nsl)]
+        for i in range(nsl):
+            b0, b1 = bounds[i], bounds[i + 1]
+            n = b1 - b0
+            buf = bufs[i % 2]
+            with torch.cuda.stream(h2d):
+                if i >= 2:
+                    h2d.wait_event(done_scan[i - 2])  # the scan two slices back has read this buffer set
+                for d_t, h_t in zip(buf[:6], ins):
+                    d_t[:n].copy_(h_t[b0:b1], non_blocking=True)
+                done_in[i].record(h2d)
+            main.wait_event(done_in[i])
+            if i >= 2:
+                main.wait_event(done_out[i - 2])  # its output buffer has been copied out
+            dq, dk, dv, db, dw, dd = (t[:n] for t in buf[:6])
+            gdn3_scan(dq, dk, dv, db, dw, dd, decay_kind=decay_kind, rope=rope, algo=algo,
+                      braid_rates=braid_rates, braid_clamp=braid_clamp, out=buf[6][:n])
+            done_scan[i].record(main)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done_scan[i])
+                out[b0:b1].copy_(buf[6][:n], non_blocking=True)
+                done_out[i].record(d2h)
+        main.wait_event(done_out[nsl - 1])
+        main.wait_stream(h2d)
+    return out
+
+
 def _cached_workspace(device, need):
     key = (device.index, _stream(device))
     ws = _WORKSPACES.get(key)

@@ -132,3 +132,16 @@ def test_default_and_allocation_free_paths_agree():
     y2 = torch.empty_like(y1)
     ops.gdn3_scan_noalloc(*args, decay_kind="log", rope=rope, out=y2)
     assert rel(y1, y2) < TOL16
+
+
+def test_host_to_host_pipelined_scan_matches_device_scan():
+    """ops.gdn3_scan_host (sliced, copies overlapped on three streams) == ops.gdn3_scan."""
+    B, T, H, M, K = 5, 200, 2, 4, 128
+    inp = scan_inputs(B, T, H, M, K, K, seed=78)
+    host = [_bf(inp[n]).pin_memory() for n in ("q", "k", "v", "beta", "beta", "logg")]
+    rope = lane_rope(M, K, K, 0.5)
+    out = torch.empty(B, T, H, M, K, dtype=torch.bfloat16).pin_memory()
+    ops.gdn3_scan_host(*host, out=out, device=DEV, slices=3, decay_kind="log", rope=rope)
+    torch.cuda.synchronize()
+    ref = ops.gdn3_scan(*[t.to(DEV) for t in host], decay_kind="log", rope=rope)
+    assert torch.equal(out, ref.cpu())
