@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   float* sL = reinterpret_cast<float*>(sm + P_OFF_SC);  // [2][64] log2 decay prefix
   float* sCE = sL + 128;                                // T_e column factor ce_l 2^{L_l}
   float* sCW = sL + 256;
+  float* sKN = sL + 384;  // |k|^2
   float* sInv = sL + 512;
   float* sNE = sL + 576;  // [2][64] 2^{-L_l}
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_OFF_BAR);
@@ -245,10 +246,9 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   // Mq^T row (k_j.q_i)
   const int quad = warp & 3, half = warp >> 2;
   const int r = quad * 32 + lane, ci = r >> 6, j = r & 63;
-  const bool arow = half == (ci == 0 ? 1 : 0);
   const int64_t tj = tbase + ci * C + j;
   float be = 0.f, bw = 0.f;
-  if (arow && tj < a.T) {
+  if (tj < a.T) {
     be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tj, h, m));
     bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tj, h, m));
   }
@@ -312,58 +312,71 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   if (ok) ok = tc::mbar_wait(mbar, 0);
   ok = !__syncthreads_or(!ok);
   tc::fence_after();
-  float d[64];
+  // TMEM columns: chunk a = [Ka Qa^T | Ka Ka^T] (0-127), chunk b = [Kb Kb^T | Kb Qb^T] (128-255)
+  const uint32_t lrow = (uint32_t)(quad * 32) << 16;
+  const uint32_t col_kk = ci == 0 ? 64u : 128u, col_kq = ci == 0 ? 0u : 192u;
+  const float* L = sL + ci * C;
+  const float* NE = sNE + ci * C;
+  const bool fold = L[C - 1] >= FOLD_MIN_LC;  // uniform per chunk, i.e. per warp
+  const float Lj = L[j];
+  // masks, all warps: this thread's half (32 columns) of row j of k k^T
+  float d[32];
   if (ok) {
-    const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(128 * ci + 64 * half);
-    tc::tmem_ld32(ta, d);
-    tc::tmem_ld32(ta + 32, d + 32);
-  }
-  tc::fence_before();
-  __syncthreads();  // the tiles are free from here: A and the Mq^T staging go over them
-  if (warp == 0) {
-    tc::fence_after();
-    tc::tmem_dealloc(tmem, 256);
-  }
-  if (ok) {
-    const float* L = sL + ci * C;
-    const float* NE = sNE + ci * C;
-    const bool fold = L[C - 1] >= FOLD_MIN_LC;  // uniform per chunk, i.e. per warp
-    const float Lj = L[j];
-    if (arow) {
-      // masks: A[j][l] = ce_j 2^{L_j - L_l} (k_j.k_l) for l < j; |k_j|^2 is the diagonal
-      float cej = 0.f, cwj = 0.f;
-      if (tj < a.T) {
-        if (P.kmd2) {
-          cej = be;
-          cwj = bw;
-        } else {
-          float kn = 0.f;  // |k_j|^2 = d[j] (selected without a dynamic register index)
+    tc::tmem_ld32(tmem + lrow + col_kk + 32 * half, d);
+    if ((j >> 5) == half) {  // |k_j|^2 is the diagonal (selected without a dynamic register index)
+      float kn = 0.f;
 #pragma unroll
-          for (int e = 0; e < 64; ++e) kn = (e == j) ? d[e] : kn;
-          const float al = stable_alpha(be * kn);
-          cej = al * be;
-          cwj = al * bw;
-        }
+      for (int e = 0; e < 32; ++e) kn = (e == (j & 31)) ? d[e] : kn;
+      sKN[ci * C + j] = kn;
+    }
+  }
+  __syncthreads();
+  if (ok) {
+    // A[j][l] = ce_j 2^{L_j - L_l} (k_j.k_l) for l < j
+    float cej = 0.f, cwj = 0.f;
+    if (tj < a.T) {
+      if (P.kmd2) {
+        cej = be;
+        cwj = bw;
+      } else {
+        const float al = stable_alpha(be * sKN[ci * C + j]);
+        cej = al * be;
+        cwj = al * bw;
       }
-      const float ej = fast_exp2(Lj);
+    }
+    const float ej = fast_exp2(Lj);
+    if (half == 0) {
       sCE[ci * C + j] = cej * ej;
       sCW[ci * C + j] = cwj;
-      const float rj = cej * ej;  // 2^{L_j - L_l} as 2^{L_j} 2^{-L_l} on folded chunks
-      float* Arow = sA + (ci * C + j) * LDA;
+    }
+    const float rj = cej * ej;  // 2^{L_j - L_l} as 2^{L_j} 2^{-L_l} on folded chunks
+    float* Arow = sA + (ci * C + j) * LDA + 32 * half;
 #pragma unroll
-      for (int e = 0; e < 64; e += 4) {
-        float g[4];
+    for (int e = 0; e < 32; e += 4) {
+      float g[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int l = e + u;
-          const float w = fold ? rj * NE[l] : cej * fast_exp2(Lj - L[l]);
-          g[u] = (l < j) ? w * d[l] : 0.f;
-        }
-        *reinterpret_cast<float4*>(Arow + e) = make_float4(g[0], g[1], g[2], g[3]);
+      for (int u = 0; u < 4; ++u) {
+        const int l = 32 * half + e + u;
+        const float w = fold ? rj * NE[l] : cej * fast_exp2(Lj - L[l]);
+        g[u] = (l < j) ? w * d[e + u] : 0.f;
       }
+      *reinterpret_cast<float4*>(Arow + e) = make_float4(g[0], g[1], g[2], g[3]);
+    }
+  }
+  __syncthreads();
+  // T = (I + A)^{-1} by 32 x 32 blocks: T11, T22 by substitution (warps 0-3) while
+  // warps 4-7 form the Mq^T rows; then R = A21 T11 and T21 = -T22 R (all warps)
+  if (ok) {
+    if (warp < 4) {
+      float* A = sA + (warp >> 1) * C * LDA;
+      if (warp & 1) subst_block<32>(A, lane);
+      else subst_block<0>(A, lane);
     } else {
       // Mq^T row l = j: Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for i >= l (2^{-L_l} q_i.k_l on
       // folded chunks); rows l, 64 i: the MN-major B operand of y += W^T Mq^T
+      float e64[64];
+      tc::tmem_ld32(tmem + lrow + col_kq, e64);
+      tc::tmem_ld32(tmem + lrow + col_kq + 32, e64 + 32);
       char* mqt = reinterpret_cast<char*>(sm + P_OFF_MQS + ci * 8192);
       const float nej = NE[j];
 #pragma unroll
@@ -372,14 +385,19 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int i = 8 * c8 + e;
-          v[e] = (i >= j) ? (fold ? nej : fast_exp2(L[i] - Lj)) * d[i] : 0.f;
+          v[e] = (i >= j) ? (fold ? nej : fast_exp2(L[i] - Lj)) * e64[i] : 0.f;
         }
         tc::st_chunk_bf16(mqt, tc::sw128(j, c8, C), v);
       }
+      tc::fence_async_smem();
     }
   }
-  tc::fence_async_smem();
+  tc::fence_before();
   __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, 256);
+  }
   if (!ok) {
     if (tid == 0 && P.err) atomicExch(P.err, (int)GDNX_ETIMEOUT);
     return;
@@ -391,13 +409,6 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
         bulk_store(P.tt + (n * P.nchunks + chn) * TT_ELEMS + 2 * C * C, tc::smem_u32(sm + P_OFF_MQS + c2 * 8192), 8192);
     }
     bulk_commit();
-  }
-  // T = (I + A)^{-1} by 32 x 32 blocks: T11, T22 by substitution (warps 0-3),
-  // then R = A21 T11 and T21 = -T22 R (all warps, 8 rows each).
-  if (warp < 4) {
-    float* A = sA + (warp >> 1) * C * LDA;
-    if (warp & 1) subst_block<32>(A, lane);
-    else subst_block<0>(A, lane);
   }
   __syncthreads();
   float* A = sA + (warp >> 2) * C * LDA;
