@@ -26,9 +26,9 @@
 //       G3  y_W = W^T Mq^T,  S += W'^T K                    (K read MN-major)
 //     with the fp32 state in TMEM for the whole sequence.
 // The state is kept as S = 2^{ls} S_tmem with a running log2 scale ls, so the
-// per-chunk decay 2^{L_C} is folded into the bf16 operands instead of a TMEM
-// read-modify-write; when ls + L_C would drop below -40 the scale is applied
-// to TMEM and reset.  Every mbarrier wait is bounded (GDNX_ETIMEOUT in the
+// per-chunk decay 2^{L_C} is folded into scalars of the read-outs instead of a
+// TMEM read-modify-write; the scale is applied to TMEM and reset when ls < -40
+// and on chunks that take the exact path (see FOLD_MIN_LC).  Every mbarrier wait is bounded (GDNX_ETIMEOUT in the
 // workspace error word, TMEM freed, kernel returns).
 #include <cuda.h>
 #include <mutex>
@@ -49,10 +49,14 @@ constexpr int VD = 128;
 constexpr int LDA = 68;                    // fp32 row stride of the A matrices (16-byte rows)
 constexpr int64_t TT_ELEMS = 3 * C * C;    // bf16 elements of T_e, T_w, Mq^T per chain-chunk
 constexpr size_t ERR_BYTES = 256;
-// Chunks whose total log2 decay L_C is at least this take the folded path: pass 1
-// stores Mq'_il = 2^{-L_l} q_i.k_l (j <= i) and pass 2 scales y_i by 2^{L_i} on the
-// way out, so q is used unscaled; below it, pass 1 stores Mq_il = 2^{L_i - L_l} q_i.k_l
-// and pass 2 forms Qd = 2^{L} q in shared memory (2^{-L_l} <= 2^60 on the folded path).
+// Chunks whose total log2 decay L_C is at least this take the folded path: the chunk's
+// decays go into scalars of the read-outs instead of passes over q and k.  With the
+// state held as 2^{ls} S_tmem (ls in [-40, 0] at the chunk start), pass 1 stores the
+// undecayed mask Mq_il = q_i.k_l (l <= i), pass 2 writes -Wk 2^{ls} as the G2 operand,
+// reads W out as W diag(f), f_l = 2^{-L_l - ls} (<= 2^100), updates S_tmem += (W diag f)^T K
+// and scales y_i by 2^{L_i + ls}.  Below it (the exact path), the state is normalised
+// to ls = 0 and scaled by 2^{L_C} in TMEM, pass 1 stores Mq_il = 2^{L_i - L_l} q_i.k_l and
+// pass 2 forms Qd = 2^{L} q and K' = 2^{L_C - L} k in shared memory.
 constexpr float FOLD_MIN_LC = -60.f;
 
 struct WyScanMaps {
@@ -372,20 +376,19 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
       if (warp & 1) subst_block<32>(A, lane);
       else subst_block<0>(A, lane);
     } else {
-      // Mq^T row l = j: Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for i >= l (2^{-L_l} q_i.k_l on
+      // Mq^T row l = j: Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for i >= l (q_i.k_l undecayed on
       // folded chunks); rows l, 64 i: the MN-major B operand of y += W^T Mq^T
       float e64[64];
       tc::tmem_ld32(tmem + lrow + col_kq, e64);
       tc::tmem_ld32(tmem + lrow + col_kq + 32, e64 + 32);
       char* mqt = reinterpret_cast<char*>(sm + P_OFF_MQS + ci * 8192);
-      const float nej = NE[j];
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int i = 8 * c8 + e;
-          v[e] = (i >= j) ? (fold ? nej : fast_exp2(L[i] - Lj)) * e64[i] : 0.f;
+          v[e] = (i >= j) ? (fold ? e64[i] : fast_exp2(L[i] - Lj) * e64[i]) : 0.f;
         }
         tc::st_chunk_bf16(mqt, tc::sw128(j, c8, C), v);
       }
@@ -567,8 +570,8 @@ __global__ void __launch_bounds__(S_NT, 1)
     wy_scan_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
   extern __shared__ uint8_t smraw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
-  float* sEL = reinterpret_cast<float*>(sm + S_OFF_PSC);  // [2][64] 2^{L_j}
-  float* sFK = sEL + 128;                                  // [2][64] K' factors
+  float* sEL = reinterpret_cast<float*>(sm + S_OFF_PSC);  // [2][64] y factors / Qd factors
+  float* sFK = sEL + 128;                                  // [2][64] W factors / K' factors
   float4* sSF = reinterpret_cast<float4*>(sm + S_OFF_SF);
   float* sInv = reinterpret_cast<float*>(sm + S_OFF_INV);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S_OFF_BAR);
@@ -673,7 +676,8 @@ __global__ void __launch_bounds__(S_NT, 1)
       const int s = (int)(ch & 1);
       bool ok = wait_or_abort(ready + s, (uint32_t)((ch >> 1) & 1), s_abort);
       if (group_any(2, !ok)) break;
-      // state -> bf16 operand (true scale); rescale TMEM when due
+      // S_tmem -> bf16 operand (times 2^ls when the chunk normalises the state), and the
+      // TMEM write-back of a normalisation (exact path: also the chunk decay 2^{L_C})
       {
         const float4 sf = sSF[s];
 #pragma unroll
@@ -710,22 +714,6 @@ __global__ void __launch_bounds__(S_NT, 1)
         }
         tc::commit(g2);
       }
-      // while G2 runs: K' = diag(f) K in place (rows 0-63; G1 has consumed K)
-      {
-        char* kqp = reinterpret_cast<char*>(sm + kq_off(s));
-        const float* f = sFK + 64 * s;
-        for (int it = tid; it < C * 16; it += G_NT) {
-          const int r = it >> 4, cc = it & 15;
-          const uint32_t off = tc::sw128(r, cc, 192);
-          float x[8];
-          load8_bf16(kqp + off, 0, x);
-          const float fr = f[r];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] *= fr;
-          tc::st_chunk_bf16(kqp, off, x);
-        }
-      }
-      tc::fence_async_smem();
       ok = wait_or_abort(g2, (uint32_t)(ch & 1), s_abort);
       tc::fence_after();
       if (group_any(2, !ok)) break;
@@ -733,6 +721,11 @@ __global__ void __launch_bounds__(S_NT, 1)
       {
         float w[32];
         tc::tmem_ld32(tmem + (s ? T_W1 : T_W0) + lbase + 32 * half, w);
+        if (sSF[s].w != 0.f) {  // folded chunk: W diag(f)
+          const float* f = sFK + 64 * s + 32 * half;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) w[e] *= f[e];
+        }
         char* wt = reinterpret_cast<char*>(sm + S_OFF_WT);
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(wt, tc::sw128(row, 4 * half + q4, 128), w + 8 * q4);
@@ -740,7 +733,8 @@ __global__ void __launch_bounds__(S_NT, 1)
       tc::fence_async_smem();
       tc::fence_before();
       if (group_any(2, *s_abort != 0)) break;
-      // G3: [y | S] or [S | y] += W^T [Mq^T | K'] / [K' | Mq^T]   (B MN-major)
+      // G3: [y | S] or [S | y] += W^T [Mq^T | K] / [K | Mq^T]   (B MN-major; W^T carries the
+      // decay factors on folded chunks, K carries them on the exact path)
       if (tid == 0) {
         tc::fence_after();
         const uint32_t d = tmem + (s ? T_S : T_Y0);
@@ -770,7 +764,7 @@ __global__ void __launch_bounds__(S_NT, 1)
       const bool ok = wait_or_abort(g3 + sp, (uint32_t)((c >> 1) & 1), s_abort);
       tc::fence_after();
       if (group_any(1, !ok)) return false;
-      const bool folded = sSF[sp].w != 0.f;  // y_i = 2^{L_i} (S0 q_i + sum_l Mq'_il W_l)
+      const bool folded = sSF[sp].w != 0.f;  // y_i = 2^{L_i + ls} y_tmem on folded chunks
       const uint32_t ty = tmem + (sp ? T_Y1 : T_Y0);
       if (maps.y_tma) {
         // rows v (TMEM lanes) x tokens i -> [token][v] swizzled tiles: 16x256b loads give
@@ -827,15 +821,21 @@ __global__ void __launch_bounds__(S_NT, 1)
       if (group_any(1, !ok)) { alive = false; break; }
       const float* Lst = reinterpret_cast<const float*>(sm + S_OFF_L + s * 256);
       const float Lc = Lst[C - 1];
-      const bool rescale = ls + Lc < -40.f;
       const bool fold = Lc >= FOLD_MIN_LC;
-      if (ptid < 64) {  // K' = f K (the S update's operand); 2^L for Qd or for y
+      // normalise the state (S_tmem *= 2^ls, ls = 0) when ls < -40, and always on the exact path
+      const bool norm = !fold || ls < -40.f;
+      const float lsc = norm ? 0.f : ls;  // ls during this chunk
+      const float wk_mult = fold ? exp2f(lsc) : 1.f;
+      if (ptid < 64) {
         const float Lj = Lst[ptid];
-        sEL[64 * s + ptid] = exp2f(Lj);
-        sFK[64 * s + ptid] = rescale ? exp2f(Lc - Lj) : exp2f(-Lj - ls);
+        sEL[64 * s + ptid] = fold ? exp2f(Lj + lsc) : exp2f(Lj);    // y factor / Qd factor
+        sFK[64 * s + ptid] = fold ? exp2f(-Lj - lsc) : exp2f(Lc - Lj);  // W factor / K' factor
       }
-      if (ptid == 0) sSF[s] = make_float4(exp2f(ls), exp2f(ls + Lc), rescale ? 1.f : 0.f, fold ? 1.f : 0.f);
-      ls = rescale ? 0.f : ls + Lc;
+      // S read-out: bf16 operand factor, TMEM write-back factor, write-back flag, folded flag
+      if (ptid == 0)
+        sSF[s] = make_float4(norm ? exp2f(ls) : 1.f, fold ? exp2f(ls) : exp2f(ls + Lc), norm ? 1.f : 0.f,
+                             fold ? 1.f : 0.f);
+      ls = fold ? lsc + Lc : 0.f;
       // lane RoPE of token j's k (row j) and q (row qr + j) in place, one set of angles
       for (int it = ptid; it < C * dch; it += G_NT) {
         const int j = it / dch, cc = it - j * dch;
@@ -891,13 +891,15 @@ __global__ void __launch_bounds__(S_NT, 1)
       tc::fence_after();
       if (ptid == 0) bulk_wait_read();  // y stores of chunk ch - 2 have read the -Wk rows
       if (group_any(1, !ok)) { alive = false; break; }
-      if (!fold) {  // exact path: Qd = 2^{L_i} q_i in place
-        for (int it = ptid; it < C * 16; it += G_NT) {
+      if (!fold) {  // exact path: Qd = 2^{L_i} q_i and K' = 2^{L_C - L_j} k_j in place (G1 has read K)
+        for (int it = ptid; it < 2 * C * 16; it += G_NT) {
           const int r = it >> 4, cc = it & 15;
-          const uint32_t off = tc::sw128(qr + r, cc, 192);
+          const bool isq = r >= C;
+          const int rr = r & 63;
+          const uint32_t off = tc::sw128(isq ? qr + rr : rr, cc, 192);
           float x[8];
           load8_bf16(kq + off, 0, x);
-          const float f = sEL[64 * s + r];
+          const float f = isq ? sEL[64 * s + rr] : sFK[64 * s + rr];
 #pragma unroll
           for (int e = 0; e < 8; ++e) x[e] *= f;
           tc::st_chunk_bf16(kq, off, x);
@@ -912,7 +914,7 @@ __global__ void __launch_bounds__(S_NT, 1)
         for (int hh = 0; hh < 2; ++hh) {
           tc::tmem_ld32(tmem + T_WK + lbase + 64 * half + 32 * hh, d);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) d[e] = -d[e];
+          for (int e = 0; e < 32; ++e) d[e] = -d[e] * wk_mult;
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(base, tc::sw128(wr + row, 4 * hh + q4, 192), d + 8 * q4);
         }
