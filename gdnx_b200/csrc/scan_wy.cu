@@ -722,9 +722,15 @@ __global__ void __launch_bounds__(S_NT, 1)
         float w[32];
         tc::tmem_ld32(tmem + (s ? T_W1 : T_W0) + lbase + 32 * half, w);
         if (sSF[s].w != 0.f) {  // folded chunk: W diag(f)
-          const float* f = sFK + 64 * s + 32 * half;
+          const float4* f4 = reinterpret_cast<const float4*>(sFK + 64 * s + 32 * half);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) w[e] *= f[e];
+          for (int e = 0; e < 8; ++e) {
+            const float4 f = f4[e];
+            w[4 * e] *= f.x;
+            w[4 * e + 1] *= f.y;
+            w[4 * e + 2] *= f.z;
+            w[4 * e + 3] *= f.w;
+          }
         }
         char* wt = reinterpret_cast<char*>(sm + S_OFF_WT);
 #pragma unroll
