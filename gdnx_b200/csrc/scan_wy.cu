@@ -1024,6 +1024,11 @@ size_t wy_workspace_bytes(const gdnx_scan_args& a) {
 }
 
 gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st) {
+  // TMA coordinates are 32-bit and pass 1 runs one CTA per (chain, chunk pair)
+  const int64_t n_chains = a.B * a.H * a.M, n_pairs = ((a.T + C - 1) / C + 1) / 2;
+  if (a.T > (int64_t(1) << 30) || a.B > (int64_t(1) << 30) || a.H > (int64_t(1) << 30) ||
+      n_chains * n_pairs > int64_t(0x7fffffff))
+    return GDNX_EUNSUPPORTED;
   WyScanMaps maps;
   if (!make_map(a.q, a, &maps.q, &maps.use_m[0]) || !make_map(a.k, a, &maps.k, &maps.use_m[1]) ||
       !make_map(a.v, a, &maps.v, &maps.use_m[2]))

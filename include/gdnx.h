@@ -140,7 +140,12 @@ typedef struct {
  * (gdn3/kmd2_native.py:97-132). */
 GDNX_API gdnx_status gdnx_scan_fwd(const gdnx_scan_args* args, void* stream);
 
-/* Workspace the chosen kernel of gdnx_scan_fwd needs (0 if none). */
+/* Workspace the chosen kernel of gdnx_scan_fwd needs (0 if none).  For the
+ * chunked tensor-core path it holds a 256-byte error word followed by the
+ * per-chunk tiles of the parallel pass (24.25 KB per chain and 64-token chunk).
+ * The first int32 of the workspace is cleared on the stream by every call and
+ * is GDNX_ETIMEOUT after the call if a kernel gave up waiting (its outputs are
+ * then invalid); reading it is optional and costs a synchronisation. */
 GDNX_API size_t gdnx_scan_workspace_bytes(const gdnx_scan_args* args);
 
 /* Allocation-free chunked scan.  No counterpart in the reference.
