@@ -43,6 +43,12 @@ def chunk_flops_per_chain_token(dk, dv, C):
     return 6 * dk * dv + 2 * C * (3 * dk + 2 * dv)
 
 
+def kr_flops_per_chain_token(P, R=4, av=16, ak=16, bv=8, bk=8, K=128, V=128):
+    """GDN3-KR algorithmic FLOPs per chain-token with chunk = compaction period P."""
+    f_compact = 2 * R * (av * ak) * (bv * bk) + 2 * V * K * P + 2 * (1 + 2 * 2) * (av * ak) * (bv * bk) * (R + 4)
+    return 4 * R * (av * ak * bk + av * bk * bv) + 4 * P * (K + V) + 2 * P * (2 * K + V) + f_compact / P
+
+
 def prefill_bytes(c):
     """q,k,v read once per head (bf16), beta + log-decay per lane (bf16), bf16 per-lane outputs."""
     B, T, H, M, K, V = (c[x] for x in "BTHMKV")
@@ -205,6 +211,9 @@ def main():
     ap.add_argument("--prefill-B", type=int, default=None, help="override B (profiling runs only)")
     ap.add_argument("--prefill-T", type=int, default=None, help="override T (profiling runs only)")
     ap.add_argument("--decode-layers", type=int, default=None, help="override layers (profiling runs only)")
+    ap.add_argument("--no-config4", dest="config4", action="store_false", help="skip the config-4 sharded prefill leg")
+    ap.add_argument("--config4-T", type=int, default=None, help="override config-4 T (smoke runs only)")
+    ap.add_argument("--config4-slabs", type=int, default=8)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -299,6 +308,74 @@ def main():
                   "collective": "nccl all_gather_into_tensor"}
         del full
 
+    # ---------------- config 4: sharded prefill with a T-slab pipelined all-gather ----------------
+    cfg4 = None
+    if args.config4:
+        c4 = dict(B=64, T=8192, H=16, M=4, K=128, V=128, chunk=64)
+        if args.config4_T:
+            c4["T"] = args.config4_T
+        from gdnx_b200.distributed import shard_for
+        sh = shard_for(c4["B"], c4["H"], world, rank)
+        lc = dict(c4)
+        lc["B" if sh.axis == "batch" else "H"] = sh.stop - sh.start
+        inp4 = make_prefill_inputs(lc, dev, seed=4 + rank)
+        slabs = args.config4_slabs
+        Ts = lc["T"] // slabs
+        ybuf = [torch.empty(lc["B"], Ts, lc["H"], lc["M"], lc["V"], dtype=torch.bfloat16, device=dev)
+                for _ in range(2)]
+        gbuf = [torch.empty((world * lc["B"], Ts, lc["H"], lc["M"], lc["V"]), dtype=torch.bfloat16, device=dev)
+                for _ in range(2)] if dist else None
+        st = torch.zeros(lc["B"] * lc["H"] * lc["M"], lc["V"], lc["K"], dtype=torch.float32, device=dev)
+        comm = torch.cuda.Stream(dev)
+        ev_scan = [torch.cuda.Event() for _ in range(2)]
+        ev_comm = [torch.cuda.Event() for _ in range(2)]
+
+        def slab_scan(i, state):
+            sl = slice(i * Ts, (i + 1) * Ts)
+            _, so = ops.gdn3_scan(inp4["q"][:, sl], inp4["k"][:, sl], inp4["v"][:, sl], inp4["beta"][:, sl],
+                                  inp4["beta"][:, sl], inp4["logg"][:, sl], decay_kind="log",
+                                  rope=lane_rope(lc["M"], lc["K"], lc["K"], 0.5, pos0=i * Ts), state=state,
+                                  return_state=True, out=ybuf[i % 2])
+            return so
+
+        def scan_only():
+            state = st
+            for i in range(slabs):
+                state = slab_scan(i, state)
+
+        def scan_and_gather():
+            state = st
+            for i in range(slabs):
+                if i >= 2:
+                    stream.wait_event(ev_comm[i % 2])  # ybuf[i % 2] gathered
+                state = slab_scan(i, state)
+                if dist:
+                    ev_scan[i % 2].record(stream)
+                    with torch.cuda.stream(comm):
+                        comm.wait_event(ev_scan[i % 2])
+                        dist.all_gather_into_tensor(gbuf[i % 2], ybuf[i % 2])
+                        ev_comm[i % 2].record(comm)
+            if dist:
+                stream.wait_stream(comm)
+
+        ms4 = timed(scan_only, 3, 3, stream, barrier)
+        ms4e = timed(scan_and_gather, 3, 3, stream, barrier)
+        ms4g = None
+        if dist:
+            ms4g = timed(lambda: dist.all_gather_into_tensor(gbuf[0], ybuf[0]), 3, 1, stream, barrier) * slabs
+        vals = torch.tensor([ms4, ms4e, ms4g or 0.0], device=dev)
+        if dist:
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        ms4, ms4e, ms4g = vals.tolist()
+        tok4 = c4["B"] * c4["T"]
+        f4 = c4["B"] * c4["T"] * c4["H"] * c4["M"] * chunk_flops_per_chain_token(128, 128, 64)
+        cfg4 = {"workload": "config4: B=64,T=%d,H=16,M=4 sharded (batch x head) over %d rank(s)" % (c4["T"], world),
+                "scan_ms": ms4, "scan_tok_per_s": tok4 / (ms4 * 1e-3), "scan_tflops": f4 / (ms4 * 1e-3) / 1e12,
+                "allgather_ms_serial": ms4g if dist else None, "e2e_ms_pipelined": ms4e,
+                "e2e_tok_per_s": tok4 / (ms4e * 1e-3), "slabs": slabs,
+                "collective": "nccl all_gather_into_tensor per T-slab on a comm stream" if dist else None}
+        del inp4, ybuf, gbuf, st
+
     # ---------------- decode (config 3) ----------------
     decode = None
     if not args.no_decode:
@@ -357,7 +434,10 @@ def main():
                                  decay_kind="log", rope=rope)
 
             kms = timed(kstep, 2, 3, stream, barrier)
-            krs[f"P{P}"] = {"ms_per_call": kms, "tok_per_s": kc["B"] * kc["T"] * world / (kms * 1e-3)}
+            kf = kc["B"] * kc["T"] * kc["H"] * kc["M"] * kr_flops_per_chain_token(P)
+            krs[f"P{P}"] = {"ms_per_call": kms, "tok_per_s": kc["B"] * kc["T"] * world / (kms * 1e-3),
+                            "tflops_by_formula": kf / (kms * 1e-3) / 1e12,
+                            "tc_frac": kf / (kms * 1e-3) / 1e12 / peaks["bf16"]}
         kr = {"metric": "KR prefill tok/s (config 2)", "B": 1, "T": kc["T"], "H": 16, "M": 4,
               "state": "A 16x16 (x) B 8x8, R=4, + U,V 128xP, delta=0.97", **krs}
 
@@ -376,7 +456,7 @@ def main():
                            "l2": "inputs 402 MB + outputs 537 MB > 126 MB L2 (no flush)",
                            "parallelism": f"(batch x head) shards, dp{world}"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
-                "clocks": clocks, "decode": decode, "gather": gather, "kr": kr}
+                "clocks": clocks, "decode": decode, "gather": gather, "kr": kr, "config4": cfg4}
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
