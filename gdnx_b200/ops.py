@@ -225,6 +225,27 @@ def _cached_workspace(device, need):
     return ws
 
 
+def device_status(workspace: Optional[torch.Tensor] = None) -> int:
+    """Device-side status of scans that used ``workspace`` (default: every workspace this
+    module owns): the error word the kernels write when a bounded wait gives up
+    (``GDNX_ETIMEOUT``; their outputs are then invalid), 0 otherwise.  Synchronises."""
+    wss = [workspace] if workspace is not None else list(_WORKSPACES.values())
+    for ws in wss:
+        if ws is None or ws.numel() < 4:
+            continue
+        code = int(ws[:4].view(torch.int32).item())
+        if code:
+            return code
+    return 0
+
+
+def check_device_status(workspace: Optional[torch.Tensor] = None) -> None:
+    """Raise ``RuntimeError`` if :func:`device_status` reports an error."""
+    code = device_status(workspace)
+    if code:
+        raise RuntimeError("gdnx device error: " + L.load().gdnx_status_string(code).decode())
+
+
 def _run_scan(a, device, workspace):
     lib = L.load()
     need = lib.gdnx_scan_workspace_bytes(C.byref(a))

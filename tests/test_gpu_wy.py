@@ -145,3 +145,18 @@ def test_host_to_host_pipelined_scan_matches_device_scan():
     torch.cuda.synchronize()
     ref = ops.gdn3_scan(*[t.to(DEV) for t in host], decay_kind="log", rope=rope)
     assert torch.equal(out, ref.cpu())
+
+
+def test_device_status_word():
+    """The workspace error word is clear after a normal call and reported when set."""
+    B, T, H, M, K = 1, 70, 2, 4, 128
+    inp = scan_inputs(B, T, H, M, K, K, seed=79)
+    args = [_bf(inp[n]).to(DEV) for n in ("q", "k", "v", "beta", "beta", "logg")]
+    ws = torch.empty(1 << 24, dtype=torch.uint8, device=DEV)
+    ops.gdn3_scan(*args, decay_kind="log", algo="chunked", workspace=ws)
+    assert ops.device_status(ws) == 0
+    ws[:4].view(torch.int32).fill_(3)  # GDNX_ETIMEOUT, as a kernel that gave up would leave it
+    with pytest.raises(RuntimeError, match="gdnx device error"):
+        ops.check_device_status(ws)
+    ops.gdn3_scan(*args, decay_kind="log", algo="chunked", workspace=ws)  # every call clears it
+    assert ops.device_status(ws) == 0
