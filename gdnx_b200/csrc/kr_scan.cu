@@ -23,7 +23,9 @@
 //  * the Kronecker operator sum_r A_r (x) B_r is materialised densely in
 //    registers next to the residual whenever A, Bk change, so its read shares
 //    the residual's loads (its per-token decay is the scalar fac^2);
-//  * compaction runs in-kernel on shared memory (compact.cuh).
+//  * compaction runs in-kernel on shared memory (compact.cuh);
+//  * bf16 q/k/v rows of the next block of tokens are fetched with cp.async into
+//    a staging area while the current block's sequential updates run.
 #include "compact.cuh"
 #include "kernels.h"
 
@@ -77,6 +79,9 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   float* ropeC = misc + 32;                        // kTB x 64 (cos of this block's angles)
   float* ropeS = ropeC + kTB * 64;                 // kTB x 64
   float* sInv = ropeS + kTB * 64;                  // 64 inverse frequencies
+  // kTB tokens x (k, q, v) raw bf16 rows of the next block (16-byte aligned)
+  __nv_bfloat16* rawst =
+      reinterpret_cast<__nv_bfloat16*>((reinterpret_cast<uintptr_t>(sInv + 64) + 15) & ~uintptr_t(15));
 
   const int64_t n = blockIdx.x;
   const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
@@ -136,6 +141,31 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   rebuild();
   build_kron();
 
+  // asynchronous staging of bf16 q/k/v rows (16-byte aligned views only)
+  const bool raw_ok = a.k.dtype == GDNX_BF16 && a.q.dtype == GDNX_BF16 && a.v.dtype == GDNX_BF16 &&
+                      ((reinterpret_cast<uintptr_t>(a.k.ptr) | reinterpret_cast<uintptr_t>(a.q.ptr) |
+                        reinterpret_cast<uintptr_t>(a.v.ptr)) & 15) == 0 &&
+                      ((a.k.sb | a.k.st | a.k.sh | a.k.sm | a.q.sb | a.q.st | a.q.sh | a.q.sm | a.v.sb | a.v.st |
+                        a.v.sh | a.v.sm) & 7) == 0;
+  constexpr int kRowK = K / 8, kRowV = V / 8;  // 16-byte chunks per row
+  constexpr int kRawPer = 2 * K + V;           // bf16 elements per staged token
+  auto prefetch_raw = [&](int64_t ts) {
+    for (int idx = tid; idx < kTB * (2 * kRowK + kRowV); idx += kNT) {
+      const int tt = idx / (2 * kRowK + kRowV), c = idx - tt * (2 * kRowK + kRowV);
+      const int64_t t = ts + tt;
+      if (t >= a.T) continue;
+      const __nv_bfloat16* src;
+      if (c < kRowK) src = reinterpret_cast<const __nv_bfloat16*>(a.k.ptr) + view_off(a.k, b, t, h, m) + 8 * c;
+      else if (c < 2 * kRowK)
+        src = reinterpret_cast<const __nv_bfloat16*>(a.q.ptr) + view_off(a.q, b, t, h, m) + 8 * (c - kRowK);
+      else src = reinterpret_cast<const __nv_bfloat16*>(a.v.ptr) + view_off(a.v, b, t, h, m) + 8 * (c - 2 * kRowK);
+      const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(rawst + tt * kRawPer + 8 * c));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (raw_ok) prefetch_raw(0);
+
   int64_t t0 = 0;
   while (t0 < a.T) {
     int64_t nt64 = a.T - t0;
@@ -143,6 +173,10 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
     if (nt64 > Pn - p) nt64 = Pn - p;
     const int nt = (int)nt64;
     // ---------- stage A: RoPE angles of the block, then per-token vectors (one warp per token) ----------
+    if (raw_ok) {
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();
+    }
     if (dpairs > 0) {
       for (int idx = tid; idx < nt * dpairs; idx += kNT) {
         const int tt = idx / dpairs, i = idx - tt * dpairs;
@@ -157,9 +191,10 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       float* sh = tk + SMT::kTokH;
       float* sq = tk + SMT::kTokQ;
       const int64_t ko = view_off(a.k, b, t, h, m), qo = view_off(a.q, b, t, h, m);
+      const __nv_bfloat16* raw = rawst + tt * kRawPer;
       for (int i = lane; i < K; i += 32) {
-        sk[i] = ld_as_f32(a.k.ptr, a.k.dtype, ko + i);
-        sq[i] = ld_as_f32(a.q.ptr, a.q.dtype, qo + i);
+        sk[i] = raw_ok ? __bfloat162float(raw[i]) : ld_as_f32(a.k.ptr, a.k.dtype, ko + i);
+        sq[i] = raw_ok ? __bfloat162float(raw[K + i]) : ld_as_f32(a.q.ptr, a.q.dtype, qo + i);
       }
       __syncwarp();
       if (dpairs > 0) {
@@ -182,7 +217,7 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       const int64_t vo = view_off(a.v, b, t, h, m);
       for (int i = lane; i < V; i += 32) {
         const float wv = P.vec_w ? ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo + i) : bw;
-        tk[SMT::kTokU + i] = wv * ld_as_f32(a.v.ptr, a.v.dtype, vo + i);
+        tk[SMT::kTokU + i] = wv * (raw_ok ? __bfloat162float(raw[2 * K + i]) : ld_as_f32(a.v.ptr, a.v.dtype, vo + i));
       }
       if (lane == 0) {
         float* sc = tk + SMT::kTokSc;
@@ -202,6 +237,7 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       tok[tt * SMT::kTokPer + SMT::kTokUold + vv] = Ug[(int64_t)vv * Pn + p + tt];
     }
     __syncthreads();
+    if (raw_ok && t0 + nt < a.T) prefetch_raw(t0 + nt);  // the staging has been read
     // ---------- stage B: running decays (thread 0) ----------
     if (tid == 0) {
       float f = fac, pre = 1.f;
@@ -323,7 +359,7 @@ gdnx_status launch_kr(const KrParams& P, cudaStream_t st) {
   const CD d{};
   const size_t floats = (size_t)d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) + kMaxP +
                         kTB * KrSmem<K, V>::kTokPer + 2 * kTB * V + (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
-  const size_t smem = floats * sizeof(float);
+  const size_t smem = floats * sizeof(float) + (size_t)kTB * (2 * K + V) * 2 + 16;  // + bf16 staging
   auto fn = kr_scan_kernel<CD>;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GDNX_ELAUNCH;
