@@ -131,25 +131,47 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
     row_times(Z);           // Y = R Z
     __syncthreads();
   }
-  // Q = orth(Y): one warp, modified Gram-Schmidt with re-orthogonalisation.
-  if (warp == 0) {
-    for (int c = 0; c < q; ++c) {
+  // Q = orth(Y): classical Gram-Schmidt applied twice per column ("twice is enough"),
+  // one thread per row, each projection a block-wide reduction of <= 8 dot products.
+  {
+    float yr[kCompMaxQ], qr[kCompMaxQ];
+    const bool has = tid < m;
+#pragma unroll
+    for (int c = 0; c < kCompMaxQ; ++c) {
+      yr[c] = has ? Y[tid * q + c] : 0.f;
+      qr[c] = 0.f;
+    }
+    float* part = red;  // [8 warps][8]
+#pragma unroll
+    for (int c = 0; c < kCompMaxQ; ++c) {
+      if (c >= q) break;
+#pragma unroll
       for (int pass = 0; pass < 2; ++pass) {
-        for (int p = 0; p < c; ++p) {
-          float dot = 0.f;
-          for (int i = lane; i < m; i += 32) dot += Qm[i * q + p] * Y[i * q + c];
-          dot = warp_sum(dot);
-          for (int i = lane; i < m; i += 32) Y[i * q + c] -= dot * Qm[i * q + p];
-          __syncwarp();
+        if (c == 0) break;
+        float dp[kCompMaxQ];
+#pragma unroll
+        for (int p = 0; p < kCompMaxQ; ++p) dp[p] = p < c ? warp_sum(qr[p] * yr[c]) : 0.f;
+        __syncthreads();
+        if (lane == 0)
+#pragma unroll
+          for (int p = 0; p < kCompMaxQ; ++p) part[warp * 8 + p] = dp[p];
+        __syncthreads();
+#pragma unroll
+        for (int p = 0; p < kCompMaxQ; ++p) {
+          if (p >= c) break;
+          float dsum = 0.f;
+          for (int w = 0; w < nt / 32; ++w) dsum += part[w * 8 + p];
+          yr[c] = fmaf(-dsum, qr[p], yr[c]);
         }
       }
-      float nn = 0.f;
-      for (int i = lane; i < m; i += 32) nn += Y[i * q + c] * Y[i * q + c];
-      nn = warp_sum(nn);
+      const float nn = block_sum(yr[c] * yr[c], red + 48);
       const float inv = nn > 1e-30f ? rsqrtf(nn) : 0.f;
-      for (int i = lane; i < m; i += 32) Qm[i * q + c] = Y[i * q + c] * inv;
-      __syncwarp();
+      qr[c] = yr[c] * inv;
     }
+    if (has)
+#pragma unroll
+      for (int c = 0; c < kCompMaxQ; ++c)
+        if (c < q) Qm[tid * q + c] = qr[c];
   }
   __syncthreads();
   // Bm = Q^T R   (q x n), Bm[c][j]
@@ -176,24 +198,39 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
     fro = warp_sum(fro);
     for (int sweep = 0; sweep < 30; ++sweep) {
       float off = 0.f;
+      // rounds s = 1..7 rotate the four disjoint pairs (i, i ^ s): their column dot
+      // products are reduced together
 #pragma unroll
-      for (int i = 0; i < kCompMaxQ - 1; ++i) {
+      for (int sr = 1; sr < kCompMaxQ; ++sr) {
+        float al[kCompMaxQ / 2], be[kCompMaxQ / 2], ga[kCompMaxQ / 2];
 #pragma unroll
-        for (int j = i + 1; j < kCompMaxQ; ++j) {
-          if (j >= q) continue;
-          float al = w0[i] * w0[i] + w1[i] * w1[i];
-          float be = w0[j] * w0[j] + w1[j] * w1[j];
-          float ga = w0[i] * w0[j] + w1[i] * w1[j];
+        for (int u = 0, i = 0; i < kCompMaxQ; ++i) {
+          const int j = i ^ sr;
+          if (j < i) continue;
+          al[u] = w0[i] * w0[i] + w1[i] * w1[i];
+          be[u] = w0[j] * w0[j] + w1[j] * w1[j];
+          ga[u] = w0[i] * w0[j] + w1[i] * w1[j];
+          ++u;
+        }
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {  // three reductions interleaved
-            al += __shfl_xor_sync(0xffffffffu, al, o);
-            be += __shfl_xor_sync(0xffffffffu, be, o);
-            ga += __shfl_xor_sync(0xffffffffu, ga, o);
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+          for (int u = 0; u < kCompMaxQ / 2; ++u) {
+            al[u] += __shfl_xor_sync(0xffffffffu, al[u], o);
+            be[u] += __shfl_xor_sync(0xffffffffu, be[u], o);
+            ga[u] += __shfl_xor_sync(0xffffffffu, ga[u], o);
           }
-          const float nrm = sqrtf(al * be);
-          if (nrm <= 1e-37f || fabsf(ga) <= 1e-6f * nrm || fabsf(ga) <= 1e-9f * fro) continue;
-          off = fmaxf(off, fabsf(ga) / nrm);
-          const float zeta = (be - al) / (2.f * ga);
+        }
+#pragma unroll
+        for (int u = 0, i = 0; i < kCompMaxQ; ++i) {
+          const int j = i ^ sr;
+          if (j < i) continue;
+          const int uu = u++;
+          if (j >= q) continue;
+          const float nrm = sqrtf(al[uu] * be[uu]);
+          if (nrm <= 1e-37f || fabsf(ga[uu]) <= 1e-6f * nrm || fabsf(ga[uu]) <= 1e-9f * fro) continue;
+          off = fmaxf(off, fabsf(ga[uu]) / nrm);
+          const float zeta = (be[uu] - al[uu]) / (2.f * ga[uu]);
           const float t = copysignf(1.f, zeta) / (fabsf(zeta) + sqrtf(1.f + zeta * zeta));
           const float cs = rsqrtf(1.f + t * t);
           const float sn = cs * t;
