@@ -221,19 +221,32 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
             ga[u] += __shfl_xor_sync(0xffffffffu, ga[u], o);
           }
         }
+        // rotation parameters of the four pairs, branch-free (a skipped pair gets cs = 1,
+        // sn = 0) so the pairs' dependent chains interleave
+        float csv[kCompMaxQ / 2], snv[kCompMaxQ / 2];
 #pragma unroll
         for (int u = 0, i = 0; i < kCompMaxQ; ++i) {
           const int j = i ^ sr;
           if (j < i) continue;
           const int uu = u++;
-          if (j >= q) continue;
-          const float nrm = sqrtf(al[uu] * be[uu]);
-          if (nrm <= 1e-37f || fabsf(ga[uu]) <= 1e-6f * nrm || fabsf(ga[uu]) <= 1e-9f * fro) continue;
-          off = fmaxf(off, fabsf(ga[uu]) / nrm);
-          const float zeta = (be[uu] - al[uu]) / (2.f * ga[uu]);
-          const float t = copysignf(1.f, zeta) / (fabsf(zeta) + sqrtf(1.f + zeta * zeta));
-          const float cs = rsqrtf(1.f + t * t);
-          const float sn = cs * t;
+          // thresholds on squares (no square roots): ga^2 against 1e-12 al be
+          const float p2 = al[uu] * be[uu], g2 = ga[uu] * ga[uu];
+          const bool rot = j < q && p2 > 1e-37f && g2 > 1e-12f * p2 && fabsf(ga[uu]) > 1e-9f * fro;
+          off = rot ? fmaxf(off, __fdividef(g2, p2)) : off;
+          // the sweep corrects rotation-parameter rounding; |2 ga| > 1e-6 sqrt(al be) keeps zeta in range
+          const float zeta = __fdividef(be[uu] - al[uu], 2.f * ga[uu]);
+          const float w1z = fmaf(zeta, zeta, 1.f);
+          const float t = copysignf(__fdividef(1.f, fabsf(zeta) + w1z * rsqrtf(w1z)), zeta);
+          const float cs = rsqrtf(fmaf(t, t, 1.f));
+          csv[uu] = rot ? cs : 1.f;
+          snv[uu] = rot ? cs * t : 0.f;
+        }
+#pragma unroll
+        for (int u = 0, i = 0; i < kCompMaxQ; ++i) {
+          const int j = i ^ sr;
+          if (j < i) continue;
+          const int uu = u++;
+          const float cs = csv[uu], sn = snv[uu];
           float a0 = w0[i], b0 = w0[j], a1 = w1[i], b1 = w1[j];
           w0[i] = cs * a0 - sn * b0; w0[j] = sn * a0 + cs * b0;
           w1[i] = cs * a1 - sn * b1; w1[j] = sn * a1 + cs * b1;
@@ -241,7 +254,7 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
           jr[i] = cs * ja - sn * jb; jr[j] = sn * ja + cs * jb;
         }
       }
-      if (off < 2e-6f) break;  // columns orthogonal to fp32 working accuracy
+      if (off < 4e-12f) break;  // (ga^2 / al be) < (2e-6)^2: columns orthogonal to fp32 working accuracy
     }
     // singular values, descending order (selection; q <= 8)
     float sv[kCompMaxQ];
