@@ -358,15 +358,30 @@ GDNX_DEV void add_residual_rmat(float* Rm, const float* U, const float* Vb, cons
       tileV[idx] = pp < np ? Vb[(int64_t)kk * P + p0 + pp] * (dsl ? dsl[p0 + pp] : 1.f) : 0.f;
     }
     __syncthreads();
+    // element e of this thread is (v = tid / K + (threads / K) e, k = tid % K): its key row of
+    // the tile is the same for every e, so it is held in registers
+    constexpr int KK = CD::a_k * CD::b_k;
+    static_assert(kCompThreads % KK == 0, "thread -> key mapping");
+    const int kk = tid % KK, v0 = tid / KK;
+    float tv[kCompPT];
+#pragma unroll
+    for (int pp = 0; pp < kCompPT; pp += 4) {
+      const float4 t4 = *reinterpret_cast<const float4*>(tileV + kk * kCompPT + pp);
+      tv[pp] = t4.x; tv[pp + 1] = t4.y; tv[pp + 2] = t4.z; tv[pp + 3] = t4.w;
+    }
 #pragma unroll
     for (int e = 0; e < 64; ++e) {
       if (e >= per) break;
-      const int idx = tid + kCompThreads * e;
-      if (idx >= V * K) break;
-      const int vv = idx / K, kk = idx % K;
+      const int vv = v0 + (kCompThreads / KK) * e;
       float s = acc[e];
 #pragma unroll
-      for (int pp = 0; pp < kCompPT; ++pp) s = fmaf(tileU[vv * kCompPT + pp], tileV[kk * kCompPT + pp], s);
+      for (int pp = 0; pp < kCompPT; pp += 4) {
+        const float4 u4 = *reinterpret_cast<const float4*>(tileU + vv * kCompPT + pp);
+        s = fmaf(u4.x, tv[pp], s);
+        s = fmaf(u4.y, tv[pp + 1], s);
+        s = fmaf(u4.z, tv[pp + 2], s);
+        s = fmaf(u4.w, tv[pp + 3], s);
+      }
       acc[e] = s;
     }
   }
