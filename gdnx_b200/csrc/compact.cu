@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(kThreads) compact_kernel(const CompParams P) {
   float* A_s = work + compact_work_floats();
   float* B_s = A_s + d.R * d.m;
   float* tileU = B_s + d.R * d.n;
-  float* tileV = tileU + a.V * kPT;
+  float* tileV = tileU + 2 * a.V * kPT;
 
   float* Ag = a.A + n * d.R * d.m;
   float* Bg = a.Bk + n * d.R * d.n;
@@ -52,7 +52,7 @@ gdnx_status launch_compact_t(const gdnx_compact_args& a, cudaStream_t st) {
   const CD d{};
   if (a.V > 128 || a.K > 128 || a.V * a.K > 64 * kThreads) return GDNX_EUNSUPPORTED;
   const size_t smem = sizeof(float) * (size_t)(d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) +
-                                               (a.V + a.K) * kPT);
+                                               2 * (a.V + a.K) * kPT);
   if (cudaFuncSetAttribute(compact_kernel<CD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GDNX_ELAUNCH;
   compact_kernel<CD><<<(unsigned)a.N, kThreads, smem, st>>>(P);

@@ -338,37 +338,68 @@ GDNX_DEV int rmat_index(int v, int k, const CD d) {
 
 // Rm += rearrange(U diag(dsl) Vb^T) for V*K <= 64*256, built in registers tile by
 // tile (dsl = per-slot scale, nullptr = 1).  Needs blockDim.x == kCompThreads.
+// tileU / tileV hold two tiles each ((V + K) x kCompPT x 2 floats): when P is a
+// multiple of 4 the next tile is fetched with cp.async while the current one is used.
 template <class CD>
 GDNX_DEV void add_residual_rmat(float* Rm, const float* U, const float* Vb, const float* dsl, int V, int K, int P,
                                 float* tileU, float* tileV, const CD d) {
   const int tid = threadIdx.x;
   const int per = (V * K + kCompThreads - 1) / kCompThreads;  // <= 64
+  constexpr int KK = CD::a_k * CD::b_k;
+  static_assert(kCompThreads % KK == 0, "thread -> key mapping");
+  const int kk = tid % KK, v0 = tid / KK;
+  const bool async = (P & 3) == 0 && ((reinterpret_cast<uintptr_t>(U) | reinterpret_cast<uintptr_t>(Vb)) & 15) == 0;
+  // tile t of slots p0 = t * kCompPT into buffer t & 1 (zero past P)
+  auto fetch = [&](int p0, int buf) {
+    float* tu = tileU + buf * V * kCompPT;
+    float* tvb = tileV + buf * K * kCompPT;
+    const int np = min(kCompPT, P - p0);
+    if (async) {
+      for (int idx = tid; idx < (V + K) * (kCompPT / 4); idx += kCompThreads) {
+        const int r = idx / (kCompPT / 4), c4 = idx % (kCompPT / 4);
+        const bool isu = r < V;
+        const int rr = isu ? r : r - V;
+        const float* src = (isu ? U : Vb) + (int64_t)rr * P + p0 + 4 * c4;
+        float* dst = (isu ? tu + rr * kCompPT : tvb + rr * kCompPT) + 4 * c4;
+        const uint32_t sd = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+        const int bytes = 4 * c4 < np ? 16 : 0;  // np is a multiple of 4 here
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sd), "l"(bytes ? src : U), "r"(bytes)
+                     : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    } else {
+      for (int idx = tid; idx < V * kCompPT; idx += kCompThreads) {
+        const int vv = idx / kCompPT, pp = idx % kCompPT;
+        tu[idx] = pp < np ? U[(int64_t)vv * P + p0 + pp] : 0.f;
+      }
+      for (int idx = tid; idx < K * kCompPT; idx += kCompThreads) {
+        const int kv = idx / kCompPT, pp = idx % kCompPT;
+        tvb[idx] = pp < np ? Vb[(int64_t)kv * P + p0 + pp] : 0.f;
+      }
+    }
+  };
   float acc[64];
 #pragma unroll
   for (int e = 0; e < 64; ++e) acc[e] = 0.f;
-  for (int p0 = 0; p0 < P; p0 += kCompPT) {
-    const int np = min(kCompPT, P - p0);
-    __syncthreads();
-    for (int idx = tid; idx < V * kCompPT; idx += kCompThreads) {
-      const int vv = idx / kCompPT, pp = idx % kCompPT;
-      tileU[idx] = pp < np ? U[(int64_t)vv * P + p0 + pp] : 0.f;
-    }
-    for (int idx = tid; idx < K * kCompPT; idx += kCompThreads) {
-      const int kk = idx / kCompPT, pp = idx % kCompPT;
-      tileV[idx] = pp < np ? Vb[(int64_t)kk * P + p0 + pp] * (dsl ? dsl[p0 + pp] : 1.f) : 0.f;
-    }
-    __syncthreads();
-    // element e of this thread is (v = tid / K + (threads / K) e, k = tid % K): its key row of
-    // the tile is the same for every e, so it is held in registers
-    constexpr int KK = CD::a_k * CD::b_k;
-    static_assert(kCompThreads % KK == 0, "thread -> key mapping");
-    const int kk = tid % KK, v0 = tid / KK;
+  __syncthreads();
+  fetch(0, 0);
+  for (int p0 = 0, t = 0; p0 < P; p0 += kCompPT, ++t) {
+    if (async) asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();  // tile t is in place; every thread is done with tile t - 1
+    if (p0 + kCompPT < P) fetch(p0 + kCompPT, (t + 1) & 1);
+    const float* tu = tileU + (t & 1) * V * kCompPT;
+    const float* tvb = tileV + (t & 1) * K * kCompPT;
+    // element e of this thread is (v = tid / K + (threads / K) e, k = tid % K): its key
+    // row of the tile (times the slot scales) is the same for every e, so it is held in registers
     float tv[kCompPT];
 #pragma unroll
     for (int pp = 0; pp < kCompPT; pp += 4) {
-      const float4 t4 = *reinterpret_cast<const float4*>(tileV + kk * kCompPT + pp);
+      const float4 t4 = *reinterpret_cast<const float4*>(tvb + kk * kCompPT + pp);
       tv[pp] = t4.x; tv[pp + 1] = t4.y; tv[pp + 2] = t4.z; tv[pp + 3] = t4.w;
     }
+#pragma unroll
+    for (int pp = 0; pp < kCompPT; ++pp)
+      if (dsl) tv[pp] *= (p0 + pp < P) ? dsl[p0 + pp] : 0.f;
 #pragma unroll
     for (int e = 0; e < 64; ++e) {
       if (e >= per) break;
@@ -376,7 +407,7 @@ GDNX_DEV void add_residual_rmat(float* Rm, const float* U, const float* Vb, cons
       float s = acc[e];
 #pragma unroll
       for (int pp = 0; pp < kCompPT; pp += 4) {
-        const float4 u4 = *reinterpret_cast<const float4*>(tileU + vv * kCompPT + pp);
+        const float4 u4 = *reinterpret_cast<const float4*>(tu + vv * kCompPT + pp);
         s = fmaf(u4.x, tv[pp], s);
         s = fmaf(u4.y, tv[pp + 1], s);
         s = fmaf(u4.z, tv[pp + 2], s);

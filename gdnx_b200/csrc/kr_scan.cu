@@ -73,9 +73,9 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   float* tok = dsl + kMaxP;                        // kTB x kTokPer
   float* ybuf = tok + kTB * SMT::kTokPer;          // kTB x V
   float* nbuf = ybuf + kTB * V;                    // kTB x V (new U columns)
-  float* tileU = nbuf + kTB * V;                   // V x kCompPT
-  float* tileV = tileU + V * kCompPT;              // K x kCompPT
-  float* misc = tileV + K * kCompPT;               // 32 floats
+  float* tileU = nbuf + kTB * V;                   // 2 x V x kCompPT
+  float* tileV = tileU + 2 * V * kCompPT;          // 2 x K x kCompPT
+  float* misc = tileV + 2 * K * kCompPT;           // 32 floats
   float* ropeC = misc + 32;                        // kTB x 64 (cos of this block's angles)
   float* ropeS = ropeC + kTB * 64;                 // kTB x 64
   float* sInv = ropeS + kTB * 64;                  // 64 inverse frequencies
@@ -358,7 +358,7 @@ gdnx_status launch_kr(const KrParams& P, cudaStream_t st) {
   constexpr int K = CD::a_k * CD::b_k, V = CD::a_v * CD::b_v;
   const CD d{};
   const size_t floats = (size_t)d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) + kMaxP +
-                        kTB * KrSmem<K, V>::kTokPer + 2 * kTB * V + (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
+                        kTB * KrSmem<K, V>::kTokPer + 2 * kTB * V + 2 * (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
   const size_t smem = floats * sizeof(float) + (size_t)kTB * (2 * K + V) * 2 + 16;  // + bf16 staging
   auto fn = kr_scan_kernel<CD>;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
