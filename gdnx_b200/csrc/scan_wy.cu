@@ -103,6 +103,12 @@ constexpr int P_NT = 256;
 constexpr int P_OFF_KQ = 0;
 constexpr int P_OFF_A = 0;                          // fp32 [2][64][LDA] over the tiles after the MMAs
 constexpr int P_OFF_MQS = 36864;                    // Mq^T staging [2][64 l][64 i] bf16 over the tiles
+constexpr int P_OFF_L1 = 53248;                     // level-1 block-product operands (see the kernel)
+constexpr int P_OFF_L1A2 = P_OFF_L1 + 8192;
+constexpr int P_OFF_L1B2 = P_OFF_L1A2 + 2048;
+constexpr int P_OFF_L2 = P_OFF_MQS;                 // level-2 operands, once the Mq^T staging is stored
+constexpr int P_OFF_L2B = P_OFF_L2 + 8192;
+constexpr int P_OFF_L2B2 = P_OFF_L2B + 4096;
 constexpr int P_OFF_SC = P_OFF_KQ + 65536;          // L, ce, cw, kn, 2^-L [2][64] each; inv_freq [64]
 constexpr int P_OFF_BAR = P_OFF_SC + (10 * 64 + 64) * 4;
 constexpr int P_SMEM = P_OFF_BAR + 64 + 1024;
@@ -140,6 +146,28 @@ GDNX_DEV void subst_block(float* A, int lane) {
   __syncwarp();
 #pragma unroll
   for (int i = 0; i < 32; ++i) A[(I0 + i) * LDA + I0 + lane] = x[i];
+}
+
+// Forward substitution for column c of one 16 x 16 diagonal block of T = (I + A)^{-1}
+// (block rows / columns B0 .. B0 + 15); x[i] = T[B0 + i][B0 + c].  The block's values
+// are written back over A's block (its strictly-lower part is consumed).
+GDNX_DEV void subst_block16(float* A, int B0, int c, float* x) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float s0 = (i == c) ? 1.f : 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int l = 0; l < i; l += 4) {
+      const float4 a4 = *reinterpret_cast<const float4*>(A + (B0 + i) * LDA + B0 + l);
+      s0 = fmaf(-a4.x, x[l], s0);
+      if (l + 1 < i) s1 = fmaf(-a4.y, x[l + 1], s1);
+      if (l + 2 < i) s2 = fmaf(-a4.z, x[l + 2], s2);
+      if (l + 3 < i) s3 = fmaf(-a4.w, x[l + 3], s3);
+    }
+    x[i] = (s0 + s1) + (s2 + s3);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 16; ++i) A[(B0 + i) * LDA + B0 + c] = x[i];
 }
 
 // out[r][lane] = sum_l X[rows r][cols X0 + l] * Y[l][lane] for the 8 rows of
@@ -368,13 +396,34 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     }
   }
   __syncthreads();
-  // T = (I + A)^{-1} by 32 x 32 blocks: T11, T22 by substitution (warps 0-3) while
-  // warps 4-7 form the Mq^T rows; then R = A21 T11 and T21 = -T22 R (all warps)
+  // T = (I + A)^{-1}: the eight 16 x 16 diagonal blocks by substitution (warps 0-3, two
+  // blocks per warp) while warps 4-7 form the Mq^T rows; then the off-diagonal blocks
+  // by two levels of block products on the tensor cores (bf16 operands, fp32 accumulate):
+  //   level 1 (16-blocks, problems p = 2 ci + beta): R = A21 T11, T21 = -T22 R
+  //   level 2 (32-blocks, problems p = ci):         R = A21 T11, T21 = -T22 R
+  // Each level stacks its problems as M = 64 rows and N = 64 columns of one MMA; the
+  // diagonal N blocks are the products (the rest is unused).  Operand tiles: level 1 in
+  // the free tail of the tile region, level 2 over the Mq^T staging once it is stored.
+  char* cL1 = reinterpret_cast<char*>(sm + P_OFF_L1);    // K-major 64 rows: K chunk 0 A21 stack, chunk 1 T11 columns
+  char* cL1A2 = reinterpret_cast<char*>(sm + P_OFF_L1A2);  // MN-major [16 k][64 m]: T22 stack
+  char* cL1B2 = reinterpret_cast<char*>(sm + P_OFF_L1B2);  // MN-major [16 k][64 n]: R stack
+  char* cL2 = reinterpret_cast<char*>(sm + P_OFF_L2);    // K-major 64 rows: chunks 0-1 A21, 2-3 T22
+  char* cL2B = reinterpret_cast<char*>(sm + P_OFF_L2B);  // MN-major [32 k][64 n]: T11 rows
+  char* cL2B2 = reinterpret_cast<char*>(sm + P_OFF_L2B2);  // MN-major [32 k][64 n]: R rows
   if (ok) {
     if (warp < 4) {
-      float* A = sA + (warp >> 1) * C * LDA;
-      if (warp & 1) subst_block<32>(A, lane);
-      else subst_block<0>(A, lane);
+      const int cs_ = warp >> 1, blk = 2 * (warp & 1) + (lane >> 4), c = lane & 15;
+      float* A = sA + cs_ * C * LDA;
+      float x[16];
+      subst_block16(A, 16 * blk, c, x);
+      const int pp = 2 * cs_ + (blk >> 1);  // level-1 problem
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        if (blk & 1)  // T22 of the problem, column c as MN-major row k = c, M offset 16 pp
+          tc::st_chunk_bf16(cL1A2, tc::sw128(c, 2 * pp + hh, 16), x + 8 * hh);
+        else  // T11 column c as K-major row n = 16 pp + c, K chunk 1
+          tc::st_chunk_bf16(cL1, tc::sw128(16 * pp + c, 2 + hh, 64), x + 8 * hh);
+      }
     } else {
       // Mq^T row l = j: Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for i >= l (q_i.k_l undecayed on
       // folded chunks); rows l, 64 i: the MN-major B operand of y += W^T Mq^T
@@ -392,8 +441,128 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
         }
         tc::st_chunk_bf16(mqt, tc::sw128(j, c8, C), v);
       }
+      // level-1 A21 stack: row m = 16 pp + r holds A[32 beta + 16 + r][32 beta .. + 15]
+      {
+        const int t = tid - 128, m = t >> 1, hh = t & 1;  // 64 rows x 2 halves
+        const int pp = m >> 4, r = m & 15, cs_ = pp >> 1, beta = pp & 1;
+        const float* src = sA + (cs_ * C + 32 * beta + 16 + r) * LDA + 32 * beta + 8 * hh;
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = src[e];
+        tc::st_chunk_bf16(cL1, tc::sw128(m, hh, 64), v);
+      }
       tc::fence_async_smem();
     }
+  }
+  tc::fence_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  if (ok && tid == 0) {  // staged Mq^T tiles -> global with bulk copies
+    for (int c2 = 0; c2 < 2; ++c2) {
+      const int64_t chn = pair * 2 + c2;
+      if (chn < P.nchunks)
+        bulk_store(P.tt + (n * P.nchunks + chn) * TT_ELEMS + 2 * C * C, tc::smem_u32(sm + P_OFF_MQS + c2 * 8192), 8192);
+    }
+    bulk_commit();
+  }
+  uint32_t mph = 1;  // the Gram MMAs completed phase 0
+  constexpr uint32_t ID_KK = tc::idesc_bf16(64, 64, false, false);
+  constexpr uint32_t ID_MNMN = tc::idesc_bf16(64, 64, true, true);
+  constexpr uint32_t ID_KMN = tc::idesc_bf16(64, 64, false, true);
+  const uint32_t sL1 = tc::smem_u32(cL1), sL1A2 = tc::smem_u32(cL1A2), sL1B2 = tc::smem_u32(cL1B2);
+  const uint32_t sL2 = tc::smem_u32(cL2), sL2B = tc::smem_u32(cL2B), sL2B2 = tc::smem_u32(cL2B2);
+  // an M = 64 accumulator row m sits in TMEM lane (m / 16) * 32 + m % 16: warps 0-3, lanes < 16
+  const bool drow = warp < 4 && lane < 16;
+  const int dm = 16 * quad + lane;  // accumulator row held by this thread (when drow)
+  const uint32_t dl = (uint32_t)(32 * quad) << 16;
+  auto mma_round = [&](auto issue) -> bool {  // one MMA group, all threads wait for it
+    if (ok && tid == 0) {
+      tc::fence_after();
+      issue();
+      tc::commit(mbar);
+    }
+    bool w = ok ? tc::mbar_wait(mbar, mph & 1) : false;
+    ++mph;
+    w = !__syncthreads_or(!w);
+    tc::fence_after();
+    return w;
+  };
+  // level 1: R = A21 T11
+  ok = mma_round([&] { tc::mma_bf16(tmem, tc::smem_desc(sL1, 16, 1024), tc::smem_desc(sL1 + 32, 16, 1024), ID_KK, 0); });
+  if (ok && warp < 4) {  // tcgen05.ld is warp-collective: all 32 lanes load, rows < 16 are used
+    float d16[16];
+    tc::tmem_ld16(tmem + dl + 16 * quad, d16);  // problem pp = quad: R[r = lane][0..15]
+    if (drow) tc::st_chunk_bf16(cL1B2, tc::sw128(lane, 2 * quad, 16), d16);
+    if (drow) tc::st_chunk_bf16(cL1B2, tc::sw128(lane, 2 * quad + 1, 16), d16 + 8);
+  }
+  tc::fence_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  // level 1: T21 = -T22 R
+  ok = mma_round([&] {
+    tc::mma_bf16(tmem + 64, tc::smem_desc(sL1A2, 8192, 1024), tc::smem_desc(sL1B2, 8192, 1024), ID_MNMN, 0);
+  });
+  if (ok && warp < 4) {
+    float d16[16];
+    tc::tmem_ld16(tmem + 64 + dl + 16 * quad, d16);
+    const int cs_ = quad >> 1, beta = quad & 1;
+    float* dst = sA + (cs_ * C + 32 * beta + 16 + (lane & 15)) * LDA + 32 * beta;
+#pragma unroll
+    if (drow)
+      for (int e = 0; e < 16; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(-d16[e], -d16[e + 1], -d16[e + 2], -d16[e + 3]);
+  }
+  tc::fence_before();
+  if (tid == 0) bulk_wait_read();  // the Mq^T staging is free for the level-2 tiles
+  __syncthreads();
+  // level-2 operands: rows m = 32 ci + r of A21 (chunks 0-1) and T22 (chunks 2-3); T11 rows
+  for (int it = tid; it < 2 * 32 * 8; it += P_NT) {
+    const int m = it >> 3, c8 = it & 7, cs_ = m >> 5, r = m & 31;
+    const float* src = sA + (cs_ * C + 32 + r) * LDA + 8 * c8;  // cols 0-31: A21, 32-63: T22
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = src[e];
+    tc::st_chunk_bf16(cL2, tc::sw128(m, c8, 64), v);
+  }
+  for (int it = tid; it < 2 * 32 * 4; it += P_NT) {
+    const int cs_ = it >> 7, k = (it >> 2) & 31, c8 = it & 3;
+    const float* src = sA + (cs_ * C + k) * LDA + 8 * c8;  // T11 row k, columns 0-31
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = src[e];
+    tc::st_chunk_bf16(cL2B, tc::sw128(k, 4 * cs_ + c8, 32), v);
+  }
+  tc::fence_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  // level 2: R = A21 T11 (K = 32)
+  ok = mma_round([&] {
+    tc::mma_bf16(tmem, tc::smem_desc(sL2, 16, 1024), tc::smem_desc(sL2B, 8192, 1024), ID_KMN, 0);
+    tc::mma_bf16(tmem, tc::smem_desc(sL2 + 32, 16, 1024), tc::smem_desc(sL2B + 2048, 8192, 1024), ID_KMN, 1);
+  });
+  if (ok && warp < 4) {
+    float d32[32];
+    const int cs_ = quad >> 1, r = dm & 31;
+    tc::tmem_ld32(tmem + dl + 32 * cs_, d32);  // R[r][0..31] of chunk cs_
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4)
+      if (drow) tc::st_chunk_bf16(cL2B2, tc::sw128(r, 4 * cs_ + q4, 32), d32 + 8 * q4);
+  }
+  tc::fence_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  // level 2: T21 = -T22 R (T22 in K chunks 2-3 of the level-2 tile)
+  ok = mma_round([&] {
+    tc::mma_bf16(tmem + 64, tc::smem_desc(sL2 + 64, 16, 1024), tc::smem_desc(sL2B2, 8192, 1024), ID_KMN, 0);
+    tc::mma_bf16(tmem + 64, tc::smem_desc(sL2 + 96, 16, 1024), tc::smem_desc(sL2B2 + 2048, 8192, 1024), ID_KMN, 1);
+  });
+  if (ok && warp < 4) {
+    float d32[32];
+    const int cs_ = quad >> 1, r = dm & 31;
+    tc::tmem_ld32(tmem + 64 + dl + 32 * cs_, d32);
+    float* dst = sA + (cs_ * C + 32 + r) * LDA;
+#pragma unroll
+    for (int e = 0; e < 32; e += 4)
+      if (drow) *reinterpret_cast<float4*>(dst + e) = make_float4(-d32[e], -d32[e + 1], -d32[e + 2], -d32[e + 3]);
   }
   tc::fence_before();
   __syncthreads();
@@ -403,39 +572,9 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   }
   if (!ok) {
     if (tid == 0 && P.err) atomicExch(P.err, (int)GDNX_ETIMEOUT);
+    if (tid == 0) bulk_wait_all();
     return;
   }
-  if (tid == 0) {  // staged Mq^T tiles -> global with bulk copies
-    for (int c2 = 0; c2 < 2; ++c2) {
-      const int64_t chn = pair * 2 + c2;
-      if (chn < P.nchunks)
-        bulk_store(P.tt + (n * P.nchunks + chn) * TT_ELEMS + 2 * C * C, tc::smem_u32(sm + P_OFF_MQS + c2 * 8192), 8192);
-    }
-    bulk_commit();
-  }
-  __syncthreads();
-  float* A = sA + (warp >> 2) * C * LDA;
-  const int r0 = 32 + 8 * (warp & 3);
-  {
-    float col[32], out[8];
-#pragma unroll
-    for (int l = 0; l < 32; ++l) col[l] = A[l * LDA + lane];  // T11[:, lane]
-    rows8_times_col(A, r0, 0, col, out);                      // A21 rows
-    __syncwarp();
-#pragma unroll
-    for (int q = 0; q < 8; ++q) A[(r0 + q) * LDA + lane] = out[q];  // R over A21
-  }
-  __syncthreads();
-  {
-    float col[32], out[8];
-#pragma unroll
-    for (int l = 0; l < 32; ++l) col[l] = A[(32 + l) * LDA + lane];  // R[:, lane]
-    rows8_times_col(A, r0, 32, col, out);                            // T22 rows
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < 8; ++q) A[(r0 + q) * LDA + lane] = -out[q];  // T21
-  }
-  __syncthreads();
   // T_e = T diag(ce 2^L), T_w = T diag(cw) as bf16 tiles in the swizzled UMMA layout,
   // straight to global (T's upper block T12 is zero); then L
   for (int it = tid; it < 2 * C * 8; it += P_NT) {
