@@ -636,8 +636,10 @@ static_assert(S_OFF_KQ0 - KB == S_OFF_MQ0, "stage-0 Mq^T position");
 static_assert(S_SMEM <= 232448, "shared memory");
 constexpr uint32_t STAGE_TX = 6 * 8192 + 3 * 8192 + 256;
 
-// TMEM columns: W^T0 | y0 | state (128) | y1 | W^T1 | [Wk; T_w K] (128), so that G2 writes
-// [W^T0 | y0] / [y1 | W^T1] and G3 writes [y0 | S] / [S | y1] with one MMA each.
+// TMEM columns: W^T0 | y0 | state (128) | y1 | W^T1 | Wk (64), so that G2 writes
+// [W^T0 | y0] / [y1 | W^T1] and G3 writes [y0 | S] / [S | y1] with one MMA each.  Wk
+// [64 j][128 k] is two M = 64 accumulators: k block kb in lanes 32 q + 16 kb + (j % 16)
+// of quadrant q = j / 16 (the M = 64 layout, the second block at lane offset 16).
 constexpr uint32_t T_W0 = 0, T_Y0 = 64, T_S = 128, T_Y1 = 256, T_W1 = 320, T_WK = 384;
 
 // 16 TMEM lanes x 32 consecutive 32-bit columns in the 16x256b fragment layout:
@@ -778,6 +780,9 @@ __global__ void __launch_bounds__(S_NT, 1)
     bulk_load(sLst + s * 256, lsg + chn * C, 256, bar);
   };
   if (tid == 0) {
+    const CUtensorMap* mps[4] = {&maps.q, &maps.k, &maps.v, &maps.y};
+    for (int i = 0; i < (maps.y_tma ? 4 : 3); ++i)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(mps[i])) : "memory");
     issue_stage(0);
     if (nchunks > 1) issue_stage(1);
   }
@@ -804,7 +809,7 @@ __global__ void __launch_bounds__(S_NT, 1)
   tc::fence_after();
 
   constexpr uint32_t ID_MN_K = tc::idesc_bf16(128, 64, true, false);
-  constexpr uint32_t ID_WK = tc::idesc_bf16(128, 128, false, true);
+  constexpr uint32_t ID_WK = tc::idesc_bf16(64, 64, false, true);
   constexpr uint32_t ID_G2 = tc::idesc_bf16(128, 128, false, false);
   constexpr uint32_t ID_G3 = tc::idesc_bf16(128, 192, false, true);
 
@@ -891,9 +896,10 @@ __global__ void __launch_bounds__(S_NT, 1)
       }
       ok = wait_or_abort(g3 + s, (uint32_t)((ch >> 1) & 1), s_abort);
       tc::fence_after();
-      // stage s is consumed: fetch chunk ch + 2 into it
-      if (tid == 0 && ok && ch + 2 < nchunks) issue_stage(ch + 2);
       if (group_any(2, !ok)) break;
+      // stage s is consumed: fetch chunk ch + 2 into it (a thread outside warp 0, which
+      // issues the next MMAs; the others go on to the next chunk's wait)
+      if (tid == 32 && ch + 2 < nchunks) issue_stage(ch + 2);
     }
   } else {
     // ========== prologue / output group: RoPE, G1, -Wk, Qd, y zero, y out ==========
@@ -977,7 +983,7 @@ __global__ void __launch_bounds__(S_NT, 1)
         sFK[64 * s + ptid] = fold ? exp2f(-Lj - lsc) : exp2f(Lc - Lj);  // W factor / K' factor
       }
       // S read-out: bf16 operand factor, TMEM write-back factor, write-back flag, folded flag
-      if (ptid == 0)
+      if (ptid == 64)
         sSF[s] = make_float4(norm ? exp2f(ls) : 1.f, fold ? exp2f(ls) : exp2f(ls + Lc), norm ? 1.f : 0.f,
                              fold ? 1.f : 0.f);
       ls = fold ? lsc + Lc : 0.f;
@@ -1011,14 +1017,16 @@ __global__ void __launch_bounds__(S_NT, 1)
       tc::fence_async_smem();
       tc::fence_before();
       group_sync(1);
-      // G1 (state-independent): Wk^T = K^T T_e^T, W^T = V^T T_w^T
+      // G1 (state-independent): Wk = T_e K (per 64-feature block of k), W^T = V^T T_w^T
       const uint32_t skq = sbase + kq_off(s), stt = sTT + s * 16384, sv = sV + s * 16384;
       if (ptid == 0) {
         tc::fence_after();
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(tmem + T_WK, tc::smem_desc(stt + k * 32, 16, 1024), tc::smem_desc(skq + k * 2048, KB, 1024),
-                       ID_WK, k > 0);
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc::mma_bf16(tmem + T_WK + ((uint32_t)(16 * kb) << 16), tc::smem_desc(stt + k * 32, 16, 1024),
+                         tc::smem_desc(skq + kb * KB + k * 2048, KB, 1024), ID_WK, k > 0);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           tc::mma_bf16(tmem + (s ? T_W1 : T_W0), tc::smem_desc(sv + k * 2048, 8192, 1024),
@@ -1050,19 +1058,17 @@ __global__ void __launch_bounds__(S_NT, 1)
           tc::st_chunk_bf16(kq, off, x);
         }
       }
-      // -Wk as rows of the G2 B operand (K-major [j][k]): TMEM rows 0-63 hold Wk[j][k]
-      // (the product [T_e; T_w] K, whose rows 64-127 are not needed); half h writes k block h
-      if (quad < 2) {
+      // -Wk as rows of the G2 B operand (K-major [j][k]), all 8 warps: lane l of quadrant q
+      // holds row j = 16 q + l % 16 of k block l / 16; half h takes 32 of its 64 columns
+      {
         float d[32];
-        char* base = kq + half * KB;
+        const int j = 16 * quad + (lane & 15);
+        char* base = kq + (lane >> 4) * KB;
+        tc::tmem_ld32(tmem + T_WK + lbase + 32 * half, d);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          tc::tmem_ld32(tmem + T_WK + lbase + 64 * half + 32 * hh, d);
+        for (int e = 0; e < 32; ++e) d[e] = -d[e] * wk_mult;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) d[e] = -d[e] * wk_mult;
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(base, tc::sw128(wr + row, 4 * hh + q4, 192), d + 8 * q4);
-        }
+        for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(base, tc::sw128(wr + j, 4 * half + q4, 192), d + 8 * q4);
       }
       tc::fence_async_smem();
       tc::fence_before();
