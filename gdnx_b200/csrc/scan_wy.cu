@@ -98,8 +98,10 @@ GDNX_DEV void expect_tx(uint32_t mbar, uint32_t bytes) {
 
 // ------------------------------- pass 1 ------------------------------------
 constexpr int P_NT = 256;
-// [2 kb][256 rows][128 B] bf16, rows: Qa | Ka | Kb | Qb (a, b: the pair's chunks), so that
-// [Ka;Kb] (rows 64-191) is the A operand and [Qa;Ka] / [Kb;Qb] (rows 0-127 / 128-255) the B operands
+constexpr int P_STORE_TID = 128;  // issues (and waits for) the Mq^T bulk stores; thread 0 issues the MMAs
+// [2 kb][256 rows][128 B] bf16, rows: Qa | Ka | Qb | Kb (a, b: the pair's chunks), so that
+// Ka / Kb (rows 64-127 / 192-255) are the A operands and [Qa;Ka] / [Qb;Kb] (rows 0-127 /
+// 128-255) the B operands of the two Gram products
 constexpr int P_OFF_KQ = 0;
 constexpr int P_OFF_A = 0;                          // fp32 [2][64][LDA] over the tiles after the MMAs
 constexpr int P_OFF_MQS = 36864;                    // Mq^T staging [2][64 l][64 i] bf16 over the tiles
@@ -123,31 +125,6 @@ struct WyParams {
   int* err;
 };
 
-// Forward substitution for one 32 x 32 diagonal block of T = (I + A)^{-1}:
-// lane c owns column I0 + c, rows I0..I0+31.  A rows are read as broadcast
-// float4s; four partial sums per row shorten the dependency chain.  The block
-// is written back over A's block (its strictly-lower part is consumed).
-template <int I0>
-GDNX_DEV void subst_block(float* A, int lane) {
-  float x[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    float s0 = (i == lane) ? 1.f : 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-    for (int l = 0; l < i; l += 4) {
-      const float4 a4 = *reinterpret_cast<const float4*>(A + (I0 + i) * LDA + I0 + l);
-      s0 = fmaf(-a4.x, x[l], s0);
-      if (l + 1 < i) s1 = fmaf(-a4.y, x[l + 1], s1);
-      if (l + 2 < i) s2 = fmaf(-a4.z, x[l + 2], s2);
-      if (l + 3 < i) s3 = fmaf(-a4.w, x[l + 3], s3);
-    }
-    x[i] = (s0 + s1) + (s2 + s3);
-  }
-  __syncwarp();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) A[(I0 + i) * LDA + I0 + lane] = x[i];
-}
-
 // Forward substitution for column c of one 16 x 16 diagonal block of T = (I + A)^{-1}
 // (block rows / columns B0 .. B0 + 15); x[i] = T[B0 + i][B0 + c].  The block's values
 // are written back over A's block (its strictly-lower part is consumed).
@@ -170,23 +147,6 @@ GDNX_DEV void subst_block16(float* A, int B0, int c, float* x) {
   for (int i = 0; i < 16; ++i) A[(B0 + i) * LDA + B0 + c] = x[i];
 }
 
-// out[r][lane] = sum_l X[rows r][cols X0 + l] * Y[l][lane] for the 8 rows of
-// this warp, Y's column held in registers (32 x 32 blocks of the 64 x 64 matrix).
-GDNX_DEV void rows8_times_col(const float* A, int r0, int X0, const float* ycol, float* out) {
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int l = 0; l < 32; l += 4) {
-      const float4 a4 = *reinterpret_cast<const float4*>(A + (r0 + r) * LDA + X0 + l);
-      s0 = fmaf(a4.x, ycol[l], s0);
-      s1 = fmaf(a4.y, ycol[l + 1], s1);
-      s0 = fmaf(a4.z, ycol[l + 2], s0);
-      s1 = fmaf(a4.w, ycol[l + 3], s1);
-    }
-    out[r] = s0 + s1;
-  }
-}
 
 __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
   extern __shared__ uint8_t smraw[];
@@ -218,7 +178,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   if (tid == 0) {
     tc::mbar_init(mbar, 1);
     tc::mbar_init(tbar, 1);
-    // rows Qa | Ka | Kb | Qb of each K block (TMA zero-fills tokens past T)
+    // rows Qa | Ka | Qb | Kb of each K block (TMA zero-fills tokens past T)
     const uint32_t bar = tc::smem_u32(tbar);
     expect_tx(bar, 8 * 8192);
     const int ck_m = maps.use_m[1] ? lm : 0, cq_m = maps.use_m[0] ? lm : 0;
@@ -227,11 +187,22 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
       const uint32_t blk = sKQ + kb * 32768;
       tma_load_5d(blk, &maps.q, 64 * kb, cq_m, (int)h, (int)tbase, (int)b, bar);
       tma_load_5d(blk + 8192, &maps.k, 64 * kb, ck_m, (int)h, (int)tbase, (int)b, bar);
-      tma_load_5d(blk + 16384, &maps.k, 64 * kb, ck_m, (int)h, (int)(tbase + C), (int)b, bar);
-      tma_load_5d(blk + 24576, &maps.q, 64 * kb, cq_m, (int)h, (int)(tbase + C), (int)b, bar);
+      tma_load_5d(blk + 16384, &maps.q, 64 * kb, cq_m, (int)h, (int)(tbase + C), (int)b, bar);
+      tma_load_5d(blk + 24576, &maps.k, 64 * kb, ck_m, (int)h, (int)(tbase + C), (int)b, bar);
     }
   }
-  if (warp == 0) tc::tmem_alloc(s_tmem, 256);
+  // this thread: token j of chunk ci, the TMEM lane of row j of that chunk's M = 64 Gram
+  // accumulator (lane 32 q + 16 ci + j % 16 of quadrant q = j / 16); warps 0-3 / 4-7 take
+  // the 32-column halves h of its masks row (k_j.k_l) and Mq^T row (k_j.q_i)
+  const int quad = warp & 3, half = warp >> 2;
+  const int ci = lane >> 4, j = 16 * quad + (lane & 15);
+  const int64_t tj = tbase + ci * C + j;
+  float be = 0.f, bw = 0.f;  // gate loads first: their latency overlaps the decay prefix
+  if (tj < a.T) {
+    be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tj, h, m));
+    bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tj, h, m));
+  }
+  if (warp == 0) tc::tmem_alloc(s_tmem, 128);
   if (dpairs > 0 && tid < 64) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[lm]);
   // warps 0, 1: log2 decay prefix of chunk `warp` (independent of k)
   if (warp < 2) {
@@ -273,17 +244,6 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     sNE[warp * C + lane] = fast_exp2(-s0);
     sNE[warp * C + lane + 32] = fast_exp2(-s1);
   }
-  // this thread: TMEM lane r = token j of chunk ci (k_j against the chunk's k or q);
-  // warps 0-3 / 4-7 take the two 64-column halves: the masks row (k_j.k_l) or the
-  // Mq^T row (k_j.q_i)
-  const int quad = warp & 3, half = warp >> 2;
-  const int r = quad * 32 + lane, ci = r >> 6, j = r & 63;
-  const int64_t tj = tbase + ci * C + j;
-  float be = 0.f, bw = 0.f;
-  if (tj < a.T) {
-    be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tj, h, m));
-    bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tj, h, m));
-  }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -297,8 +257,8 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     for (int it = tid; it < 2 * C * dch; it += P_NT) {
       const int rr = it / dch, cc = it - rr * dch;  // rr: token of the pair
       const int jj = rr & 63;
-      const int kr = C + rr;                         // Ka rows 64-127, Kb rows 128-191
-      const int qr = rr < C ? jj : 3 * C + jj;       // Qa rows 0-63, Qb rows 192-255
+      const int qr = (rr < C ? 0 : 2 * C) + jj;      // Qa rows 0-63, Qb rows 128-191
+      const int kr = qr + C;                         // Ka rows 64-127, Kb rows 192-255
       float x1[8], x2[8], y1[8], y2[8];
       const uint32_t o1 = tc::sw128(kr, cc, 256), o2 = tc::sw128(kr, cc + dch, 256);
       const uint32_t p1 = tc::sw128(qr, cc, 256), p2 = tc::sw128(qr, cc + dch, 256);
@@ -327,39 +287,46 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   tc::fence_async_smem();
   tc::fence_before();
   __syncthreads();
-  // on the tensor cores, A = [Ka;Kb] (M = 128): D_a = A [Qa;Ka]^T (cols 0-127),
-  // D_b = A [Kb;Qb]^T (cols 128-255); rows 0-63 of D_a and 64-127 of D_b are used
+  // on the tensor cores, two M = 64 Gram products in 128 TMEM columns: chunk a's
+  // Ka [Qa;Ka]^T in lanes 0-15 of each quadrant, chunk b's Kb [Qb;Kb]^T in lanes 16-31
+  // (lane offset 16); columns 0-63 hold k_j.q_i, 64-127 k_j.k_l
   if (ok && tid == 0) {
     tc::fence_after();
-    constexpr uint32_t ID = tc::idesc_bf16(128, 128, false, false);
+    constexpr uint32_t ID = tc::idesc_bf16(64, 128, false, false);
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
       const uint32_t ko = sKQ + (s >> 2) * 32768 + (s & 3) * 32;
-      const uint64_t da = tc::smem_desc(ko + 64 * 128, 16, 1024);
-      tc::mma_bf16(tmem, da, tc::smem_desc(ko, 16, 1024), ID, s > 0);
-      tc::mma_bf16(tmem + 128, da, tc::smem_desc(ko + 128 * 128, 16, 1024), ID, s > 0);
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) {
+        const uint32_t kc = ko + c2 * 128 * 128;  // chunk c2: [Q;K] rows, K at +64 rows
+        tc::mma_bf16(tmem + ((uint32_t)(16 * c2) << 16), tc::smem_desc(kc + 64 * 128, 16, 1024),
+                     tc::smem_desc(kc, 16, 1024), ID, s > 0);
+      }
     }
     tc::commit(mbar);
   }
   if (ok) ok = tc::mbar_wait(mbar, 0);
   ok = !__syncthreads_or(!ok);
   tc::fence_after();
-  // TMEM columns: chunk a = [Ka Qa^T | Ka Ka^T] (0-127), chunk b = [Kb Kb^T | Kb Qb^T] (128-255)
   const uint32_t lrow = (uint32_t)(quad * 32) << 16;
-  const uint32_t col_kk = ci == 0 ? 64u : 128u, col_kq = ci == 0 ? 0u : 192u;
   const float* L = sL + ci * C;
   const float* NE = sNE + ci * C;
-  const bool fold = L[C - 1] >= FOLD_MIN_LC;  // uniform per chunk, i.e. per warp
+  const bool fold = L[C - 1] >= FOLD_MIN_LC;
   const float Lj = L[j];
   // masks, all warps: this thread's half (32 columns) of row j of k k^T
-  float d[32];
   if (ok) {
-    tc::tmem_ld32(tmem + lrow + col_kk + 32 * half, d);
+    float d[32];
+    tc::tmem_ld32(tmem + lrow + 64 + 32 * half, d);
     if ((j >> 5) == half) {  // |k_j|^2 is the diagonal (selected without a dynamic register index)
-      float kn = 0.f;
+      const int id = j & 31;  // d[id] by halving selects (static register indices only)
+      float t[16];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) kn = (e == (j & 31)) ? d[e] : kn;
-      sKN[ci * C + j] = kn;
+      for (int e = 0; e < 16; ++e) t[e] = (id & 16) ? d[e + 16] : d[e];
+#pragma unroll
+      for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int e = 0; e < w; ++e) t[e] = (id & w) ? t[e + w] : t[e];
+      sKN[ci * C + j] = t[0];
     }
   }
   __syncthreads();
@@ -383,6 +350,8 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     }
     const float rj = cej * ej;  // 2^{L_j - L_l} as 2^{L_j} 2^{-L_l} on folded chunks
     float* Arow = sA + (ci * C + j) * LDA + 32 * half;
+    float d[32];
+    tc::tmem_ld32(tmem + lrow + 64 + 32 * half, d);  // again (not held across the barrier)
 #pragma unroll
     for (int e = 0; e < 32; e += 4) {
       float g[4];
@@ -394,10 +363,27 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
       }
       *reinterpret_cast<float4*>(Arow + e) = make_float4(g[0], g[1], g[2], g[3]);
     }
+    // Mq^T row l = j, columns i of this half: Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for i >= l
+    // (q_i.k_l undecayed on folded chunks); rows l, 64 i: the MN-major B operand of
+    // y += W^T Mq^T, staged over the consumed tiles
+    float dq[32];
+    tc::tmem_ld32(tmem + lrow + 32 * half, dq);
+    char* mqt = reinterpret_cast<char*>(sm + P_OFF_MQS + ci * 8192);
+#pragma unroll
+    for (int c8 = 0; c8 < 4; ++c8) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = 32 * half + 8 * c8 + e;
+        v[e] = (i >= j) ? (fold ? dq[8 * c8 + e] : fast_exp2(L[i] - Lj) * dq[8 * c8 + e]) : 0.f;
+      }
+      tc::st_chunk_bf16(mqt, tc::sw128(j, 4 * half + c8, C), v);
+    }
+    tc::fence_async_smem();
   }
   __syncthreads();
   // T = (I + A)^{-1}: the eight 16 x 16 diagonal blocks by substitution (warps 0-3, two
-  // blocks per warp) while warps 4-7 form the Mq^T rows; then the off-diagonal blocks
+  // blocks per warp) while warps 4-7 stack the level-1 A21 blocks; then the off-diagonal blocks
   // by two levels of block products on the tensor cores (bf16 operands, fp32 accumulate):
   //   level 1 (16-blocks, problems p = 2 ci + beta): R = A21 T11, T21 = -T22 R
   //   level 2 (32-blocks, problems p = ci):         R = A21 T11, T21 = -T22 R
@@ -425,22 +411,6 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
           tc::st_chunk_bf16(cL1, tc::sw128(16 * pp + c, 2 + hh, 64), x + 8 * hh);
       }
     } else {
-      // Mq^T row l = j: Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for i >= l (q_i.k_l undecayed on
-      // folded chunks); rows l, 64 i: the MN-major B operand of y += W^T Mq^T
-      float e64[64];
-      tc::tmem_ld32(tmem + lrow + col_kq, e64);
-      tc::tmem_ld32(tmem + lrow + col_kq + 32, e64 + 32);
-      char* mqt = reinterpret_cast<char*>(sm + P_OFF_MQS + ci * 8192);
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        float v[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int i = 8 * c8 + e;
-          v[e] = (i >= j) ? (fold ? e64[i] : fast_exp2(L[i] - Lj) * e64[i]) : 0.f;
-        }
-        tc::st_chunk_bf16(mqt, tc::sw128(j, c8, C), v);
-      }
       // level-1 A21 stack: row m = 16 pp + r holds A[32 beta + 16 + r][32 beta .. + 15]
       {
         const int t = tid - 128, m = t >> 1, hh = t & 1;  // 64 rows x 2 halves
@@ -457,7 +427,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   tc::fence_async_smem();
   tc::fence_before();
   __syncthreads();
-  if (ok && tid == 0) {  // staged Mq^T tiles -> global with bulk copies
+  if (ok && tid == P_STORE_TID) {  // staged Mq^T tiles -> global with bulk copies
     for (int c2 = 0; c2 < 2; ++c2) {
       const int64_t chn = pair * 2 + c2;
       if (chn < P.nchunks)
@@ -507,12 +477,12 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     tc::tmem_ld16(tmem + 64 + dl + 16 * quad, d16);
     const int cs_ = quad >> 1, beta = quad & 1;
     float* dst = sA + (cs_ * C + 32 * beta + 16 + (lane & 15)) * LDA + 32 * beta;
-#pragma unroll
     if (drow)
+#pragma unroll
       for (int e = 0; e < 16; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(-d16[e], -d16[e + 1], -d16[e + 2], -d16[e + 3]);
   }
   tc::fence_before();
-  if (tid == 0) bulk_wait_read();  // the Mq^T staging is free for the level-2 tiles
+  if (tid == P_STORE_TID) bulk_wait_read();  // the Mq^T staging is free for the level-2 tiles
   __syncthreads();
   // level-2 operands: rows m = 32 ci + r of A21 (chunks 0-1) and T22 (chunks 2-3); T11 rows
   for (int it = tid; it < 2 * 32 * 8; it += P_NT) {
@@ -568,11 +538,11 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   __syncthreads();
   if (warp == 0) {
     tc::fence_after();
-    tc::tmem_dealloc(tmem, 256);
+    tc::tmem_dealloc(tmem, 128);
   }
   if (!ok) {
     if (tid == 0 && P.err) atomicExch(P.err, (int)GDNX_ETIMEOUT);
-    if (tid == 0) bulk_wait_all();
+    if (tid == P_STORE_TID) bulk_wait_all();
     return;
   }
   // T_e = T diag(ce 2^L), T_w = T diag(cw) as bf16 tiles in the swizzled UMMA layout,
@@ -588,11 +558,16 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     } else {
       const float* src = sA + (cj * C + jj) * LDA + 8 * c8;
       const float4 u0 = *reinterpret_cast<const float4*>(src), u1 = *reinterpret_cast<const float4*>(src + 4);
+      const float4* ce4 = reinterpret_cast<const float4*>(sCE + cj * C + 8 * c8);
+      const float4* cw4 = reinterpret_cast<const float4*>(sCW + cj * C + 8 * c8);
+      const float4 e0 = ce4[0], e1 = ce4[1], w0 = cw4[0], w1 = cw4[1];
       const float t8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      const float ce8[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+      const float cw8[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        te[e] = t8[e] * sCE[cj * C + 8 * c8 + e];
-        tw[e] = t8[e] * sCW[cj * C + 8 * c8 + e];
+        te[e] = t8[e] * ce8[e];
+        tw[e] = t8[e] * cw8[e];
       }
     }
     char* dst = reinterpret_cast<char*>(P.tt + (n * P.nchunks + chn) * TT_ELEMS);
@@ -604,7 +579,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     const int64_t chn = pair * 2 + (tid >> 6);
     if (chn < P.nchunks) P.lsum[(n * P.nchunks + chn) * C + (tid & 63)] = sL[tid];
   }
-  if (tid == 0) bulk_wait_read();  // the Mq^T stores have read shared memory
+  if (tid == P_STORE_TID) bulk_wait_read();  // the Mq^T stores have read shared memory
 }
 
 // ------------------------------- pass 2 ------------------------------------
