@@ -962,6 +962,22 @@ __global__ void __launch_bounds__(S_NT, 1)
         sSF[s] = make_float4(norm ? exp2f(ls) : 1.f, fold ? exp2f(ls) : exp2f(ls + Lc), norm ? 1.f : 0.f,
                              fold ? 1.f : 0.f);
       ls = fold ? lsc + Lc : 0.f;
+      // G1, first part (needs no rotated k): W^T = V^T T_w^T; and this stage's y buffer to
+      // zero (its chunk two back is written out) while the tensor core runs it
+      const uint32_t skq = sbase + kq_off(s), stt = sTT + s * 16384, sv = sV + s * 16384;
+      if (ptid == 0) {
+        tc::fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(tmem + (s ? T_W1 : T_W0), tc::smem_desc(sv + k * 2048, 8192, 1024),
+                       tc::smem_desc(stt + 8192 + k * 32, 16, 1024), ID_MN_K, k > 0);
+      }
+      {
+        float z[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) z[e] = 0.f;
+        tc::tmem_st32(tmem + (s ? T_Y1 : T_Y0) + lbase + 32 * half, z);
+      }
       // lane RoPE of token j's k (row j) and q (row qr + j) in place, one set of angles
       for (int it = ptid; it < C * dch; it += G_NT) {
         const int j = it / dch, cc = it - j * dch;
@@ -992,8 +1008,7 @@ __global__ void __launch_bounds__(S_NT, 1)
       tc::fence_async_smem();
       tc::fence_before();
       group_sync(1);
-      // G1 (state-independent): Wk = T_e K (per 64-feature block of k), W^T = V^T T_w^T
-      const uint32_t skq = sbase + kq_off(s), stt = sTT + s * 16384, sv = sV + s * 16384;
+      // G1, second part: Wk = T_e K (per 64-feature block of k); one commit covers both parts
       if (ptid == 0) {
         tc::fence_after();
 #pragma unroll
@@ -1002,18 +1017,7 @@ __global__ void __launch_bounds__(S_NT, 1)
           for (int k = 0; k < 4; ++k)
             tc::mma_bf16(tmem + T_WK + ((uint32_t)(16 * kb) << 16), tc::smem_desc(stt + k * 32, 16, 1024),
                          tc::smem_desc(skq + kb * KB + k * 2048, KB, 1024), ID_WK, k > 0);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(tmem + (s ? T_W1 : T_W0), tc::smem_desc(sv + k * 2048, 8192, 1024),
-                       tc::smem_desc(stt + 8192 + k * 32, 16, 1024), ID_MN_K, k > 0);
         tc::commit(g1);
-      }
-      // while G1 runs: y buffer of this stage to zero (its chunk two back is written out)
-      {
-        float z[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) z[e] = 0.f;
-        tc::tmem_st32(tmem + (s ? T_Y1 : T_Y0) + lbase + 32 * half, z);
       }
       ok = wait_or_abort(g1, (uint32_t)(ch & 1), s_abort);
       tc::fence_after();
