@@ -352,16 +352,27 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     float* Arow = sA + (ci * C + j) * LDA + 32 * half;
     float d[32];
     tc::tmem_ld32(tmem + lrow + 64 + 32 * half, d);  // again (not held across the barrier)
+    if (fold) {  // (lanes of one warp can be on different chunks: a per-lane branch, rarely divergent)
 #pragma unroll
-    for (int e = 0; e < 32; e += 4) {
-      float g[4];
+      for (int e = 0; e < 32; e += 4) {
+        const float4 ne = *reinterpret_cast<const float4*>(NE + 32 * half + e);
+        const float n4[4] = {ne.x, ne.y, ne.z, ne.w};
+        float g[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int l = 32 * half + e + u;
-        const float w = fold ? rj * NE[l] : cej * fast_exp2(Lj - L[l]);
-        g[u] = (l < j) ? w * d[e + u] : 0.f;
+        for (int u = 0; u < 4; ++u) g[u] = (32 * half + e + u < j) ? rj * n4[u] * d[e + u] : 0.f;
+        *reinterpret_cast<float4*>(Arow + e) = make_float4(g[0], g[1], g[2], g[3]);
       }
-      *reinterpret_cast<float4*>(Arow + e) = make_float4(g[0], g[1], g[2], g[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        float g[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int l = 32 * half + e + u;
+          g[u] = (l < j) ? cej * fast_exp2(Lj - L[l]) * d[e + u] : 0.f;
+        }
+        *reinterpret_cast<float4*>(Arow + e) = make_float4(g[0], g[1], g[2], g[3]);
+      }
     }
     // Mq^T row l = j, columns i of this half: Mq[i][l] = 2^{L_i - L_l} (q_i.k_l) for i >= l
     // (q_i.k_l undecayed on folded chunks); rows l, 64 i: the MN-major B operand of
@@ -372,10 +383,15 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
 #pragma unroll
     for (int c8 = 0; c8 < 4; ++c8) {
       float v[8];
+      if (fold) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int i = 32 * half + 8 * c8 + e;
-        v[e] = (i >= j) ? (fold ? dq[8 * c8 + e] : fast_exp2(L[i] - Lj) * dq[8 * c8 + e]) : 0.f;
+        for (int e = 0; e < 8; ++e) v[e] = (32 * half + 8 * c8 + e >= j) ? dq[8 * c8 + e] : 0.f;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = 32 * half + 8 * c8 + e;
+          v[e] = (i >= j) ? fast_exp2(L[i] - Lj) * dq[8 * c8 + e] : 0.f;
+        }
       }
       tc::st_chunk_bf16(mqt, tc::sw128(j, 4 * half + c8, C), v);
     }
