@@ -352,7 +352,10 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     float* Arow = sA + (ci * C + j) * LDA + 32 * half;
     float d[32];
     tc::tmem_ld32(tmem + lrow + 64 + 32 * half, d);  // again (not held across the barrier)
-    if (fold) {  // (lanes of one warp can be on different chunks: a per-lane branch, rarely divergent)
+    if (32 * half >= 16 * quad + 16) {  // l >= j for the whole half row (warp-uniform)
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(Arow + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else if (fold) {  // (lanes of one warp can be on different chunks: a per-lane branch, rarely divergent)
 #pragma unroll
       for (int e = 0; e < 32; e += 4) {
         const float4 ne = *reinterpret_cast<const float4*>(NE + 32 * half + e);
@@ -383,7 +386,10 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
 #pragma unroll
     for (int c8 = 0; c8 < 4; ++c8) {
       float v[8];
-      if (fold) {
+      if (32 * half + 32 <= 16 * quad) {  // i < j for the whole half row (warp-uniform)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      } else if (fold) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = (32 * half + 8 * c8 + e >= j) ? dq[8 * c8 + e] : 0.f;
       } else {
