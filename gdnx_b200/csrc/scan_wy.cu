@@ -175,7 +175,9 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   const uint32_t sKQ = tc::smem_u32(cKQ);
   const bool braided = a.decay_kind == GDNX_DECAY_BRAIDED;
 
-  if (tid == 0) {
+  // Set-up work away from warps 0-1 (the decay prefix) and thread 0 (the MMA issuer):
+  // warp 7 issues the tile loads, warp 6 allocates TMEM, warps 2-3 the RoPE frequencies.
+  if (tid == 224) {
     tc::mbar_init(mbar, 1);
     tc::mbar_init(tbar, 1);
     // rows Qa | Ka | Qb | Kb of each K block (TMA zero-fills tokens past T)
@@ -202,8 +204,8 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tj, h, m));
     bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tj, h, m));
   }
-  if (warp == 0) tc::tmem_alloc(s_tmem, 128);
-  if (dpairs > 0 && tid < 64) sInv[tid] = 1.0f / powf(10000.0f, (float)tid / a.rope.den[lm]);
+  if (warp == 6) tc::tmem_alloc(s_tmem, 128);
+  if (dpairs > 0 && tid >= 64 && tid < 128) sInv[tid - 64] = 1.0f / powf(10000.0f, (float)(tid - 64) / a.rope.den[lm]);
   // warps 0, 1: log2 decay prefix of chunk `warp` (independent of k)
   if (warp < 2) {
     float lg[2];
@@ -558,7 +560,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   }
   tc::fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 6) {
     tc::fence_after();
     tc::tmem_dealloc(tmem, 128);
   }
