@@ -199,10 +199,19 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   const int quad = warp & 3, half = warp >> 2;
   const int ci = lane >> 4, j = 16 * quad + (lane & 15);
   const int64_t tj = tbase + ci * C + j;
-  float be = 0.f, bw = 0.f;  // gate loads first: their latency overlaps the decay prefix
+  // gate and decay loads first, as raw bits (converted where used, so nothing waits on them
+  // here): their latency overlaps the set-up and the tile loads
+  uint32_t rbe = 0, rbw = 0, rdec[2] = {0, 0};
   if (tj < a.T) {
-    be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tj, h, m));
-    bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tj, h, m));
+    rbe = ld_raw(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, tj, h, m));
+    rbw = ld_raw(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, tj, h, m));
+  }
+  if (warp < 2 && !braided) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int64_t t = tbase + warp * C + lane + 32 * s;
+      if (t < a.T) rdec[s] = ld_raw(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
+    }
   }
   if (warp == 6) tc::tmem_alloc(s_tmem, 128);
   if (dpairs > 0 && tid >= 64 && tid < 128) sInv[tid - 64] = 1.0f / powf(10000.0f, (float)(tid - 64) / a.rope.den[lm]);
@@ -217,7 +226,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
         const int64_t od = view_off(a.decay, b, t, h, m);
         float l;
         if (a.decay_kind == GDNX_DECAY_LOG) {
-          l = ld_as_f32(a.decay.ptr, a.decay.dtype, od);
+          l = raw_f32(rdec[s], a.decay.dtype);
           if (!P.kmd2) l = fminf(l, 0.f);
         } else if (braided) {
           float acc = 0.f;
@@ -226,7 +235,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
             acc += expf(-fminf(softplus_f(ld_as_f32(a.decay.ptr, a.decay.dtype, od + z)), 5.0f) * a.braid_rates[z]);
           l = logf(fmaxf(fminf(acc * 0.25f, a.braid_clamp), 1e-30f));
         } else {
-          float g = ld_as_f32(a.decay.ptr, a.decay.dtype, od);
+          float g = raw_f32(rdec[s], a.decay.dtype);
           if (!P.kmd2) g = fminf(fmaxf(g, 0.f), 1.f);
           l = logf(fmaxf(g, 1e-30f));
         }
@@ -336,6 +345,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
     // A[j][l] = ce_j 2^{L_j - L_l} (k_j.k_l) for l < j
     float cej = 0.f, cwj = 0.f;
     if (tj < a.T) {
+      const float be = raw_f32(rbe, a.gate_e.dtype), bw = raw_f32(rbw, a.gate_w.dtype);
       if (P.kmd2) {
         cej = be;
         cwj = bw;
