@@ -108,19 +108,40 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
       for (int c = 0; c < 8; ++c) Y[i * 8 + c] = acc[c];
     }
   };
-  // Out[j][c] = sum_i R[i][j] X[i][c] (n x 8, X = Y or Q): thread -> column j, 2 of the 8 outputs
+  // Out[j][c] = sum_i R[i][j] X[i][c] (n x 8, X = Y or Q): lane group g = lane / 8 of warp w
+  // takes column j = 8 w + lane % 8 over the rows i with (i / 8) % 4 == g (R reads hit 32
+  // distinct banks), eight independent sums; the four groups' sums meet by shuffles
   auto col_times = [&](const float* X, float* Out, int out_stride_j, int out_stride_c) {
-    for (int t = tid; t < n * 4; t += nt) {
-      const int jj = t >> 2, c0 = (t & 3) * 2;
-      float a0 = 0.f, a1 = 0.f;
-      for (int i = 0; i < m; ++i) {
-        const float r = Rm[i * ld + jj];
-        const float2 x = *reinterpret_cast<const float2*>(X + i * 8 + c0);
-        a0 = fmaf(r, x.x, a0);
-        a1 = fmaf(r, x.y, a1);
+    const int g = lane >> 3, jj = warp * 8 + (lane & 7);
+    const bool has = jj < n && warp * 8 < n;
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+    if (has) {
+      for (int i0 = 8 * g; i0 < m; i0 += 32) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+          const int i = i0 + b;
+          if (i >= m) break;
+          const float r = Rm[i * ld + jj];
+          const float4 x0 = *reinterpret_cast<const float4*>(X + i * 8);
+          const float4 x1 = *reinterpret_cast<const float4*>(X + i * 8 + 4);
+          acc[0] = fmaf(r, x0.x, acc[0]); acc[1] = fmaf(r, x0.y, acc[1]);
+          acc[2] = fmaf(r, x0.z, acc[2]); acc[3] = fmaf(r, x0.w, acc[3]);
+          acc[4] = fmaf(r, x1.x, acc[4]); acc[5] = fmaf(r, x1.y, acc[5]);
+          acc[6] = fmaf(r, x1.z, acc[6]); acc[7] = fmaf(r, x1.w, acc[7]);
+        }
       }
-      Out[jj * out_stride_j + c0 * out_stride_c] = a0;
-      Out[jj * out_stride_j + (c0 + 1) * out_stride_c] = a1;
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 8);
+      acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 16);
+    }
+    if (has) {  // group g writes outputs 2 g, 2 g + 1
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        if ((c >> 1) == g) Out[jj * out_stride_j + c * out_stride_c] = acc[c];
     }
   };
   row_times(Gs);
