@@ -152,47 +152,60 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
     row_times(Z);           // Y = R Z
     __syncthreads();
   }
-  // Q = orth(Y): classical Gram-Schmidt applied twice per column ("twice is enough"),
-  // one thread per row, each projection a block-wide reduction of <= 8 dot products.
-  {
-    float yr[kCompMaxQ], qr[kCompMaxQ];
-    const bool has = tid < m;
-#pragma unroll
-    for (int c = 0; c < kCompMaxQ; ++c) {
-      yr[c] = has ? Y[tid * q + c] : 0.f;
-      qr[c] = 0.f;
-    }
-    float* part = red;  // [8 warps][8]
+  // Q = orth(Y): classical Gram-Schmidt applied twice per column ("twice is enough") on
+  // one warp, lane l holding rows l + 32 r, so every projection is a warp reduction of
+  // <= 8 dot products (no block barriers); the other warps wait at the barrier below.
+  static_assert(kCompMaxM <= 32 * 8, "one warp holds every row of Y");
+  if (warp == 0) {
+    float qv[kCompMaxQ][8];  // qv[p][r] = Q[lane + 32 r][p]
 #pragma unroll
     for (int c = 0; c < kCompMaxQ; ++c) {
       if (c >= q) break;
+      float y[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int i = lane + 32 * r;
+        y[r] = i < m ? Y[i * q + c] : 0.f;
+      }
 #pragma unroll
       for (int pass = 0; pass < 2; ++pass) {
         if (c == 0) break;
         float dp[kCompMaxQ];
 #pragma unroll
-        for (int p = 0; p < kCompMaxQ; ++p) dp[p] = p < c ? warp_sum(qr[p] * yr[c]) : 0.f;
-        __syncthreads();
-        if (lane == 0)
-#pragma unroll
-          for (int p = 0; p < kCompMaxQ; ++p) part[warp * 8 + p] = dp[p];
-        __syncthreads();
-#pragma unroll
         for (int p = 0; p < kCompMaxQ; ++p) {
-          if (p >= c) break;
-          float dsum = 0.f;
-          for (int w = 0; w < nt / 32; ++w) dsum += part[w * 8 + p];
-          yr[c] = fmaf(-dsum, qr[p], yr[c]);
-        }
-      }
-      const float nn = block_sum(yr[c] * yr[c], red + 48);
-      const float inv = nn > 1e-30f ? rsqrtf(nn) : 0.f;
-      qr[c] = yr[c] * inv;
-    }
-    if (has)
+          float acc = 0.f;
+          if (p < c)
 #pragma unroll
-      for (int c = 0; c < kCompMaxQ; ++c)
-        if (c < q) Qm[tid * q + c] = qr[c];
+            for (int r = 0; r < 8; ++r) acc = fmaf(qv[p][r], y[r], acc);
+          dp[p] = acc;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int p = 0; p < kCompMaxQ; ++p)
+            if (p < c) dp[p] += __shfl_xor_sync(0xffffffffu, dp[p], o);
+#pragma unroll
+        for (int p = 0; p < kCompMaxQ; ++p)
+          if (p < c)
+#pragma unroll
+            for (int r = 0; r < 8; ++r) y[r] = fmaf(-dp[p], qv[p][r], y[r]);
+      }
+      float nn = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) nn = fmaf(y[r], y[r], nn);
+      nn = warp_sum(nn);
+      const float inv = nn > 1e-30f ? rsqrtf(nn) : 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) qv[c][r] = y[r] * inv;
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int i = lane + 32 * r;
+      if (i < m)
+#pragma unroll
+        for (int c = 0; c < kCompMaxQ; ++c)
+          if (c < q) Qm[i * q + c] = qv[c][r];
+    }
   }
   __syncthreads();
   // Bm = Q^T R   (q x n), Bm[c][j]
