@@ -49,10 +49,27 @@ struct KrSmem {
   static constexpr int kTokPer = 4 * K + 2 * V + 8;
 };
 
-template <class CD>
+// Cluster barrier (release / acquire at cluster scope: orders the CTAs' global-memory
+// slot writes and reads).
+GDNX_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+GDNX_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// CL = 1: one CTA per chain.  CL = 2: a cluster of two CTAs per chain, CTA r owning state
+// rows r V/2 .. (r+1) V/2 - 1 (the rows evolve independently given the token's vectors);
+// both CTAs form the token vectors and run each compaction on the whole state (the same
+// inputs give the same factors), and cluster barriers order the slot ring's global
+// reads and writes between them.
+template <class CD, int CL>
 __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   constexpr int K = CD::a_k * CD::b_k, V = CD::a_v * CD::b_v;
-  constexpr int TPR = kNT / V;     // threads per state row
+  constexpr int VL = V / CL;       // state rows of this CTA
+  constexpr int TPR = kNT / VL;    // threads per state row
   constexpr int KC = K / 4 / TPR;  // float4 key chunks per thread
   using SMT = KrSmem<K, V>;
   extern __shared__ float4 smem4[];
@@ -83,10 +100,11 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   __nv_bfloat16* rawst =
       reinterpret_cast<__nv_bfloat16*>((reinterpret_cast<uintptr_t>(sInv + 64) + 15) & ~uintptr_t(15));
 
-  const int64_t n = blockIdx.x;
+  const int cr = CL == 1 ? 0 : (int)cluster_rank();
+  const int64_t n = blockIdx.x / CL;
   const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int v = tid / TPR, j = tid % TPR;
+  const int v = cr * VL + tid / TPR, j = tid % TPR;
   const int av = v / d.b_v, bv = v % d.b_v;
 
   float* Ug = A.U + n * (int64_t)V * Pn;
@@ -232,11 +250,12 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       const int kk = idx / nt, tt = idx - kk * nt;
       tok[tt * SMT::kTokPer + SMT::kTokKold + kk] = Vg[(int64_t)kk * Pn + p + tt];
     }
-    for (int idx = tid; idx < V * nt; idx += kNT) {
-      const int vv = idx / nt, tt = idx - vv * nt;
+    for (int idx = tid; idx < VL * nt; idx += kNT) {  // this CTA's rows
+      const int vv = cr * VL + idx / nt, tt = idx % nt;
       tok[tt * SMT::kTokPer + SMT::kTokUold + vv] = Ug[(int64_t)vv * Pn + p + tt];
     }
     __syncthreads();
+    if (CL > 1) cluster_sync_all();  // both CTAs have read the evicted slots before either flushes
     if (raw_ok && t0 + nt < a.T) prefetch_raw(t0 + nt);  // the staging has been read
     // ---------- stage B: running decays (thread 0) ----------
     if (tid == 0) {
@@ -301,18 +320,19 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
     }
     __syncthreads();
     // ---------- flush: outputs, new slots, slot decays ----------
-    for (int idx = tid; idx < nt * V; idx += kNT) {
-      const int tt = idx / V, vv = idx % V;
-      st_from_f32(a.y, a.y_dtype, b * a.y_sb + (t0 + tt) * a.y_st + h * a.y_sh + m * a.y_sm + vv, ybuf[idx]);
+    for (int idx = tid; idx < nt * VL; idx += kNT) {
+      const int tt = idx / VL, vv = cr * VL + idx % VL;
+      st_from_f32(a.y, a.y_dtype, b * a.y_sb + (t0 + tt) * a.y_st + h * a.y_sh + m * a.y_sm + vv, ybuf[tt * V + vv]);
     }
-    for (int idx = tid; idx < V * nt; idx += kNT) {
-      const int vv = idx / nt, tt = idx % nt;
+    for (int idx = tid; idx < VL * nt; idx += kNT) {
+      const int vv = cr * VL + idx / nt, tt = idx % nt;
       Ug[(int64_t)vv * Pn + p + tt] = nbuf[tt * V + vv];
     }
-    for (int idx = tid; idx < K * nt; idx += kNT) {
-      const int kk = idx / nt, tt = idx % nt;
-      Vg[(int64_t)kk * Pn + p + tt] = tok[tt * SMT::kTokPer + SMT::kTokK + kk];
-    }
+    if (cr == 0)
+      for (int idx = tid; idx < K * nt; idx += kNT) {
+        const int kk = idx / nt, tt = idx % nt;
+        Vg[(int64_t)kk * Pn + p + tt] = tok[tt * SMT::kTokPer + SMT::kTokK + kk];
+      }
     {
       const float pre = misc[1];
       for (int s = tid; s < Pn; s += kNT) {
@@ -334,6 +354,7 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       for (int i = tid; i < R * d.m; i += kNT) A_s[i] *= fac;
       for (int i = tid; i < R * d.n; i += kNT) B_s[i] *= fac;
       fac = 1.f;
+      if (CL > 1) cluster_sync_all();  // the other CTA's slot writes are visible
       rebuild();                      // Rm = rearrange(U Vb^T), Rs exact again
       add_kron_rmat(Rm, A_s, B_s, d);
       __syncthreads();
@@ -344,6 +365,10 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
     }
   }
   // ---------- materialise the state ----------
+  if (CL > 1) {
+    cluster_sync_all();  // the other CTA is done reading the slots
+    if (cr != 0) return;
+  }
   for (int i = tid; i < R * d.m; i += kNT) Ag[i] = A_s[i] * fac;
   for (int i = tid; i < R * d.n; i += kNT) Bg[i] = B_s[i] * fac;
   for (int idx = tid; idx < K * Pn; idx += kNT) Vg[idx] *= dsl[idx % Pn];
@@ -360,10 +385,32 @@ gdnx_status launch_kr(const KrParams& P, cudaStream_t st) {
   const size_t floats = (size_t)d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) + kMaxP +
                         kTB * KrSmem<K, V>::kTokPer + 2 * kTB * V + 2 * (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
   const size_t smem = floats * sizeof(float) + (size_t)kTB * (2 * K + V) * 2 + 16;  // + bf16 staging
-  auto fn = kr_scan_kernel<CD>;
+  const int64_t N = P.a.base.B * P.a.base.H * P.a.base.M;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return GDNX_ELAUNCH;
+  if (2 * N <= sms) {  // idle SMs: two CTAs (a cluster) per chain
+    auto fn = kr_scan_kernel<CD, 2>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return GDNX_ELAUNCH;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * N));
+    cfg.blockDim = dim3(kNT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, fn, P) != cudaSuccess) return GDNX_ELAUNCH;
+    return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+  }
+  auto fn = kr_scan_kernel<CD, 1>;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GDNX_ELAUNCH;
-  const int64_t N = P.a.base.B * P.a.base.H * P.a.base.M;
   fn<<<(unsigned)N, kNT, smem, st>>>(P);
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
 }

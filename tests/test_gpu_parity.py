@@ -259,6 +259,24 @@ def test_kr_scan_chunked_calls_equal_one_call():
     assert rel(s2.U, s1.U) < 1e-5 and rel(s2.A, s1.A) < 1e-4
 
 
+def test_kr_scan_one_cta_and_cluster_paths_agree():
+    """80 chains (more CTA pairs than SMs: one CTA per chain) against the same chains run
+    16 at a time (a two-CTA cluster per chain)."""
+    B, T, P, dims = 20, 48, 16, (16, 16, 8, 8)
+    ins = parity_inputs(B, T, 1, 4, 128, 128, seed=9)
+    N = B * 4
+    G = R.sketch_matrix(N, 64, 8).to(DEV)
+    s_all = ops.KRState.zeros(N, 4, P, dims, 128, 128, DEV)
+    y_all = ops.gdn3_kr_scan(*gpu(*ins), s_all, G, P=P)
+    ys, us = [], []
+    for b0 in range(0, B, 4):
+        st = ops.KRState.zeros(16, 4, P, dims, 128, 128, DEV)
+        ys.append(ops.gdn3_kr_scan(*gpu(*[t[b0:b0 + 4] for t in ins]), st, G[4 * b0:4 * b0 + 16], P=P))
+        us.append(st.U)
+    assert rel(torch.cat(ys, 0), y_all) < 1e-4
+    assert rel(torch.cat(us, 0), s_all.U) < 1e-4
+
+
 # ----------------------------------------------------------------- chunked tensor-core path --
 
 @pytest.mark.parametrize("T,rope_rf", [(64, None), (1, None), (100, 0.5), (256, 0.5), (130, 0.25)])
