@@ -160,3 +160,24 @@ def test_device_status_word():
         ops.check_device_status(ws)
     ops.gdn3_scan(*args, decay_kind="log", algo="chunked", workspace=ws)  # every call clears it
     assert ops.device_status(ws) == 0
+
+
+@pytest.mark.parametrize("kind", ["gamma", "braided"])
+def test_decay_kinds_on_the_chunked_path(kind):
+    """Decay given as gamma in (0, 1] or as the braided projection [.., 4], read by pass 1."""
+    B, T, H, M, K = 1, 150, 2, 4, 128
+    inp = scan_inputs(B, T, H, M, K, K, seed=80)
+    g = torch.Generator().manual_seed(81)
+    q, k, v, beta = (_bf(inp[n]) for n in ("q", "k", "v", "beta"))
+    if kind == "gamma":
+        dec_in = _bf(torch.exp(inp["logg"]))
+        gam = dec_in.float()
+    else:
+        dec_in = _bf(torch.randn(B, T, H, M, 4, generator=g) * 3)
+        gam = PR.braided_decay(dec_in.float())
+    logg = torch.log(gam)
+    Yo, So = _oracle(q.float(), k.float(), v.float(), beta.float(), logg, 0.5, M)
+    rope = lane_rope(M, K, K, 0.5)
+    y, S = ops.gdn3_scan(q.to(DEV), k.to(DEV), v.to(DEV), beta.to(DEV), beta.to(DEV), dec_in.to(DEV),
+                         decay_kind=kind, rope=rope, return_state=True, algo="chunked", out_dtype=torch.float32)
+    assert rel(y, Yo) < TOL16 and rel(S, So) < TOL16
