@@ -31,6 +31,7 @@
 // and on chunks that take the exact path (see FOLD_MIN_LC).  Every mbarrier wait is bounded (GDNX_ETIMEOUT in the
 // workspace error word, TMEM freed, kernel returns).
 #include <cuda.h>
+#include <cstdlib>
 #include <mutex>
 
 #include "chunk_common.cuh"
@@ -123,6 +124,7 @@ struct WyParams {
   __nv_bfloat16* tt;  // [N][nchunks][3][64*64] bf16 (T_e, T_w, Mq^T; swizzled tiles)
   float* lsum;        // [N][nchunks][64] log2 decay prefix
   int* err;
+  int64_t n0;         // first chain of this launch (a launch covers chains n0 .. n0 + grid chains - 1)
 };
 
 // Forward substitution for column c of one 16 x 16 diagonal block of T = (I + A)^{-1}
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   const gdnx_scan_args& a = P.a;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t npairs = (P.nchunks + 1) / 2;
-  const int64_t n = blockIdx.x / npairs, pair = blockIdx.x % npairs;
+  const int64_t n = P.n0 + blockIdx.x / npairs, pair = blockIdx.x % npairs;
   const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
   const int lm = (int)m;
   const int dpairs = (a.rope.enable && lm < 4) ? a.rope.pairs[lm] : 0;
@@ -739,7 +741,7 @@ __global__ void __launch_bounds__(S_NT, 1)
   const int quad = warp & 3;
   const int row = quad * 32 + lane;
   const uint32_t lbase = (uint32_t)(quad * 32) << 16;
-  const int64_t n = blockIdx.x;
+  const int64_t n = P.n0 + blockIdx.x;
   const int64_t m = n % a.M, h = (n / a.M) % a.H, b = n / (a.M * a.H);
   const int lm = (int)m;
   const int dpairs = (a.rope.enable && lm < 4) ? a.rope.pairs[lm] : 0;
@@ -1181,6 +1183,27 @@ size_t wy_workspace_bytes(const gdnx_scan_args& a) {
   return ERR_BYTES + (size_t)N * nch * (TT_ELEMS * 2 + C * 4);
 }
 
+constexpr int kMaxDevices = 64, kMaxPieces = 8;
+struct SideStream {
+  std::mutex mu;
+  bool init = false;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev[kMaxPieces + 1] = {};
+};
+SideStream g_side[kMaxDevices];  // per device, created on first use, kept until exit
+
+// Pieces for the pass-1 / pass-2 overlap: enough that each piece's pass 2 (one CTA per
+// chain and per SM) is a single wave, at most kMaxPieces; the environment variable
+// GDNX_WY_PIECES overrides the count (1 = no overlap).
+int wy_pieces(int64_t n_chains, int sms) {
+  static const int forced = [] {
+    const char* e = getenv("GDNX_WY_PIECES");
+    return e ? atoi(e) : 0;
+  }();
+  int64_t p = forced > 0 ? forced : (n_chains + sms - 1) / sms;
+  return (int)(p < 1 ? 1 : (p > kMaxPieces ? kMaxPieces : p));
+}
+
 gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st) {
   // TMA coordinates are 32-bit and pass 1 runs one CTA per (chain, chunk pair)
   const int64_t n_chains = a.B * a.H * a.M, n_pairs = ((a.T + C - 1) / C + 1) / 2;
@@ -1216,8 +1239,43 @@ gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st) {
       cudaFuncSetAttribute(wy_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_SMEM) != cudaSuccess)
     return GDNX_ELAUNCH;
   const int64_t npairs = (nch + 1) / 2;
-  wy_prep_kernel<<<(unsigned)(N * npairs), P_NT, P_SMEM, st>>>(P, maps);
-  wy_scan_kernel<<<(unsigned)N, S_NT, S_SMEM, st>>>(P, maps);
+  // The chains go in pieces: pass 1 of every piece on a side stream, pass 2 of piece i on
+  // the caller's stream once pass 1 of piece i is done, so pass 1 of later pieces fills
+  // the SMs that pass 2 (one CTA per SM) leaves idle in its last wave.
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0)
+    return GDNX_ELAUNCH;
+  const int pieces = wy_pieces(N, sms);
+  if (pieces == 1) {
+    P.n0 = 0;
+    wy_prep_kernel<<<(unsigned)(N * npairs), P_NT, P_SMEM, st>>>(P, maps);
+    wy_scan_kernel<<<(unsigned)N, S_NT, S_SMEM, st>>>(P, maps);
+  } else {
+    if (dev >= kMaxDevices) return GDNX_ELAUNCH;
+    SideStream& ss = g_side[dev];
+    std::lock_guard<std::mutex> lk(ss.mu);
+    if (!ss.init) {
+      if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess) return GDNX_ELAUNCH;
+      for (int i = 0; i < kMaxPieces + 1; ++i)
+        if (cudaEventCreateWithFlags(&ss.ev[i], cudaEventDisableTiming) != cudaSuccess) return GDNX_ELAUNCH;
+      ss.init = true;
+    }
+    // fork: the side stream starts after the caller's earlier work (and the error-word clear)
+    if (cudaEventRecord(ss.ev[kMaxPieces], st) != cudaSuccess ||
+        cudaStreamWaitEvent(ss.stream, ss.ev[kMaxPieces], 0) != cudaSuccess)
+      return GDNX_ELAUNCH;
+    for (int i = 0; i < pieces; ++i) {
+      const int64_t c0 = N * i / pieces, c1 = N * (i + 1) / pieces;
+      WyParams Pi = P;
+      Pi.n0 = c0;
+      wy_prep_kernel<<<(unsigned)((c1 - c0) * npairs), P_NT, P_SMEM, ss.stream>>>(Pi, maps);
+      if (cudaEventRecord(ss.ev[i], ss.stream) != cudaSuccess || cudaStreamWaitEvent(st, ss.ev[i], 0) != cudaSuccess)
+        return GDNX_ELAUNCH;
+      wy_scan_kernel<<<(unsigned)(c1 - c0), S_NT, S_SMEM, st>>>(Pi, maps);
+    }
+    // join: the last wait above orders every side-stream launch before the caller's later work
+  }
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
 }
 

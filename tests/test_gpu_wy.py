@@ -181,3 +181,18 @@ def test_decay_kinds_on_the_chunked_path(kind):
     y, S = ops.gdn3_scan(q.to(DEV), k.to(DEV), v.to(DEV), beta.to(DEV), beta.to(DEV), dec_in.to(DEV),
                          decay_kind=kind, rope=rope, return_state=True, algo="chunked", out_dtype=torch.float32)
     assert rel(y, Yo) < TOL16 and rel(S, So) < TOL16
+
+
+def test_chain_pieces_overlap_is_bit_identical():
+    """More chains than SMs: the library runs pass 1 of later chain pieces on a side stream
+    beside pass 2 of earlier ones.  Each chain's result must not depend on that split."""
+    B, T, H, M, K = 12, 96, 16, 4, 128  # 768 chains
+    inp = scan_inputs(B, T, H, M, K, K, seed=82)
+    args = [_bf(inp[n]).to(DEV) for n in ("q", "k", "v", "beta", "beta", "logg")]
+    rope = lane_rope(M, K, K, 0.5)
+    kw = dict(decay_kind="log", rope=rope, algo="chunked", return_state=True)
+    y, S = ops.gdn3_scan(*args, **kw)
+    for b0 in range(0, B, 2):  # 128 chains per call: one piece
+        yb, Sb = ops.gdn3_scan(*[t[b0:b0 + 2] for t in args], **kw)
+        assert torch.equal(yb, y[b0:b0 + 2])
+        assert torch.equal(Sb, S[b0 * H * M:(b0 + 2) * H * M])
