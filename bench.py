@@ -43,6 +43,17 @@ def chunk_flops_per_chain_token(dk, dv, C):
     return 6 * dk * dv + 2 * C * (3 * dk + 2 * dv)
 
 
+def wy_pieces(n_chains):
+    """Launch pairs (pass 1 + pass 2) one prefill call makes: the library cuts the chains into
+    single-wave pieces (one pass-2 CTA per SM) when at most 8 are needed."""
+    forced = int(os.environ.get("GDNX_WY_PIECES", "0") or 0)
+    if forced > 0:
+        return min(forced, 8)
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    p = -(-n_chains // sms)
+    return 1 if p > 8 else p
+
+
 def kr_flops_per_chain_token(P, R=4, av=16, ak=16, bv=8, bk=8, K=128, V=128):
     """GDN3-KR algorithmic FLOPs per chain-token with chunk = compaction period P."""
     f_compact = 2 * R * (av * ak) * (bv * bk) + 2 * V * K * P + 2 * (1 + 2 * 2) * (av * ak) * (bv * bk) * (R + 4)
@@ -455,7 +466,7 @@ def main():
                            "state": "fp32", "io": "bf16", "algo": args.algo,
                            "l2": "inputs 402 MB + outputs 537 MB > 126 MB L2 (no flush)",
                            "parallelism": f"(batch x head) shards, dp{world}"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * args.steps,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * wy_pieces(c["B"] * c["H"] * c["M"]) * args.steps,
                 "clocks": clocks, "decode": decode, "gather": gather, "kr": kr, "config4": cfg4}
         print(json.dumps(line), flush=True)
     if dist:

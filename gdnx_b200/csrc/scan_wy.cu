@@ -1193,15 +1193,17 @@ struct SideStream {
 SideStream g_side[kMaxDevices];  // per device, created on first use, kept until exit
 
 // Pieces for the pass-1 / pass-2 overlap: enough that each piece's pass 2 (one CTA per
-// chain and per SM) is a single wave, at most kMaxPieces; the environment variable
+// chain and per SM) is a single wave; none when that would take more than kMaxPieces
+// (multi-wave pieces measured slower than one launch).  The environment variable
 // GDNX_WY_PIECES overrides the count (1 = no overlap).
 int wy_pieces(int64_t n_chains, int sms) {
   static const int forced = [] {
     const char* e = getenv("GDNX_WY_PIECES");
     return e ? atoi(e) : 0;
   }();
-  int64_t p = forced > 0 ? forced : (n_chains + sms - 1) / sms;
-  return (int)(p < 1 ? 1 : (p > kMaxPieces ? kMaxPieces : p));
+  if (forced > 0) return forced > kMaxPieces ? kMaxPieces : forced;
+  const int64_t p = (n_chains + sms - 1) / sms;
+  return p > kMaxPieces ? 1 : (int)p;
 }
 
 gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st) {
