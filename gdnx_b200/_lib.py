@@ -16,7 +16,7 @@ GDNX_MODE_GDN3, GDNX_MODE_KMD2 = 0, 1
 GDNX_DECAY_GAMMA, GDNX_DECAY_LOG, GDNX_DECAY_BRAIDED = 0, 1, 2
 GDNX_ALGO_AUTO, GDNX_ALGO_RECURRENT, GDNX_ALGO_CHUNKED = 0, 1, 2
 
-EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_fwd_noalloc", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
+EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_fwd_noalloc", "gdnx_scan_noalloc_status", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
             "gdnx_decode_step", "gdnx_status_string", "gdnx_version")
 
 
@@ -87,6 +87,8 @@ def load(path: Path = LIB_PATH):
     lib.gdnx_scan_fwd.restype = C.c_int
     lib.gdnx_scan_fwd_noalloc.argtypes = [C.POINTER(ScanArgs), C.c_void_p]
     lib.gdnx_scan_fwd_noalloc.restype = C.c_int
+    lib.gdnx_scan_noalloc_status.argtypes = [C.POINTER(C.c_int32), C.c_void_p]
+    lib.gdnx_scan_noalloc_status.restype = C.c_int
     lib.gdnx_scan_workspace_bytes.argtypes = [C.POINTER(ScanArgs)]
     lib.gdnx_scan_workspace_bytes.restype = C.c_size_t
     lib.gdnx_kr_scan_fwd.argtypes = [C.POINTER(KrScanArgs), C.c_void_p]

@@ -137,6 +137,14 @@ gdnx_status gdnx_scan_fwd_noalloc(const gdnx_scan_args* a, void* stream) {
   return gdnx::launch_chunked_scan_static_scratch(*a, (cudaStream_t)stream);
 }
 
+gdnx_status gdnx_scan_noalloc_status(int32_t* device_error, void* stream) {
+  if (!device_error) return GDNX_EINVAL;
+  int word = 0;
+  const gdnx_status s = gdnx::static_scratch_status(&word, (cudaStream_t)stream);
+  if (s == GDNX_OK) *device_error = word;
+  return s;
+}
+
 gdnx_status gdnx_decode_step(const gdnx_decode_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
   if (a->B == 0) return GDNX_OK;

@@ -21,5 +21,7 @@ size_t wy_workspace_bytes(const gdnx_scan_args& a);
 gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st);
 // Single-pass kernel with its scratch in a library-owned static device array (no allocation).
 gdnx_status launch_chunked_scan_static_scratch(const gdnx_scan_args& a, cudaStream_t st);
+// Error word of that static array, read after the stream's work (synchronises the stream).
+gdnx_status static_scratch_status(int* out, cudaStream_t st);
 
 }  // namespace gdnx

@@ -638,6 +638,9 @@ namespace {
 
 constexpr size_t kStaticScratchBytes = 256;  // maximum scratch this variant offers
 static __device__ __align__(256) unsigned char g_chunked_scratch[kStaticScratchBytes];
+// The single-pass kernel's whole scratch need is its int32 error word; a kernel change
+// that needs more must grow the array (or this entry point must reject the request).
+static_assert(sizeof(int) <= kStaticScratchBytes, "the chunked kernel's scratch fits the static array");
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
@@ -661,6 +664,18 @@ gdnx_status static_scratch(void** out) {
 }
 
 }  // namespace
+
+gdnx_status static_scratch_status(int* out, cudaStream_t st) {
+  void* scratch = nullptr;
+  const gdnx_status s = static_scratch(&scratch);
+  if (s != GDNX_OK) return s;
+  int word = 0;
+  if (cudaMemcpyAsync(&word, scratch, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return GDNX_ELAUNCH;
+  *out = word;
+  return GDNX_OK;
+}
 
 gdnx_status launch_chunked_scan_static_scratch(const gdnx_scan_args& a, cudaStream_t st) {
   if (!chunked_eligible(a)) return GDNX_EUNSUPPORTED;

@@ -1183,27 +1183,68 @@ size_t wy_workspace_bytes(const gdnx_scan_args& a) {
   return ERR_BYTES + (size_t)N * nch * (TT_ELEMS * 2 + C * 4);
 }
 
-constexpr int kMaxDevices = 64, kMaxPieces = 8;
+constexpr int kMaxPieces = 8, kMaxSideStreams = 64;
+// A side stream (plus its events) belongs to one (device, caller stream) pair, so that
+// unrelated callers' pass-1 launches are never tied together and a capture of one
+// caller's stream pulls in only that caller's side stream.  Created on first use outside
+// stream capture, kept until exit.
 struct SideStream {
-  std::mutex mu;
-  bool init = false;
+  int dev = -1;
+  cudaStream_t caller = nullptr;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev[kMaxPieces + 1] = {};
+  std::mutex mu;  // held while a call enqueues on this side stream
 };
-SideStream g_side[kMaxDevices];  // per device, created on first use, kept until exit
+std::mutex g_side_mu;
+SideStream g_side[kMaxSideStreams];
+int g_side_count = 0;
+
+// The side stream of (dev, caller), created if `may_create`; nullptr when none is available
+// (table full, creation failed, or not created during a capture).
+SideStream* side_stream_for(int dev, cudaStream_t caller, bool may_create) {
+  std::lock_guard<std::mutex> lk(g_side_mu);
+  for (int i = 0; i < g_side_count; ++i)
+    if (g_side[i].dev == dev && g_side[i].caller == caller) return &g_side[i];
+  if (!may_create || g_side_count == kMaxSideStreams) return nullptr;
+  SideStream& ss = g_side[g_side_count];
+  if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  int made = 0;
+  for (; made < kMaxPieces + 1; ++made)
+    if (cudaEventCreateWithFlags(&ss.ev[made], cudaEventDisableTiming) != cudaSuccess) break;
+  if (made < kMaxPieces + 1) {  // undo the partial set-up
+    cudaGetLastError();
+    for (int i = 0; i < made; ++i) cudaEventDestroy(ss.ev[i]);
+    cudaStreamDestroy(ss.stream);
+    ss.stream = nullptr;
+    return nullptr;
+  }
+  ss.dev = dev;
+  ss.caller = caller;
+  ++g_side_count;
+  return &ss;
+}
 
 // Pieces for the pass-1 / pass-2 overlap: enough that each piece's pass 2 (one CTA per
 // chain and per SM) is a single wave; none when that would take more than kMaxPieces
 // (multi-wave pieces measured slower than one launch).  The environment variable
-// GDNX_WY_PIECES overrides the count (1 = no overlap).
+// GDNX_WY_PIECES overrides the count (1 = no overlap); never more pieces than chains.
 int wy_pieces(int64_t n_chains, int sms) {
   static const int forced = [] {
     const char* e = getenv("GDNX_WY_PIECES");
     return e ? atoi(e) : 0;
   }();
-  if (forced > 0) return forced > kMaxPieces ? kMaxPieces : forced;
-  const int64_t p = (n_chains + sms - 1) / sms;
-  return p > kMaxPieces ? 1 : (int)p;
+  int64_t p;
+  if (forced > 0) {
+    p = forced > kMaxPieces ? kMaxPieces : forced;
+  } else {
+    p = (n_chains + sms - 1) / sms;
+    if (p > kMaxPieces) p = 1;
+  }
+  if (p > n_chains) p = n_chains;
+  return p < 1 ? 1 : (int)p;
 }
 
 gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st) {
@@ -1248,35 +1289,44 @@ gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st) {
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
       sms <= 0)
     return GDNX_ELAUNCH;
-  const int pieces = wy_pieces(N, sms);
+  int pieces = wy_pieces(N, sms);
+  SideStream* ss = nullptr;
+  if (pieces > 1) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return GDNX_ELAUNCH;
+    ss = side_stream_for(dev, st, cap == cudaStreamCaptureStatusNone);
+    if (!ss) pieces = 1;
+  }
   if (pieces == 1) {
     P.n0 = 0;
     wy_prep_kernel<<<(unsigned)(N * npairs), P_NT, P_SMEM, st>>>(P, maps);
     wy_scan_kernel<<<(unsigned)N, S_NT, S_SMEM, st>>>(P, maps);
   } else {
-    if (dev >= kMaxDevices) return GDNX_ELAUNCH;
-    SideStream& ss = g_side[dev];
-    std::lock_guard<std::mutex> lk(ss.mu);
-    if (!ss.init) {
-      if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess) return GDNX_ELAUNCH;
-      for (int i = 0; i < kMaxPieces + 1; ++i)
-        if (cudaEventCreateWithFlags(&ss.ev[i], cudaEventDisableTiming) != cudaSuccess) return GDNX_ELAUNCH;
-      ss.init = true;
-    }
+    std::lock_guard<std::mutex> lk(ss->mu);
     // fork: the side stream starts after the caller's earlier work (and the error-word clear)
-    if (cudaEventRecord(ss.ev[kMaxPieces], st) != cudaSuccess ||
-        cudaStreamWaitEvent(ss.stream, ss.ev[kMaxPieces], 0) != cudaSuccess)
+    if (cudaEventRecord(ss->ev[kMaxPieces], st) != cudaSuccess ||
+        cudaStreamWaitEvent(ss->stream, ss->ev[kMaxPieces], 0) != cudaSuccess)
       return GDNX_ELAUNCH;
-    for (int i = 0; i < pieces; ++i) {
+    gdnx_status status = GDNX_OK;
+    for (int i = 0; i < pieces && status == GDNX_OK; ++i) {
       const int64_t c0 = N * i / pieces, c1 = N * (i + 1) / pieces;
       WyParams Pi = P;
       Pi.n0 = c0;
-      wy_prep_kernel<<<(unsigned)((c1 - c0) * npairs), P_NT, P_SMEM, ss.stream>>>(Pi, maps);
-      if (cudaEventRecord(ss.ev[i], ss.stream) != cudaSuccess || cudaStreamWaitEvent(st, ss.ev[i], 0) != cudaSuccess)
-        return GDNX_ELAUNCH;
+      wy_prep_kernel<<<(unsigned)((c1 - c0) * npairs), P_NT, P_SMEM, ss->stream>>>(Pi, maps);
+      if (cudaEventRecord(ss->ev[i], ss->stream) != cudaSuccess || cudaStreamWaitEvent(st, ss->ev[i], 0) != cudaSuccess) {
+        status = GDNX_ELAUNCH;
+        break;
+      }
       wy_scan_kernel<<<(unsigned)(c1 - c0), S_NT, S_SMEM, st>>>(Pi, maps);
     }
-    // join: the last wait above orders every side-stream launch before the caller's later work
+    // join: every side-stream launch is ordered before the caller's later work (on an error
+    // too, so nothing enqueued here outlives the call unjoined)
+    if (status != GDNX_OK) {
+      cudaGetLastError();
+      if (cudaEventRecord(ss->ev[kMaxPieces], ss->stream) == cudaSuccess)
+        cudaStreamWaitEvent(st, ss->ev[kMaxPieces], 0);
+      return status;
+    }
   }
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
 }

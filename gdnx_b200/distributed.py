@@ -61,3 +61,67 @@ def sharded_scan(scan_fn: Callable, inputs: dict, world: int, rank: int, group=N
     # heads: [world*B, T, h, M, V] -> [B, T, world*h, M, V]
     parts = parts.reshape((world,) + tuple(y.shape))
     return parts.permute(1, 2, 0, 3, 4, 5).reshape(y.shape[0], y.shape[1], H, *y.shape[3:])
+
+
+# ----------------------------------------------------------------------------
+# failure handling: bounded collectives, abort on timeout
+# ----------------------------------------------------------------------------
+
+class CollectiveTimeout(RuntimeError):
+    """A collective did not complete before its host-side deadline; the group was aborted."""
+
+
+def init_scan_group(backend: str = "nccl", timeout_s: float = 60.0, device_id=None) -> None:
+    """Initialise the default process group for sharded scans with failure handling on.
+
+    For NCCL the communicator is created non-blocking (``TORCH_NCCL_USE_COMM_NONBLOCKING``)
+    and asynchronous error handling is enabled (``TORCH_NCCL_ASYNC_ERROR_HANDLING``), so a
+    collective that outlives ``timeout_s`` is aborted by the process group's watchdog
+    (``ncclCommAbort``) instead of blocking the rank; :func:`gather_with_deadline` adds a
+    host-side deadline per call.  Rendezvous comes from the usual ``MASTER_*`` / ``RANK`` /
+    ``WORLD_SIZE`` environment.
+    """
+    import datetime
+    import os
+    import torch.distributed as dist
+    if backend == "nccl":
+        os.environ.setdefault("TORCH_NCCL_USE_COMM_NONBLOCKING", "1")
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
+    kw = {"device_id": device_id} if device_id is not None else {}
+    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
+
+
+def abort_group(group=None) -> None:
+    """Abort ``group`` (the default group when None): NCCL communicators are aborted
+    (``ncclCommAbort``), so no rank stays blocked in a collective a peer never joins.
+    Falls back to destroying the group where the backend has no abort."""
+    import torch.distributed as dist
+    from torch.distributed import distributed_c10d as c10d
+    try:
+        c10d._abort_process_group(group if group is not None else c10d.GroupMember.WORLD)
+    except Exception:
+        try:
+            dist.destroy_process_group(group)
+        except Exception:
+            pass
+
+
+def gather_with_deadline(out: torch.Tensor, local: torch.Tensor, timeout_s: float, group=None,
+                         poll_s: float = 0.01) -> torch.Tensor:
+    """``all_gather_into_tensor(out, local)`` that gives up after ``timeout_s`` seconds.
+
+    The collective is issued asynchronously and its completion polled on the host; past
+    the deadline the group is aborted (:func:`abort_group`) and :class:`CollectiveTimeout`
+    is raised, so a rank whose peer died or never joined learns of it instead of hanging.
+    """
+    import time
+    import torch.distributed as dist
+    work = dist.all_gather_into_tensor(out, local, group=group, async_op=True)
+    deadline = time.monotonic() + timeout_s
+    while not work.is_completed():
+        if time.monotonic() > deadline:
+            abort_group(group)
+            raise CollectiveTimeout(f"all-gather did not complete within {timeout_s:.1f} s; group aborted")
+        time.sleep(poll_s)
+    work.wait()
+    return out

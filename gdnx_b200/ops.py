@@ -144,17 +144,29 @@ _WORKSPACES = {}
 # ----------------------------------------------------------------------------
 
 _HOST_BUFS = {}
+_HOST_BUF_CONFIGS = 4  # buffer configurations kept resident (least recently used dropped first)
+_HOST_STREAMS = {}
 
 
 def _host_pipeline_buffers(device, shapes_dtypes):
     """Two device buffer sets (double buffering) for the sliced host scan, cached by shape."""
     key = (device.index,) + tuple(shapes_dtypes)
-    bufs = _HOST_BUFS.get(key)
+    bufs = _HOST_BUFS.pop(key, None)
     if bufs is None:
         bufs = [[torch.empty(shp, dtype=dt, device=device) for shp, dt in shapes_dtypes] for _ in range(2)]
-        _HOST_BUFS.clear()  # keep one configuration resident
-        _HOST_BUFS[key] = bufs
+        while len(_HOST_BUFS) >= _HOST_BUF_CONFIGS:
+            _HOST_BUFS.pop(next(iter(_HOST_BUFS)))
+    _HOST_BUFS[key] = bufs  # most recently used last
     return bufs
+
+
+def _host_copy_streams(device):
+    """The copy-in and copy-out streams of the host scan on ``device`` (created once)."""
+    ss = _HOST_STREAMS.get(device.index)
+    if ss is None:
+        ss = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+        _HOST_STREAMS[device.index] = ss
+    return ss
 
 
 def gdn3_scan_host(q, k, v, b_gate, w_gate, decay, *, out: torch.Tensor, device=None, slices: Optional[int] = None,
@@ -184,7 +196,7 @@ def gdn3_scan_host(q, k, v, b_gate, w_gate, decay, *, out: torch.Tensor, device=
     bufs = _host_pipeline_buffers(device, shapes)
     with torch.cuda.device(device):
         main = torch.cuda.current_stream(device)
-        h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        h2d, d2h = _host_copy_streams(device)
         h2d.wait_stream(main)
         d2h.wait_stream(main)
         done_in = [torch.cuda.Event() for _ in range(nsl)]
@@ -490,3 +502,15 @@ def gdn3_scan_noalloc(q, k, v, b_gate, w_gate, decay, *, decay_kind="gamma", rop
     with torch.cuda.device(q.device):
         L.check(lib.gdnx_scan_fwd_noalloc(C.byref(a), C.c_void_p(_stream(q.device))), "gdnx_scan_fwd_noalloc")
     return out
+
+
+def noalloc_status(device=None) -> int:
+    """Device error word of the allocation-free scans on ``device`` (after the current
+    stream's work; synchronises it): 0, or ``GDNX_ETIMEOUT`` if a kernel gave up a
+    bounded wait (its outputs are then invalid).  The next such scan clears it."""
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    lib = L.load()
+    word = C.c_int32(0)
+    with torch.cuda.device(device):
+        L.check(lib.gdnx_scan_noalloc_status(C.byref(word), C.c_void_p(_stream(device))), "gdnx_scan_noalloc_status")
+    return int(word.value)

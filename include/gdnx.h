@@ -155,14 +155,21 @@ GDNX_API size_t gdnx_scan_workspace_bytes(const gdnx_scan_args* args);
  * results as gdnx_scan_fwd with algo = GDNX_ALGO_CHUNKED, but `workspace` /
  * `workspace_bytes` are ignored: the kernel's scratch (its device error word)
  * lives in a 256-byte array that the library keeps in every GPU that loads it
- * until the process exits.  Requests the chunked kernel cannot take return
- * GDNX_EUNSUPPORTED; a scratch need above the 256-byte maximum returns
- * GDNX_EWORKSPACE.  The first call on a device looks the array's device
- * address up (once per device); make that first call before any stream
- * capture.  Every call shares the array and clears it on the stream before
- * the kernel, so calls that overlap on the GPU (other streams, other host
- * threads) race on it.  Nothing is allocated or freed. */
+ * until the process exits.  The single-pass kernel this entry point runs needs
+ * only that word (a compile-time check keeps it within the array).  Requests
+ * the chunked kernel cannot take return GDNX_EUNSUPPORTED.  The first call on
+ * a device looks the array's device address up (once per device); make that
+ * first call before any stream capture.  Every call shares the array and
+ * clears it on the stream before the kernel, so calls that overlap on the GPU
+ * (other streams, other host threads) race on it.  Nothing is allocated or
+ * freed.  gdnx_scan_noalloc_status reads the word back. */
 GDNX_API gdnx_status gdnx_scan_fwd_noalloc(const gdnx_scan_args* args, void* stream);
+
+/* Device error word of gdnx_scan_fwd_noalloc's static array after the work on
+ * `stream` has finished (the call synchronises `stream`): 0, or GDNX_ETIMEOUT
+ * when a kernel gave up a bounded wait and its outputs are invalid.  The next
+ * gdnx_scan_fwd_noalloc call clears it.  No counterpart in the reference. */
+GDNX_API gdnx_status gdnx_scan_noalloc_status(int32_t* device_error, void* stream);
 
 /* Kronecker-residual (GDN3-KR) scan with periodic compaction. */
 typedef struct {

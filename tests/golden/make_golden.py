@@ -17,6 +17,11 @@ seeded inputs, what they return:
 * ``kmd2.pt``          -- ``research/kernel_ab/ref_scan.scan`` and
   ``research/kmd2_ablation/exact_cache.reference_scan_with_scores``.
 * ``compaction.pt``    -- one ``GDN3LinearAttn._compact_vec`` call.
+* ``gdn3_kr_p256.pt``  -- the frozen loop at config 2's compaction period
+  (P = 256, R = 4, A 16x16 (x) B 8x8, d = 128, one head of four lanes, bf16-rounded
+  config-2 inputs, T = 1024: four compactions) -- every 8th token and the last
+  one, plus the relative L2 distance of the
+  reference's own chunked ``_gdn3_recurrent_state`` from it (its floor).
 * ``prologue.pt``      -- braided decay (``forward`` lines 809-822 restated by
   calling the same torch ops on the module's buffers) and ``_apply_partial_rope``.
 """
@@ -120,6 +125,24 @@ def make_kmd2():
     torch.save(out, HERE / 'kmd2.pt')
 
 
+def make_kr_p256():
+    from gdn3._reference_recurrence import reference_recurrent_state
+    from oracle.inputs import scan_inputs, expand_lanes
+    B, T, H, M, K = 1, 1024, 1, 4, 128
+    inp = scan_inputs(B, T, H, M, K, K, seed=2, dtype=torch.bfloat16)
+    ins = [t.contiguous() for t in expand_lanes(inp, M)]
+    L = _layer(K, K, 256)
+    with torch.no_grad():
+        Y = reference_recurrent_state(L, *ins)
+        Yc = L._gdn3_recurrent_state(*ins)
+    keep = list(range(0, T, 8)) + [T - 1]
+    floor = ((Yc - Y).double().norm() / Y.double().norm()).item()
+    torch.save(dict(shape=(B, T, H, M, K), seed=2, P=256, dims=(16, 16, 8, 8), t_index=torch.tensor(keep),
+                    Y=Y[:, keep].clone(), Y_sum=Y.double().sum(), Y_sq=Y.double().square().sum(),
+                    chunked_floor=floor),
+               HERE / 'gdn3_kr_p256.pt')
+
+
 def make_compaction():
     g = torch.Generator().manual_seed(5)
     N, R, V, K, P = 6, 4, 128, 128, 16
@@ -156,10 +179,11 @@ if __name__ == '__main__':
         raise SystemExit('usage: make_golden.py /path/to/reference')
     sys.path.insert(0, REF)
     torch.manual_seed(0)
-    make_gdn3_frozen()
-    make_gdn3_config0()
-    make_kmd2()
-    make_compaction()
-    make_prologue()
+    makers = dict(gdn3_frozen=make_gdn3_frozen, gdn3_config0=make_gdn3_config0, kmd2=make_kmd2,
+                  compaction=make_compaction, prologue=make_prologue, gdn3_kr_p256=make_kr_p256)
+    only = sys.argv[2:]  # optional fixture names; default: all
+    for name, fn in makers.items():
+        if not only or name in only:
+            fn()
     for f in sorted(HERE.glob('*.pt')):
         print(f.name, f.stat().st_size)

@@ -84,3 +84,66 @@ def test_rank_failure_surfaces_as_error_on_the_other_rank():
     res = _run(4, 2, fail_rank=1)
     assert res[1][0] == "error" and "injected" in res[1][1]
     assert res[0][0] == "error"  # its collective cannot complete: gloo reports it instead of hanging
+
+
+def _deadline_worker(rank, world, port, out_q, absent_rank):
+    """Rank ``absent_rank`` never joins the gather (it stays alive, idle, until the end)."""
+    import time
+    from gdnx_b200.distributed import CollectiveTimeout, gather_with_deadline, init_scan_group
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    init_scan_group("gloo", timeout_s=30)
+    x = torch.full((4,), float(rank))
+    out = torch.empty(4 * world)
+    try:
+        if rank == absent_rank:
+            time.sleep(6)
+            out_q.put((rank, "absent", 0.0))
+            return
+        t0 = time.monotonic()
+        try:
+            gather_with_deadline(out, x, timeout_s=1.5)
+            out_q.put((rank, "completed", time.monotonic() - t0))
+        except CollectiveTimeout as e:
+            out_q.put((rank, "timeout", time.monotonic() - t0))
+    except Exception as e:
+        out_q.put((rank, "error", type(e).__name__ + ": " + str(e)[:120]))
+
+
+def test_gather_deadline_aborts_instead_of_hanging():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_deadline_worker, args=(r, 2, port, q, 1)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict((r, (s, v)) for r, s, v in (q.get(timeout=120) for _ in ps))
+    for p in ps:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert res[1][0] == "absent"
+    assert res[0][0] == "timeout", res[0]
+    assert 1.4 < res[0][1] < 10.0  # gave up at its deadline, not at the group's 30 s timeout
+
+
+def _deadline_ok_worker(rank, world, port, out_q):
+    from gdnx_b200.distributed import gather_with_deadline, init_scan_group
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    init_scan_group("gloo", timeout_s=30)
+    out = torch.empty(4 * world)
+    gather_with_deadline(out, torch.full((4,), float(rank)), timeout_s=20)
+    out_q.put((rank, "ok", float(out.sum())))
+    dist.destroy_process_group()
+
+
+def test_gather_with_deadline_completes_normally():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_deadline_ok_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(timeout=30)
+    assert all(s == "ok" and v == 4.0 for _, s, v in res), res

@@ -51,6 +51,19 @@ def test_gdn3_config0_dense_bit_exact_and_dense_form():
     assert rel_l2(S, S_kr) < 1e-5
 
 
+def test_gdn3_kr_loop_at_config2_period_bit_exact():
+    """P = 256 (config 2's compaction period), four compactions, bf16-rounded inputs."""
+    c = _load("gdn3_kr_p256.pt")
+    B, T, H, M, K = c["shape"]
+    inp = scan_inputs(B, T, H, M, K, K, seed=c["seed"], dtype=torch.bfloat16)
+    ins = [t.contiguous() for t in expand_lanes(inp, M)]
+    Y, st = R.gdn3_kr_scan(*ins, R=4, P=c["P"], dims=R.KronDims(*c["dims"]))
+    assert torch.equal(Y[:, c["t_index"]], c["Y"])
+    assert Y.double().sum() == c["Y_sum"]
+    assert st.p == T % c["P"]
+    assert c["chunked_floor"] < 2e-3
+
+
 @pytest.mark.parametrize("case", ["r1", "r4"])
 def test_kmd2_loop_bit_exact(case):
     c = _load("kmd2.pt")[case]

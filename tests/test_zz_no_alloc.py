@@ -37,6 +37,7 @@ def test_noalloc_matches_the_allocating_entry_two_calls_in_a_row(T):
         torch.cuda.synchronize()
         assert rel(y.float(), y_ref.float()) < TOL16, call
         assert rel(S, S_ref) < TOL16, call
+        assert ops.noalloc_status(DEV) == 0, call  # no bounded wait gave up
 
 
 def test_noalloc_rejects_requests_the_chunked_kernel_cannot_take():
