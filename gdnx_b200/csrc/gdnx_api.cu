@@ -63,6 +63,21 @@ gdnx_status check_common(int64_t B, int64_t H, int64_t M, int64_t K, int64_t V, 
   return GDNX_OK;
 }
 
+// Which kernel family gdnx_scan_fwd runs for a request.
+enum class Path { kRecurrent, kWy, kGeneral };
+
+Path select_path(const gdnx_scan_args& a) {
+  if (a.algo == GDNX_ALGO_RECURRENT) return Path::kRecurrent;
+  if (gdnx::chunked_eligible(a)) return Path::kWy;
+  if (!gdnx::wy_general_eligible(a)) return Path::kRecurrent;
+  if (a.algo == GDNX_ALGO_CHUNKED) return Path::kGeneral;
+  // automatic choice: GDN3 with fp32 q/k/v keeps the exact fp32 recurrence (its contract is
+  // fp32 accuracy); every other form takes the tensor cores
+  const bool f32 = a.q.dtype == GDNX_F32 || a.k.dtype == GDNX_F32 || a.v.dtype == GDNX_F32;
+  if (a.mode == GDNX_MODE_GDN3 && f32) return Path::kRecurrent;
+  return Path::kGeneral;
+}
+
 }  // namespace
 
 extern "C" {
@@ -83,8 +98,11 @@ const char* gdnx_version(void) { return "gdnx-b200 0.1 sm_100a"; }
 
 size_t gdnx_scan_workspace_bytes(const gdnx_scan_args* a) {
   if (!a) return 0;
-  if (a->algo != GDNX_ALGO_RECURRENT && gdnx::chunked_eligible(*a)) return gdnx::chunked_workspace_bytes(*a);
-  return 0;
+  switch (select_path(*a)) {
+    case Path::kWy: return gdnx::chunked_workspace_bytes(*a);
+    case Path::kGeneral: return gdnx::wy_general_workspace_bytes(*a);
+    default: return 0;
+  }
 }
 
 gdnx_status gdnx_scan_fwd(const gdnx_scan_args* a, void* stream) {
@@ -112,12 +130,13 @@ gdnx_status gdnx_scan_fwd(const gdnx_scan_args* a, void* stream) {
   if (a->state_in && !is_device_ptr(a->state_in)) return GDNX_EINVAL;
   if (a->state_out && !is_device_ptr(a->state_out)) return GDNX_EINVAL;
   cudaStream_t st = (cudaStream_t)stream;
-  const bool chunk_ok = gdnx::chunked_eligible(*a);
-  if (a->algo == GDNX_ALGO_CHUNKED && !chunk_ok) return GDNX_EUNSUPPORTED;
-  if (a->algo != GDNX_ALGO_RECURRENT && chunk_ok) {
-    if (a->workspace_bytes < gdnx::chunked_workspace_bytes(*a)) return GDNX_EWORKSPACE;
-    if (gdnx::chunked_workspace_bytes(*a) && !is_device_ptr(a->workspace)) return GDNX_EWORKSPACE;
-    return gdnx::launch_chunked_scan(*a, st);
+  const Path path = select_path(*a);
+  if (a->algo == GDNX_ALGO_CHUNKED && path == Path::kRecurrent) return GDNX_EUNSUPPORTED;
+  if (path != Path::kRecurrent) {
+    const size_t need = gdnx_scan_workspace_bytes(a);
+    if (a->workspace_bytes < need) return GDNX_EWORKSPACE;
+    if (need && !is_device_ptr(a->workspace)) return GDNX_EWORKSPACE;
+    return path == Path::kWy ? gdnx::launch_chunked_scan(*a, st) : gdnx::launch_wy_general(*a, st);
   }
   return gdnx::launch_recurrent_scan(*a, st);
 }

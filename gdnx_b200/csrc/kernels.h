@@ -19,6 +19,12 @@ gdnx_status launch_chunked_scan(const gdnx_scan_args& a, cudaStream_t st);
 // TMA tensor maps (the single-pass kernel then runs instead).
 size_t wy_workspace_bytes(const gdnx_scan_args& a);
 gdnx_status launch_wy_scan(const gdnx_scan_args& a, cudaStream_t st);
+// General two-pass WY scan (scan_wy_general.cu): vector gates, per-channel decay,
+// query slots, scores, fp32/bf16/fp16 inputs.  Workspace = error word + one
+// record per chain and 64-token chunk.
+bool wy_general_eligible(const gdnx_scan_args& a);
+size_t wy_general_workspace_bytes(const gdnx_scan_args& a);
+gdnx_status launch_wy_general(const gdnx_scan_args& a, cudaStream_t st);
 // Single-pass kernel with its scratch in a library-owned static device array (no allocation).
 gdnx_status launch_chunked_scan_static_scratch(const gdnx_scan_args& a, cudaStream_t st);
 // Error word of that static array, read after the stream's work (synchronises the stream).
