@@ -127,50 +127,59 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_sample_rate(target_s, max_T=512, B=None):
-    """Oracle port (CPU restatement of the reference's frozen loop, dense case) on
-    a T-slice of config 1; returns (tok/s, threads, sample description)."""
-    from oracle import recurrence as R
+CPU_SAMPLE = dict(B=1, T=512)  # one batch row of config 1 (all 64 chains), first 512 tokens
+
+
+def cpu_sample_inputs():
     from oracle.inputs import scan_inputs, expand_lanes
+    c = CFG1
+    inp = scan_inputs(CPU_SAMPLE["B"], CPU_SAMPLE["T"], c["H"], c["M"], c["K"], c["V"], seed=1, dtype=torch.bfloat16)
+    return expand_lanes(inp, c["M"])
+
+
+def cpu_sample_rate(target_s):
+    """Oracle port (CPU restatement of the reference's frozen loop, dense case) on the
+    fixed config-1 slice CPU_SAMPLE, repeated for about ``target_s`` seconds; returns
+    (tok/s, threads, sample description)."""
+    from oracle import recurrence as R
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    c = dict(CFG1)
-    if B is not None:
-        c["B"] = B
-    T = 8
+    ins = cpu_sample_inputs()
+    R.dense_scan(*ins)
+    reps, t0 = 0, time.perf_counter()
     while True:
-        inp = scan_inputs(c["B"], T, c["H"], c["M"], c["K"], c["V"], seed=1, dtype=torch.bfloat16)
-        ins = expand_lanes(inp, c["M"])
-        t0 = time.perf_counter()
         R.dense_scan(*ins)
+        reps += 1
         dt = time.perf_counter() - t0
-        if dt >= target_s or T >= max_T:
+        if dt >= target_s:
             break
-        T = min(max_T, T * 2 if dt < target_s / 4 else int(T * target_s / dt * 1.1) + 1)
-    return c["B"] * T / dt, threads, f"config-1 T-slice B={c['B']},T={T},H=16,M=4,d=128 ({dt:.1f} s)", T
+    tok = CPU_SAMPLE["B"] * CPU_SAMPLE["T"]
+    return tok * reps / dt, threads, (f"config-1 slice B={CPU_SAMPLE['B']},T={CPU_SAMPLE['T']},H=16,M=4,d=128 "
+                                     f"x{reps} ({dt:.1f} s)")
 
 
 def run_reference(args, rank):
     """--impl reference: the reference recurrence restated on the CPU (rank 0 only)."""
     if rank != 0:
         return
-    rate0, threads, sample, T = cpu_sample_rate(target_s=2.0)
     from oracle import recurrence as R
-    from oracle.inputs import scan_inputs, expand_lanes
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    ins = cpu_sample_inputs()
     c = CFG1
-    inp = scan_inputs(c["B"], T, c["H"], c["M"], c["K"], c["V"], seed=1, dtype=torch.bfloat16)
-    ins = expand_lanes(inp, c["M"])
+    T = CPU_SAMPLE["T"]
     for _ in range(args.warmup):
         R.dense_scan(*ins)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         R.dense_scan(*ins)
     dt = (time.perf_counter() - t0) / args.steps
-    value = c["B"] * T / dt
+    sample = f"config-1 slice B={CPU_SAMPLE['B']},T={T},H=16,M=4,d=128 per step"
+    value = CPU_SAMPLE["B"] * T / dt
     line = {"impl": "reference", "metric": "chunked-scan prefill tok/s", "value": value, "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "config1-prefill T-slice", "B": c["B"], "T": T,
+            "data": "synthetic", "config": {"workload": "config1-prefill slice", "B": CPU_SAMPLE["B"], "T": T,
                                             "H": c["H"], "M": c["M"], "K": c["K"], "V": c["V"]},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -225,6 +234,10 @@ def main():
     ap.add_argument("--no-config4", dest="config4", action="store_false", help="skip the config-4 sharded prefill leg")
     ap.add_argument("--config4-T", type=int, default=None, help="override config-4 T (smoke runs only)")
     ap.add_argument("--config4-slabs", type=int, default=8)
+    ap.add_argument("--no-config4-ref-1gpu", dest="config4_ref_1gpu", action="store_false",
+                    help="skip timing the full config-4 scan on rank 0 alone (N > 1)")
+    ap.add_argument("--no-dropins", dest="dropins", action="store_false",
+                    help="skip the drop-in legs (module input forms)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -319,7 +332,7 @@ def main():
                   "collective": "nccl all_gather_into_tensor"}
         del full
 
-    # ---------------- config 4: sharded prefill with a T-slab pipelined all-gather ----------------
+    # ---------------- config 4: sharded prefill, fused lane epilogue, pipelined all-gather ----------------
     cfg4 = None
     if args.config4:
         c4 = dict(B=64, T=8192, H=16, M=4, K=128, V=128, chunk=64)
@@ -330,62 +343,90 @@ def main():
         lc = dict(c4)
         lc["B" if sh.axis == "batch" else "H"] = sh.stop - sh.start
         inp4 = make_prefill_inputs(lc, dev, seed=4 + rank)
+        gr = torch.Generator(device=dev).manual_seed(40 + rank)
+        router = torch.randn(lc["B"], lc["T"], lc["H"], lc["M"], device=dev, generator=gr).to(torch.bfloat16)
+        norm = 1 + 0.1 * torch.randn(lc["V"], device=dev, generator=gr)
+        rope4 = lane_rope(lc["M"], lc["K"], lc["K"], 0.5)
+        yfull = torch.empty(lc["B"], lc["T"], lc["H"], lc["M"], lc["V"], dtype=torch.bfloat16, device=dev)
+
+        def scan_only():  # one call per rank over the whole sequence
+            ops.gdn3_scan(inp4["q"], inp4["k"], inp4["v"], inp4["beta"], inp4["beta"], inp4["logg"], decay_kind="log",
+                          rope=rope4, out=yfull)
+
+        ms4 = timed(scan_only, 3, 3, stream, barrier)
+        del yfull
         slabs = args.config4_slabs
         Ts = lc["T"] // slabs
-        ybuf = [torch.empty(lc["B"], Ts, lc["H"], lc["M"], lc["V"], dtype=torch.bfloat16, device=dev)
-                for _ in range(2)]
-        gbuf = [torch.empty((world * lc["B"], Ts, lc["H"], lc["M"], lc["V"]), dtype=torch.bfloat16, device=dev)
+        ybuf = [torch.empty(lc["B"], Ts, lc["H"], lc["M"], lc["V"], dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        rbuf = [torch.empty(lc["B"], Ts, lc["H"], lc["V"], dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        gbuf = [torch.empty((world * lc["B"], Ts, lc["H"], lc["V"]), dtype=torch.bfloat16, device=dev)
                 for _ in range(2)] if dist else None
         st = torch.zeros(lc["B"] * lc["H"] * lc["M"], lc["V"], lc["K"], dtype=torch.float32, device=dev)
         comm = torch.cuda.Stream(dev)
         ev_scan = [torch.cuda.Event() for _ in range(2)]
         ev_comm = [torch.cuda.Event() for _ in range(2)]
 
-        def slab_scan(i, state):
+        def slab(i, state):
             sl = slice(i * Ts, (i + 1) * Ts)
             _, so = ops.gdn3_scan(inp4["q"][:, sl], inp4["k"][:, sl], inp4["v"][:, sl], inp4["beta"][:, sl],
                                   inp4["beta"][:, sl], inp4["logg"][:, sl], decay_kind="log",
                                   rope=lane_rope(lc["M"], lc["K"], lc["K"], 0.5, pos0=i * Ts), state=state,
                                   return_state=True, out=ybuf[i % 2])
+            ops.lane_route(ybuf[i % 2], router[:, sl], norm, out=rbuf[i % 2])
             return so
 
-        def scan_only():
-            state = st
-            for i in range(slabs):
-                state = slab_scan(i, state)
-
-        def scan_and_gather():
+        def scan_route_gather():
             state = st
             for i in range(slabs):
                 if i >= 2:
-                    stream.wait_event(ev_comm[i % 2])  # ybuf[i % 2] gathered
-                state = slab_scan(i, state)
+                    stream.wait_event(ev_comm[i % 2])  # rbuf[i % 2] gathered
+                state = slab(i, state)
                 if dist:
                     ev_scan[i % 2].record(stream)
                     with torch.cuda.stream(comm):
                         comm.wait_event(ev_scan[i % 2])
-                        dist.all_gather_into_tensor(gbuf[i % 2], ybuf[i % 2])
+                        dist.all_gather_into_tensor(gbuf[i % 2], rbuf[i % 2])
                         ev_comm[i % 2].record(comm)
             if dist:
                 stream.wait_stream(comm)
 
-        ms4 = timed(scan_only, 3, 3, stream, barrier)
-        ms4e = timed(scan_and_gather, 3, 3, stream, barrier)
+        ms4e = timed(scan_route_gather, 3, 3, stream, barrier)
         ms4g = None
         if dist:
-            ms4g = timed(lambda: dist.all_gather_into_tensor(gbuf[0], ybuf[0]), 3, 1, stream, barrier) * slabs
+            ms4g = timed(lambda: dist.all_gather_into_tensor(gbuf[0], rbuf[0]), 3, 1, stream, barrier) * slabs
         vals = torch.tensor([ms4, ms4e, ms4g or 0.0], device=dev)
         if dist:
             dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         ms4, ms4e, ms4g = vals.tolist()
         tok4 = c4["B"] * c4["T"]
         f4 = c4["B"] * c4["T"] * c4["H"] * c4["M"] * chunk_flops_per_chain_token(128, 128, 64)
+        gathered = world * rbuf[0].numel() * rbuf[0].element_size() * slabs  # bytes of the full routed output
         cfg4 = {"workload": "config4: B=64,T=%d,H=16,M=4 sharded (batch x head) over %d rank(s)" % (c4["T"], world),
                 "scan_ms": ms4, "scan_tok_per_s": tok4 / (ms4 * 1e-3), "scan_tflops": f4 / (ms4 * 1e-3) / 1e12,
-                "allgather_ms_serial": ms4g if dist else None, "e2e_ms_pipelined": ms4e,
-                "e2e_tok_per_s": tok4 / (ms4e * 1e-3), "slabs": slabs,
-                "collective": "nccl all_gather_into_tensor per T-slab on a comm stream" if dist else None}
-        del inp4, ybuf, gbuf, st
+                "scan_tc_frac_per_rank": f4 / world / (ms4 * 1e-3) / 1e12 / peaks["bf16"],
+                "e2e_ms_pipelined": ms4e, "e2e_tok_per_s": tok4 / (ms4e * 1e-3), "slabs": slabs,
+                "epilogue": "gdnx_epilogue lane routing + head norm per slab (routed [B,T,H,V] bf16)",
+                "allgather_ms_serial": ms4g if dist else None,
+                "allgather_bytes_total": gathered if dist else None,
+                "nccl_busbw_gbs": (gathered * (world - 1) / world / (ms4g * 1e-3) / 1e9) if dist else None,
+                "collective": "nccl all_gather_into_tensor of routed slabs on a comm stream" if dist else None}
+        if dist and args.config4_ref_1gpu:
+            # the same full config-4 scan on one GPU (rank 0), for the per-N speed-up
+            t1 = torch.zeros(1, device=dev)
+            if rank == 0:
+                full = dict(c4)
+                inpf = make_prefill_inputs(full, dev, seed=4)
+                yf = torch.empty(full["B"], full["T"], full["H"], full["M"], full["V"], dtype=torch.bfloat16, device=dev)
+                t1[0] = timed(lambda: ops.gdn3_scan(inpf["q"], inpf["k"], inpf["v"], inpf["beta"], inpf["beta"],
+                                                    inpf["logg"], decay_kind="log", rope=rope4, out=yf),
+                              3, 3, stream, lambda: None)
+                del inpf, yf
+            barrier()
+            dist.all_reduce(t1, op=dist.ReduceOp.MAX)
+            cfg4["scan_ms_1gpu"] = t1.item()
+            cfg4["scan_speedup_vs_1gpu"] = t1.item() / ms4
+            cfg4["scan_efficiency"] = t1.item() / ms4 / world
+        del inp4, ybuf, rbuf, gbuf, st, router
 
     # ---------------- decode (config 3) ----------------
     decode = None
@@ -452,9 +493,58 @@ def main():
         kr = {"metric": "KR prefill tok/s (config 2)", "B": 1, "T": kc["T"], "H": 16, "M": 4,
               "state": "A 16x16 (x) B 8x8, R=4, + U,V 128xP, delta=0.97", **krs}
 
+    # ---------------- the drop-ins on the input forms the reference modules pass ----------------
+    dropins = None
+    if args.dropins:
+        from gdnx_b200 import kmd2_fast_scan
+        from gdnx_b200.gdn3_upgrade import gdn3_recurrent_state
+        import types
+        B, T, H, dk = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["K"]
+        g = torch.Generator(device=dev).manual_seed(11 + rank)
+        dropins = {}
+        # KMD2NativeAttn.forward -> kmd2_fast_scan: fp32 q [B,T,H,4,dk] (scaled), k, v, per-channel g
+        q = torch.nn.functional.normalize(torch.randn(B, T, H, 4, dk, device=dev, generator=g), dim=-1) * dk ** -0.5
+        k = torch.nn.functional.normalize(torch.randn(B, T, H, dk, device=dev, generator=g), dim=-1)
+        v = torch.randn(B, T, H, dk, device=dev, generator=g)
+        gd = torch.exp(-torch.nn.functional.softplus(1.2 * torch.randn(B, T, H, dk, device=dev, generator=g) - 0.6))
+        be = torch.sigmoid(torch.randn(B, T, H, device=dev, generator=g))
+        bw = torch.sigmoid(torch.randn(B, T, H, device=dev, generator=g))
+        mix = torch.randn(H, 4, device=dev, generator=g)
+        kms = timed(lambda: kmd2_fast_scan.scan_with_update_norm(q, k, v, gd, be, bw, mix), 5, 3, stream, barrier)
+        kf = B * T * H * chunk_flops_per_chain_token(dk, dk, 64)
+        dropins["kmd2_fast_scan"] = {
+            "call": "kmd2_fast_scan.scan_with_update_norm", "shape": f"B={B},T={T},H={H},r_out=4,dk=dv={dk} fp32, "
+            "per-channel decay, scores", "kernels": "wyg_prep_kernel + wyg_chain_kernel", "ms": kms,
+            "tok_per_s": B * T / (kms * 1e-3), "tflops": kf / (kms * 1e-3) / 1e12}
+        del q, k, v, gd, be, bw
+        # GDN3LinearAttn with bf16 features: per-lane rotated q/k, vector erase/write gates
+        M = CFG1["M"]
+        bf = torch.bfloat16
+        qx = torch.nn.functional.normalize(torch.randn(B, T, H, M, dk, device=dev, generator=g), dim=-1).to(bf)
+        kx = torch.nn.functional.normalize(torch.randn(B, T, H, M, dk, device=dev, generator=g), dim=-1).to(bf)
+        vx = torch.randn(B, T, H, M, dk, device=dev, generator=g).to(bf)
+        bg = torch.sigmoid(torch.randn(B, T, H, M, dk, device=dev, generator=g)).to(bf)
+        wg = torch.sigmoid(torch.randn(B, T, H, M, dk, device=dev, generator=g)).to(bf)
+        dec = 0.78 + 0.219 * torch.rand(B, T, H, M, device=dev, generator=g)
+        layer = types.SimpleNamespace(R=4, P=1 << 30, a_v=16, a_k=16, b_v=8, b_k=8, slow_decay=0.97,
+                                      compact_mode="svd")
+        gms = timed(lambda: gdn3_recurrent_state(layer, qx, kx, vx, bg, wg, dec), 5, 3, stream, barrier)
+        gf = B * T * H * M * chunk_flops_per_chain_token(dk, dk, 64)
+        dropins["gdn3_bf16_vector_gates"] = {
+            "call": "gdn3_upgrade.gdn3_recurrent_state (T < P: dense)", "shape": f"B={B},T={T},H={H},M={M},d={dk} "
+            "bf16 per-lane q/k/v, vector b/w gates, gamma decay", "kernels": "wyg_prep_kernel + wyg_chain_kernel",
+            "ms": gms, "tok_per_s": B * T / (gms * 1e-3), "tflops": gf / (gms * 1e-3) / 1e12}
+        qx, kx, vx, bg, wg = (t.float() for t in (qx, kx, vx, bg, wg))
+        fms = timed(lambda: gdn3_recurrent_state(layer, qx, kx, vx, bg, wg, dec), 2, 1, stream, barrier)
+        dropins["gdn3_fp32_exact"] = {
+            "call": "gdn3_upgrade.gdn3_recurrent_state (T < P: dense)", "shape": "as above, fp32 features "
+            "(what GDN3LinearAttn.forward passes)", "kernels": "recurrent_scan_kernel (exact fp32 contract)",
+            "ms": fms, "tok_per_s": B * T / (fms * 1e-3)}
+        del qx, kx, vx, bg, wg, dec
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, threads, sample, _ = cpu_sample_rate(target_s=10.0, max_T=4096)
+        rate, threads, sample = cpu_sample_rate(target_s=10.0)
         cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
 
     if rank == 0:
@@ -467,7 +557,7 @@ def main():
                            "l2": "inputs 402 MB + outputs 537 MB > 126 MB L2 (no flush)",
                            "parallelism": f"(batch x head) shards, dp{world}"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * wy_pieces(c["B"] * c["H"] * c["M"]) * args.steps,
-                "clocks": clocks, "decode": decode, "gather": gather, "kr": kr, "config4": cfg4}
+                "clocks": clocks, "decode": decode, "gather": gather, "kr": kr, "config4": cfg4, "dropins": dropins}
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()

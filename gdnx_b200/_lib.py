@@ -15,9 +15,10 @@ GDNX_F32, GDNX_BF16, GDNX_F16 = 0, 1, 2
 GDNX_MODE_GDN3, GDNX_MODE_KMD2 = 0, 1
 GDNX_DECAY_GAMMA, GDNX_DECAY_LOG, GDNX_DECAY_BRAIDED = 0, 1, 2
 GDNX_ALGO_AUTO, GDNX_ALGO_RECURRENT, GDNX_ALGO_CHUNKED = 0, 1, 2
+GDNX_EPILOGUE_LANE_ROUTE, GDNX_EPILOGUE_RMS_GATED = 0, 1
 
 EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_fwd_noalloc", "gdnx_scan_noalloc_status", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
-            "gdnx_decode_step", "gdnx_status_string", "gdnx_version")
+            "gdnx_decode_step", "gdnx_epilogue", "gdnx_status_string", "gdnx_version")
 
 
 class View(C.Structure):
@@ -71,6 +72,14 @@ class DecodeArgs(C.Structure):
                 ("y_sb", C.c_int64), ("y_sh", C.c_int64), ("y_sm", C.c_int64)]
 
 
+class EpilogueArgs(C.Structure):
+    _fields_ = [("B", C.c_int64), ("T", C.c_int64), ("H", C.c_int64), ("M", C.c_int64), ("V", C.c_int64),
+                ("kind", C.c_int32), ("eps", C.c_float),
+                ("y", View), ("router", View), ("gate", View), ("weight", C.c_void_p),
+                ("out", C.c_void_p), ("out_dtype", C.c_int32),
+                ("out_sb", C.c_int64), ("out_st", C.c_int64), ("out_sh", C.c_int64)]
+
+
 _lib = None
 
 
@@ -97,6 +106,8 @@ def load(path: Path = LIB_PATH):
     lib.gdnx_compact.restype = C.c_int
     lib.gdnx_decode_step.argtypes = [C.POINTER(DecodeArgs), C.c_void_p]
     lib.gdnx_decode_step.restype = C.c_int
+    lib.gdnx_epilogue.argtypes = [C.POINTER(EpilogueArgs), C.c_void_p]
+    lib.gdnx_epilogue.restype = C.c_int
     lib.gdnx_status_string.argtypes = [C.c_int]
     lib.gdnx_status_string.restype = C.c_char_p
     lib.gdnx_version.argtypes = []

@@ -514,3 +514,58 @@ def noalloc_status(device=None) -> int:
     with torch.cuda.device(device):
         L.check(lib.gdnx_scan_noalloc_status(C.byref(word), C.c_void_p(_stream(device))), "gdnx_scan_noalloc_status")
     return int(word.value)
+
+
+# ----------------------------------------------------------------------------
+# output epilogues
+# ----------------------------------------------------------------------------
+
+def lane_route(y: torch.Tensor, router_logits: torch.Tensor, norm: Optional[torch.Tensor] = None, *,
+               out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """GDN3 lane routing and per-head norm in one pass (gdn3/gdn3_upgrade.py:842-856):
+    ``softmax`` over the lanes of ``router_logits [B,T,H,M]``, the weighted lane sum of
+    ``y [B,T,H,M,V]``, then ``F.normalize(., dim=-1, eps=1e-6) * sqrt(V) * norm``.
+    Returns ``[B,T,H,V]`` (``out_dtype`` defaults to ``y``'s)."""
+    _require_cuda(y, router_logits, norm, out)
+    B, T, H, M, V = y.shape
+    out = out if out is not None else torch.empty(B, T, H, V, dtype=out_dtype or y.dtype, device=y.device)
+    a = L.EpilogueArgs()
+    a.B, a.T, a.H, a.M, a.V = B, T, H, M, V
+    a.kind = L.GDNX_EPILOGUE_LANE_ROUTE
+    a.y = _view(y, True)
+    a.router = _view(router_logits.unsqueeze(-1), True)
+    w = None
+    if norm is not None:
+        w = norm.detach().to(torch.float32).contiguous()
+        a.weight = w.data_ptr()
+    a.out, a.out_dtype = out.data_ptr(), _DT[out.dtype]
+    a.out_sb, a.out_st, a.out_sh = out.stride()[:3]
+    lib = L.load()
+    with torch.cuda.device(y.device):
+        L.check(lib.gdnx_epilogue(C.byref(a), C.c_void_p(_stream(y.device))), "gdnx_epilogue")
+    return out
+
+
+def rms_norm_gated(y: torch.Tensor, gate: torch.Tensor, weight: Optional[torch.Tensor] = None, *, eps: float = 1e-6,
+                   out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """KMD-2 output norm (``Qwen3_5RMSNormGated`` as called at gdn3/kmd2_native.py:176):
+    ``weight * y * rsqrt(mean(y^2) + eps) * silu(gate)`` over the last dim, computed in
+    fp32 from ``y [B,T,H,V]`` and ``gate [B,T,H,V]``; output in ``out_dtype`` (default the
+    gate's dtype)."""
+    _require_cuda(y, gate, weight, out)
+    B, T, H, V = y.shape
+    out = out if out is not None else torch.empty(B, T, H, V, dtype=out_dtype or gate.dtype, device=y.device)
+    a = L.EpilogueArgs()
+    a.B, a.T, a.H, a.M, a.V = B, T, H, 1, V
+    a.kind, a.eps = L.GDNX_EPILOGUE_RMS_GATED, eps
+    a.y, a.gate = _view(y, False), _view(gate, False)
+    w = None
+    if weight is not None:
+        w = weight.detach().to(torch.float32).contiguous()
+        a.weight = w.data_ptr()
+    a.out, a.out_dtype = out.data_ptr(), _DT[out.dtype]
+    a.out_sb, a.out_st, a.out_sh = out.stride()[:3]
+    lib = L.load()
+    with torch.cuda.device(y.device):
+        L.check(lib.gdnx_epilogue(C.byref(a), C.c_void_p(_stream(y.device))), "gdnx_epilogue")
+    return out

@@ -233,6 +233,35 @@ typedef struct {
 
 GDNX_API gdnx_status gdnx_decode_step(const gdnx_decode_args* args, void* stream);
 
+/* Output epilogues of the recurrent layers (one pass over the scan output). */
+typedef enum {
+  /* GDN3 lane routing + head norm (gdn3/gdn3_upgrade.py:842-856):
+   *   w = softmax_m(router[b,t,h,:]); r = sum_m w_m y[b,t,h,m,:];
+   *   out = r / max(|r|, 1e-6) * sqrt(V) * weight                              */
+  GDNX_EPILOGUE_LANE_ROUTE = 0,
+  /* KMD-2 gated RMS norm (Qwen3_5RMSNormGated; gdn3/kmd2_native.py:66,176):
+   *   out = weight * y * rsqrt(mean(y^2) + eps) * silu(gate)                   */
+  GDNX_EPILOGUE_RMS_GATED = 1
+} gdnx_epilogue_kind;
+
+typedef struct {
+  int64_t B, T, H, M, V;      /* M <= 8 lanes (LANE_ROUTE); V <= 128, a multiple of 4 */
+  int32_t kind;               /* gdnx_epilogue_kind */
+  float eps;                  /* RMS_GATED */
+  gdnx_view y;                /* [B,T,H,M,V] (LANE_ROUTE) or [B,T,H,V] (RMS_GATED)      */
+  gdnx_view router;           /* [B,T,H,M] router logits, dim 1 (LANE_ROUTE)           */
+  gdnx_view gate;             /* [B,T,H,V] gate z (RMS_GATED)                           */
+  const float* weight;        /* [V] fp32 device: the layer's norm weight; NULL = ones  */
+  void* out;                  /* [B,T,H,V] */
+  int32_t out_dtype;
+  int64_t out_sb, out_st, out_sh;
+} gdnx_epilogue_args;
+
+/* Replaces the lane routing and per-head norm that follow
+ * GDN3LinearAttn._gdn3_recurrent_state (gdn3/gdn3_upgrade.py:842-856) and the
+ * Qwen3_5RMSNormGated call after KMD2NativeAttn._scan (gdn3/kmd2_native.py:176). */
+GDNX_API gdnx_status gdnx_epilogue(const gdnx_epilogue_args* args, void* stream);
+
 GDNX_API const char* gdnx_status_string(gdnx_status s);
 
 /* Library build identification (for load checks). */

@@ -22,6 +22,9 @@ seeded inputs, what they return:
   config-2 inputs, T = 1024: four compactions) -- every 8th token and the last
   one, plus the relative L2 distance of the
   reference's own chunked ``_gdn3_recurrent_state`` from it (its floor).
+* ``epilogue.pt``      -- the GDN3 output epilogue (``forward`` lines 842-856 restated
+  by calling the same torch ops on a module's ``norm`` parameter, set to random
+  values) and ``Qwen3_5RMSNormGated`` from transformers on random inputs.
 * ``prologue.pt``      -- braided decay (``forward`` lines 809-822 restated by
   calling the same torch ops on the module's buffers) and ``_apply_partial_rope``.
 """
@@ -157,6 +160,31 @@ def make_compaction():
                     slow_decay=L.slow_decay), HERE / 'compaction.pt')
 
 
+def make_epilogue():
+    import torch.nn.functional as F
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5RMSNormGated
+    g = torch.Generator().manual_seed(13)
+    L = _layer(128, 128, 16)
+    with torch.no_grad():
+        L.norm.copy_(1.0 + 0.1 * torch.randn(128, generator=g))
+    y = torch.randn(2, 9, 2, 4, 128, generator=g)
+    logits = torch.randn(2, 9, 2, 4, generator=g)
+    V = 128
+    router_weights = F.softmax(logits, dim=-1)
+    routed = (router_weights.unsqueeze(-1) * y).sum(dim=3)
+    routed_normed = F.normalize(routed, p=2, dim=-1, eps=1e-6) * torch.sqrt(torch.tensor(float(V)))
+    out = routed_normed * L.norm
+    nm = Qwen3_5RMSNormGated(128, eps=1e-6)
+    with torch.no_grad():
+        nm.weight.copy_(1.0 + 0.1 * torch.randn(128, generator=g))
+    yk = torch.randn(2, 9, 2, 128, generator=g)
+    z = torch.randn(2, 9, 2, 128, generator=g)
+    with torch.no_grad():
+        ok = nm(yk, z)
+    torch.save(dict(y=y, logits=logits, norm=L.norm.detach().clone(), out=out.detach(),
+                    y_kmd2=yk, z=z, weight=nm.weight.detach().clone(), out_kmd2=ok), HERE / 'epilogue.pt')
+
+
 def make_prologue():
     g = torch.Generator().manual_seed(9)
     out = {}
@@ -180,7 +208,8 @@ if __name__ == '__main__':
     sys.path.insert(0, REF)
     torch.manual_seed(0)
     makers = dict(gdn3_frozen=make_gdn3_frozen, gdn3_config0=make_gdn3_config0, kmd2=make_kmd2,
-                  compaction=make_compaction, prologue=make_prologue, gdn3_kr_p256=make_kr_p256)
+                  compaction=make_compaction, prologue=make_prologue, gdn3_kr_p256=make_kr_p256,
+                  epilogue=make_epilogue)
     only = sys.argv[2:]  # optional fixture names; default: all
     for name, fn in makers.items():
         if not only or name in only:

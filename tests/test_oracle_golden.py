@@ -116,3 +116,10 @@ def test_lane_rope_bit_exact(rf):
 def test_braided_decay_bit_exact():
     c = _load("prologue.pt")["braid"]
     assert torch.equal(PR.braided_decay(c["decay_proj"], clamp=c["clamp"]), c["decay"])
+
+
+def test_epilogues_bit_exact():
+    from oracle import epilogue as E
+    c = _load("epilogue.pt")
+    assert torch.equal(E.lane_route(c["y"], c["logits"], c["norm"]), c["out"])
+    torch.testing.assert_close(E.rms_norm_gated(c["y_kmd2"], c["z"], c["weight"]), c["out_kmd2"], rtol=0, atol=0)
