@@ -372,23 +372,25 @@ def main():
                                   inp4["beta"][:, sl], inp4["logg"][:, sl], decay_kind="log",
                                   rope=lane_rope(lc["M"], lc["K"], lc["K"], 0.5, pos0=i * Ts), state=state,
                                   return_state=True, out=ybuf[i % 2])
-            ops.lane_route(ybuf[i % 2], router[:, sl], norm, out=rbuf[i % 2])
             return so
 
         def scan_route_gather():
+            # slab i's lane routing (HBM-bound) and all-gather run on a second stream while
+            # slab i+1 scans (tensor/latency-bound)
             state = st
             for i in range(slabs):
                 if i >= 2:
-                    stream.wait_event(ev_comm[i % 2])  # rbuf[i % 2] gathered
+                    stream.wait_event(ev_comm[i % 2])  # ybuf / rbuf [i % 2] consumed
                 state = slab(i, state)
-                if dist:
-                    ev_scan[i % 2].record(stream)
-                    with torch.cuda.stream(comm):
-                        comm.wait_event(ev_scan[i % 2])
+                ev_scan[i % 2].record(stream)
+                with torch.cuda.stream(comm):
+                    comm.wait_event(ev_scan[i % 2])
+                    sl = slice(i * Ts, (i + 1) * Ts)
+                    ops.lane_route(ybuf[i % 2], router[:, sl], norm, out=rbuf[i % 2])
+                    if dist:
                         dist.all_gather_into_tensor(gbuf[i % 2], rbuf[i % 2])
-                        ev_comm[i % 2].record(comm)
-            if dist:
-                stream.wait_stream(comm)
+                    ev_comm[i % 2].record(comm)
+            stream.wait_stream(comm)
 
         ms4e = timed(scan_route_gather, 3, 3, stream, barrier)
         ms4g = None

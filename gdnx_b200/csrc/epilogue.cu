@@ -1,4 +1,4 @@
-// Output epilogues of the recurrent layers, one warp per (batch, token, head) row:
+// Output epilogues of the recurrent layers, half a warp per (batch, token, head) row:
 //
 //   GDN3 lane routing (gdn3/gdn3_upgrade.py:842-856):
 //     w_m = softmax_m(router_logits[b,t,h,:]);  r = sum_m w_m y[b,t,h,m,:]
@@ -50,61 +50,142 @@ GDNX_DEV void st4f(void* p, int dtype, int64_t off, const float* x) {
   }
 }
 
-__global__ void __launch_bounds__(NT) epilogue_kernel(const gdnx_epilogue_args a) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
-  if (row >= a.B * a.T * a.H) return;
-  const int64_t h = row % a.H, t = (row / a.H) % a.T, b = row / (a.H * a.T);
+// Eight consecutive elements as fp32 (16-byte aligned).
+GDNX_DEV void ld8f(const void* p, int dtype, int64_t off, float* x) {
+  if (dtype == GDNX_BF16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + off);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __uint_as_float(w[i] << 16);
+      x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+    return;
+  }
+  ld4f(p, dtype, off, x);
+  ld4f(p, dtype, off + 4, x + 4);
+}
+GDNX_DEV void st8f(void* p, int dtype, int64_t off, const float* x) {
+  st4f(p, dtype, off, x);
+  st4f(p, dtype, off + 4, x + 4);
+}
+// Sum over the 16 lanes of a half warp.
+GDNX_DEV float half_sum(float x) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// Lane routing: a half warp per row (8 channels per lane), two passes of two rows per
+// warp with every load of both passes issued before the arithmetic.
+template <int MT>
+__global__ void __launch_bounds__(NT) lane_route_kernel(const gdnx_epilogue_args a) {
+  const int lane = threadIdx.x & 31, hw = lane >> 4, c = 8 * (lane & 15);
+  const int64_t rows = a.B * a.T * a.H;
+  const int64_t base = ((int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5)) * 4;
   const int V = (int)a.V;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  if (a.kind == GDNX_EPILOGUE_LANE_ROUTE) {
-    float lg[8];
-    float mx = -INFINITY;
-    for (int m = 0; m < a.M; ++m) {
-      lg[m] = ld_as_f32(a.router.ptr, a.router.dtype, b * a.router.sb + t * a.router.st + h * a.router.sh + m * a.router.sm);
-      mx = fmaxf(mx, lg[m]);
-    }
-    float den = 0.f;
-    for (int m = 0; m < a.M; ++m) {
-      lg[m] = expf(lg[m] - mx);
-      den += lg[m];
-    }
-    for (int m = 0; m < a.M; ++m) {
-      const float w = lg[m] / den;
-      const int c = 4 * lane;  // V <= 128: four values per lane
-      if (c < V) {
-        float y[4];
-        ld4f(a.y.ptr, a.y.dtype, b * a.y.sb + t * a.y.st + h * a.y.sh + m * a.y.sm + c, y);
+  float y[2][MT][8], lg[2][MT];
+  int64_t rb[2], rt[2], rh[2];
+  bool live[2];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = fmaf(w, y[e], acc[e]);
+  for (int p = 0; p < 2; ++p) {
+    const int64_t row = base + 2 * p + hw;
+    live[p] = row < rows && c < V;
+    {  // 32-bit index arithmetic (the launcher guarantees B*T*H < 2^31)
+      const uint32_t r32 = (uint32_t)row, H32 = (uint32_t)a.H, T32 = (uint32_t)a.T;
+      const uint32_t bt = r32 / H32;
+      rh[p] = r32 - bt * H32;
+      rb[p] = bt / T32;
+      rt[p] = bt - (uint32_t)rb[p] * T32;
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (live[p] && m < a.M) {
+        ld8f(a.y.ptr, a.y.dtype, rb[p] * a.y.sb + rt[p] * a.y.st + rh[p] * a.y.sh + m * a.y.sm + c, y[p][m]);
+        lg[p][m] = ld_as_f32(a.router.ptr, a.router.dtype,
+                             rb[p] * a.router.sb + rt[p] * a.router.st + rh[p] * a.router.sh + m * a.router.sm);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[p][m][e] = 0.f;
+        lg[p][m] = m < a.M ? 0.f : -INFINITY;  // lanes past M get zero weight
       }
     }
-    const float ss = warp_sum(acc[0] * acc[0] + acc[1] * acc[1] + acc[2] * acc[2] + acc[3] * acc[3]);
+  }
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    float mx = lg[p][0];
+#pragma unroll
+    for (int m = 1; m < MT; ++m) mx = fmaxf(mx, lg[p][m]);
+    float den = 0.f, w[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      w[m] = expf(lg[p][m] - mx);
+      den += w[m];
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float wm = w[m] / den;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wm, y[p][m][e], acc[e]);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(acc[e], acc[e], ss);
+    ss = half_sum(ss);
     const float sc = sqrtf((float)V) / fmaxf(sqrtf(ss), 1e-6f);
-    const int c = 4 * lane;
-    if (c < V) {
-      float o[4];
+    if (live[p]) {
+      float o[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) o[e] = acc[e] * sc * (a.weight ? a.weight[c + e] : 1.f);
-      st4f(a.out, a.out_dtype, b * a.out_sb + t * a.out_st + h * a.out_sh + c, o);
+      for (int e = 0; e < 8; ++e) o[e] = acc[e] * sc * (a.weight ? a.weight[c + e] : 1.f);
+      st8f(a.out, a.out_dtype, rb[p] * a.out_sb + rt[p] * a.out_st + rh[p] * a.out_sh + c, o);
     }
-  } else {  // GDNX_EPILOGUE_RMS_GATED
-    const int c = 4 * lane;
-    float y[4] = {0.f, 0.f, 0.f, 0.f}, z[4] = {0.f, 0.f, 0.f, 0.f};
-    if (c < V) {
-      ld4f(a.y.ptr, a.y.dtype, b * a.y.sb + t * a.y.st + h * a.y.sh + c, y);
-      ld4f(a.gate.ptr, a.gate.dtype, b * a.gate.sb + t * a.gate.st + h * a.gate.sh + c, z);
+  }
+}
+
+// Gated RMS norm: a half warp per row, four rows per warp, loads first.
+__global__ void __launch_bounds__(NT) rms_gated_kernel(const gdnx_epilogue_args a) {
+  const int lane = threadIdx.x & 31, hw = lane >> 4, c = 8 * (lane & 15);
+  const int64_t rows = a.B * a.T * a.H;
+  const int64_t base = ((int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5)) * 4;
+  const int V = (int)a.V;
+  float y[2][8], z[2][8];
+  int64_t rb[2], rt[2], rh[2];
+  bool live[2];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int64_t row = base + 2 * p + hw;
+    live[p] = row < rows && c < V;
+    {  // 32-bit index arithmetic (the launcher guarantees B*T*H < 2^31)
+      const uint32_t r32 = (uint32_t)row, H32 = (uint32_t)a.H, T32 = (uint32_t)a.T;
+      const uint32_t bt = r32 / H32;
+      rh[p] = r32 - bt * H32;
+      rb[p] = bt / T32;
+      rt[p] = bt - (uint32_t)rb[p] * T32;
     }
-    const float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
+    if (live[p]) {
+      ld8f(a.y.ptr, a.y.dtype, rb[p] * a.y.sb + rt[p] * a.y.st + rh[p] * a.y.sh + c, y[p]);
+      ld8f(a.gate.ptr, a.gate.dtype, rb[p] * a.gate.sb + rt[p] * a.gate.st + rh[p] * a.gate.sh + c, z[p]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[p][e] = z[p][e] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(y[p][e], y[p][e], ss);
+    ss = half_sum(ss);
     const float r = rsqrtf(ss / (float)V + a.eps);
-    if (c < V) {
-      float o[4];
+    if (live[p]) {
+      float o[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float sil = z[e] / (1.f + expf(-z[e]));
-        o[e] = (a.weight ? a.weight[c + e] : 1.f) * (y[e] * r) * sil;
+      for (int e = 0; e < 8; ++e) {
+        const float sil = z[p][e] / (1.f + expf(-z[p][e]));
+        o[e] = (a.weight ? a.weight[c + e] : 1.f) * (y[p][e] * r) * sil;
       }
-      st4f(a.out, a.out_dtype, b * a.out_sb + t * a.out_st + h * a.out_sh + c, o);
+      st8f(a.out, a.out_dtype, rb[p] * a.out_sb + rt[p] * a.out_st + rh[p] * a.out_sh + c, o);
     }
   }
 }
@@ -113,9 +194,20 @@ __global__ void __launch_bounds__(NT) epilogue_kernel(const gdnx_epilogue_args a
 
 gdnx_status launch_epilogue(const gdnx_epilogue_args& a, cudaStream_t st) {
   const int64_t rows = a.B * a.T * a.H;
-  const int64_t blocks = (rows + NT / 32 - 1) / (NT / 32);
-  if (blocks > int64_t(0x7fffffff)) return GDNX_EUNSUPPORTED;
-  epilogue_kernel<<<(unsigned)blocks, NT, 0, st>>>(a);
+  const int64_t per_block = 4 * (NT / 32);  // four rows per warp
+  const int64_t blocks = (rows + per_block - 1) / per_block;
+  if (rows >= int64_t(0x7fffffff)) return GDNX_EUNSUPPORTED;
+  if (a.kind == GDNX_EPILOGUE_RMS_GATED) {
+    rms_gated_kernel<<<(unsigned)blocks, NT, 0, st>>>(a);
+  } else if (a.M == 1) {
+    lane_route_kernel<1><<<(unsigned)blocks, NT, 0, st>>>(a);
+  } else if (a.M == 2) {
+    lane_route_kernel<2><<<(unsigned)blocks, NT, 0, st>>>(a);
+  } else if (a.M <= 4) {
+    lane_route_kernel<4><<<(unsigned)blocks, NT, 0, st>>>(a);
+  } else {
+    lane_route_kernel<8><<<(unsigned)blocks, NT, 0, st>>>(a);
+  }
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
 }
 

@@ -204,14 +204,13 @@ gdnx_status gdnx_compact(const gdnx_compact_args* a, void* stream) {
 
 gdnx_status gdnx_epilogue(const gdnx_epilogue_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
-  if (a->B < 0 || a->T < 0 || a->H <= 0 || a->V <= 0 || a->V > 128 || a->V % 4) return GDNX_EINVAL;
+  if (a->B < 0 || a->T < 0 || a->H <= 0 || a->V <= 0 || a->V > 128 || a->V % 8) return GDNX_EINVAL;
   if (a->kind != GDNX_EPILOGUE_LANE_ROUTE && a->kind != GDNX_EPILOGUE_RMS_GATED) return GDNX_EINVAL;
   if (a->B == 0 || a->T == 0) return GDNX_OK;
   auto vec_ok = [](const gdnx_view& v, int64_t dim) {
     if (!is_device_ptr(v.ptr) || !dtype_ok(v.dtype) || v.dim != dim) return false;
-    const int al = v.dtype == GDNX_F32 ? 16 : 8;
-    if (reinterpret_cast<uintptr_t>(v.ptr) % al) return false;
-    return v.sb % 4 == 0 && v.st % 4 == 0 && v.sh % 4 == 0 && v.sm % 4 == 0 && v.sb >= 0 && v.st >= 0 &&
+    if (reinterpret_cast<uintptr_t>(v.ptr) % 16) return false;
+    return v.sb % 8 == 0 && v.st % 8 == 0 && v.sh % 8 == 0 && v.sm % 8 == 0 && v.sb >= 0 && v.st >= 0 &&
            v.sh >= 0 && v.sm >= 0;
   };
   if (!vec_ok(a->y, a->V)) return GDNX_EINVAL;
@@ -224,7 +223,7 @@ gdnx_status gdnx_epilogue(const gdnx_epilogue_args* a, void* stream) {
   if (a->weight && !is_device_ptr(a->weight)) return GDNX_EINVAL;
   if (!is_device_ptr(a->out) || !dtype_ok(a->out_dtype)) return GDNX_EINVAL;
   const int al = a->out_dtype == GDNX_F32 ? 16 : 8;
-  if (reinterpret_cast<uintptr_t>(a->out) % al || a->out_sb % 4 || a->out_st % 4 || a->out_sh % 4) return GDNX_EINVAL;
+  if (reinterpret_cast<uintptr_t>(a->out) % al || a->out_sb % 8 || a->out_st % 8 || a->out_sh % 8) return GDNX_EINVAL;
   return gdnx::launch_epilogue(*a, (cudaStream_t)stream);
 }
 

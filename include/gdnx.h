@@ -245,7 +245,8 @@ typedef enum {
 } gdnx_epilogue_kind;
 
 typedef struct {
-  int64_t B, T, H, M, V;      /* M <= 8 lanes (LANE_ROUTE); V <= 128, a multiple of 4 */
+  int64_t B, T, H, M, V;      /* M <= 8 lanes (LANE_ROUTE); V <= 128, a multiple of 8;
+                                 y/gate/out strides multiples of 8 elements */
   int32_t kind;               /* gdnx_epilogue_kind */
   float eps;                  /* RMS_GATED */
   gdnx_view y;                /* [B,T,H,M,V] (LANE_ROUTE) or [B,T,H,V] (RMS_GATED)      */

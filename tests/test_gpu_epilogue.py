@@ -62,3 +62,13 @@ def test_scan_then_route_equals_oracle_chain():
     vx = f["v"].unsqueeze(3).expand(-1, -1, -1, 4, -1)
     Yo, _ = R.dense_scan(qx, kx, vx, f["beta"].unsqueeze(-1), f["beta"].unsqueeze(-1), torch.exp(f["logg"]))
     assert rel(out, E.lane_route(Yo, logits, norm)) < 2e-2
+
+
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_lane_route_lane_counts(M):
+    g = torch.Generator().manual_seed(6 + M)
+    y = torch.randn(2, 11, 3, M, 128, generator=g)
+    logits = torch.randn(2, 11, 3, M, generator=g)
+    norm = 1 + 0.1 * torch.randn(128, generator=g)
+    out = ops.lane_route(y.to(DEV), logits.to(DEV), norm.to(DEV))
+    assert rel(out, E.lane_route(y, logits, norm)) < 1e-5
