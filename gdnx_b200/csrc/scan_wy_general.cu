@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(P_NT, 2) wyg_prep_kernel(const GenParams P) {
     const int partner = role1 ? lane + dp4 : (role2 ? lane - dp4 : lane);
     const float4 lc4 = *reinterpret_cast<const float4*>(sLC + 4 * lane);
     const float lc[4] = {lc4.x, lc4.y, lc4.z, lc4.w};
-#pragma unroll
+#pragma unroll 1
     for (int jj = 0; jj < 8; ++jj) {
       const int j = 8 * warp + jj;
       const int64_t t = t0 + j;
@@ -377,9 +377,9 @@ __global__ void __launch_bounds__(P_NT, 2) wyg_prep_kernel(const GenParams P) {
       float fb[4], f0[4], fc[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        fb[e] = fast_exp2(Lr[jj][e] - an[e]);  // <= 1 within the block
-        f0[e] = fast_exp2(Lr[jj][e]);
-        fc[e] = fast_exp2(lc[e] - Lr[jj][e]);
+        fb[e] = exp2f(Lr[jj][e] - an[e]);  // <= 1 within the block
+        f0[e] = exp2f(Lr[jj][e]);
+        fc[e] = exp2f(lc[e] - Lr[jj][e]);
       }
       const int rh = 32 * J + (j & 15);
       st4_bf16(cHQ, sw_off4(rh, lane, 128), hv[0] * fb[0], hv[1] * fb[1], hv[2] * fb[2], hv[3] * fb[3]);
@@ -417,7 +417,7 @@ __global__ void __launch_bounds__(P_NT, 2) wyg_prep_kernel(const GenParams P) {
       const int l = 8 * warp + jj;
       float x[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) x[e] = (J >= (l >> 4)) ? kreg[jj][e] * fast_exp2(an[e] - Lr[jj][e]) : 0.f;
+      for (int e = 0; e < 4; ++e) x[e] = (J >= (l >> 4)) ? kreg[jj][e] * exp2f(an[e] - Lr[jj][e]) : 0.f;
       st4_bf16(kb, sw_off4(l, lane, 64), x[0], x[1], x[2], x[3]);
     }
     tc::fence_async_smem();
