@@ -18,7 +18,7 @@ GDNX_ALGO_AUTO, GDNX_ALGO_RECURRENT, GDNX_ALGO_CHUNKED = 0, 1, 2
 GDNX_EPILOGUE_LANE_ROUTE, GDNX_EPILOGUE_RMS_GATED = 0, 1
 
 EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_fwd_noalloc", "gdnx_scan_noalloc_status", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
-            "gdnx_decode_step", "gdnx_epilogue", "gdnx_status_string", "gdnx_version")
+            "gdnx_decode_step", "gdnx_epilogue", "gdnx_gdn3_prologue", "gdnx_status_string", "gdnx_version")
 
 
 class View(C.Structure):
@@ -80,6 +80,20 @@ class EpilogueArgs(C.Structure):
                 ("out_sb", C.c_int64), ("out_st", C.c_int64), ("out_sh", C.c_int64)]
 
 
+class PrologueArgs(C.Structure):
+    _fields_ = [("B", C.c_int64), ("T", C.c_int64), ("H", C.c_int64), ("M", C.c_int64), ("K", C.c_int64),
+                ("V", C.c_int64), ("C", C.c_int32), ("a_k", C.c_int32), ("b_k", C.c_int32), ("a_v", C.c_int32),
+                ("b_v", C.c_int32), ("conv_k", C.c_int32), ("qkv", View), ("conv_w", C.c_void_p),
+                ("q_a", View), ("q_b", View), ("k_a", View), ("k_b", View), ("v_a", View), ("v_b", View),
+                ("mix_qk", C.c_void_p), ("mix_v", C.c_void_p), ("str_qk", C.c_void_p), ("str_v", C.c_void_p),
+                ("b_proj", View), ("w_proj", View), ("proj_a", View), ("proj_b", View),
+                ("q_out", C.c_void_p), ("k_out", C.c_void_p), ("v_out", C.c_void_p), ("out_dtype", C.c_int32),
+                ("out_sb", C.c_int64), ("out_st", C.c_int64), ("out_sh", C.c_int64),
+                ("b_out", C.c_void_p), ("w_out", C.c_void_p), ("gate_dtype", C.c_int32),
+                ("gate_sb", C.c_int64), ("gate_st", C.c_int64), ("gate_sh", C.c_int64), ("gate_sm", C.c_int64),
+                ("wgate_sb", C.c_int64), ("wgate_st", C.c_int64), ("wgate_sh", C.c_int64), ("wgate_sm", C.c_int64)]
+
+
 _lib = None
 
 
@@ -108,6 +122,8 @@ def load(path: Path = LIB_PATH):
     lib.gdnx_decode_step.restype = C.c_int
     lib.gdnx_epilogue.argtypes = [C.POINTER(EpilogueArgs), C.c_void_p]
     lib.gdnx_epilogue.restype = C.c_int
+    lib.gdnx_gdn3_prologue.argtypes = [C.POINTER(PrologueArgs), C.c_void_p]
+    lib.gdnx_gdn3_prologue.restype = C.c_int
     lib.gdnx_status_string.argtypes = [C.c_int]
     lib.gdnx_status_string.restype = C.c_char_p
     lib.gdnx_version.argtypes = []

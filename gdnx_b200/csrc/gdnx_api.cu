@@ -227,6 +227,33 @@ gdnx_status gdnx_epilogue(const gdnx_epilogue_args* a, void* stream) {
   return gdnx::launch_epilogue(*a, (cudaStream_t)stream);
 }
 
+gdnx_status gdnx_gdn3_prologue(const gdnx_prologue_args* a, void* stream) {
+  if (!a) return GDNX_EINVAL;
+  if (a->B < 0 || a->T < 0 || a->H <= 0 || a->M <= 0 || a->K <= 0 || a->V <= 0 || a->V > a->K) return GDNX_EINVAL;
+  if (a->conv_k < 1 || a->C < 0) return GDNX_EINVAL;
+  if (a->B == 0 || a->T == 0) return GDNX_OK;
+  if (!is_device_ptr(a->qkv.ptr) || !dtype_ok(a->qkv.dtype) || a->qkv.dim != 3 * a->H * a->K) return GDNX_EINVAL;
+  if (!is_device_ptr(a->conv_w)) return GDNX_EINVAL;
+  const bool coprod = a->q_a.ptr != nullptr;
+  if (coprod) {
+    if (a->C < 1 || a->a_k * a->b_k != a->K || a->a_v * a->b_v != a->V) return GDNX_EINVAL;
+    const gdnx_view* f[6] = {&a->q_a, &a->q_b, &a->k_a, &a->k_b, &a->v_a, &a->v_b};
+    const int64_t d[6] = {a->a_k, a->b_k, a->a_k, a->b_k, a->a_v, a->b_v};
+    for (int i = 0; i < 6; ++i)
+      if (!is_device_ptr(f[i]->ptr) || !dtype_ok(f[i]->dtype) || f[i]->dim != d[i]) return GDNX_EINVAL;
+    if (!is_device_ptr(a->mix_qk) || !is_device_ptr(a->mix_v) || !is_device_ptr(a->str_qk) || !is_device_ptr(a->str_v))
+      return GDNX_EINVAL;
+  }
+  if (a->b_proj.ptr && (!view_ok(a->b_proj, (int)a->K) || !view_ok(a->proj_a, 1) || !is_device_ptr(a->b_out)))
+    return GDNX_EINVAL;
+  if (a->w_proj.ptr && (!view_ok(a->w_proj, (int)a->V) || !view_ok(a->proj_b, 1) || !is_device_ptr(a->w_out)))
+    return GDNX_EINVAL;
+  if (!is_device_ptr(a->q_out) || !is_device_ptr(a->k_out) || !is_device_ptr(a->v_out) || !dtype_ok(a->out_dtype) ||
+      !dtype_ok(a->gate_dtype))
+    return GDNX_EINVAL;
+  return gdnx::launch_proj_prologue(*a, (cudaStream_t)stream);
+}
+
 gdnx_status gdnx_kr_scan_fwd(const gdnx_kr_scan_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
   const gdnx_scan_args& b = a->base;

@@ -10,6 +10,7 @@ gdnx_status launch_decode_128(const gdnx_decode_args& a, cudaStream_t st);
 gdnx_status launch_compact(const gdnx_compact_args& a, cudaStream_t st);
 gdnx_status launch_kr_scan(const gdnx_kr_scan_args& a, cudaStream_t st);
 gdnx_status launch_epilogue(const gdnx_epilogue_args& a, cudaStream_t st);
+gdnx_status launch_proj_prologue(const gdnx_prologue_args& a, cudaStream_t st);
 
 // Chunked tensor-core scan (dense GDN3 / KMD-2 with per-chain scalar decay).
 bool chunked_eligible(const gdnx_scan_args& a);

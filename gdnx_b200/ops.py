@@ -569,3 +569,62 @@ def rms_norm_gated(y: torch.Tensor, gate: torch.Tensor, weight: Optional[torch.T
     with torch.cuda.device(y.device):
         L.check(lib.gdnx_epilogue(C.byref(a), C.c_void_p(_stream(y.device))), "gdnx_epilogue")
     return out
+
+
+def gdn3_prologue(qkv, conv_w, *, H: int, K: int, M: int, coprod=None, mix=None, b_proj=None, proj_a=None,
+                  w_proj=None, proj_b=None, dims=(16, 16, 8, 8), out_dtype: Optional[torch.dtype] = None,
+                  gate_dtype: Optional[torch.dtype] = None):
+    """GDN3 projection prologue (gdn3/gdn3_upgrade.py:752-807, blend :201-250) after the layer's GEMMs.
+
+    ``qkv [B,T,3*H*K]`` (the qkv projection), ``conv_w [3*H*K, 1, k]`` (the depthwise ``Conv1d``
+    weight); ``coprod = (q_a, q_b, k_a, k_b, v_a, v_b)`` as ``[B,T,H,C,dim]`` factor projections and
+    ``mix = (coprod_mix_qk, coprod_mix_v, coprod_strength_qk, coprod_strength_v)`` ([H] each), or None
+    for dense features; ``b_proj [B,T,H,M,K]`` + ``proj_a [B,T,H]`` and ``w_proj [B,T,H,M,V]`` +
+    ``proj_b [B,T,H]`` for the gates.  Returns ``(q, k, v)`` ``[B,T,H,K]`` (lane-shared; the scan
+    applies the lane RoPE) and ``(b_gates, w_gates)`` ``[B,T,H,M,K]`` (or None)."""
+    _require_cuda(qkv, conv_w, b_proj, w_proj)
+    B, T = qkv.shape[:2]
+    V = K
+    out_dtype = out_dtype or qkv.dtype
+    gate_dtype = gate_dtype or out_dtype
+    dev = qkv.device
+    q, k, v = (torch.empty(B, T, H, K, dtype=out_dtype, device=dev) for _ in range(3))
+    a = L.PrologueArgs()
+    a.B, a.T, a.H, a.M, a.K, a.V = B, T, H, M, K, V
+    a.a_k, a.b_k, a.a_v, a.b_v = dims[1], dims[3], dims[0], dims[2]
+    cw = conv_w.detach().reshape(3 * H * K, -1).to(torch.float32).contiguous()
+    a.conv_k = cw.shape[1]
+    a.conv_w = cw.data_ptr()
+    qv = L.View()
+    qv.ptr, qv.dtype, qv.dim = qkv.data_ptr(), _DT[qkv.dtype], qkv.shape[-1]
+    if qkv.stride(-1) != 1:
+        raise ValueError("qkv must have a contiguous last dim")
+    qv.sb, qv.st = qkv.stride(0), qkv.stride(1)
+    a.qkv = qv
+    keep = [cw]
+    if coprod is not None:
+        fs = [_view(f, False, slots=True) for f in coprod]
+        a.q_a, a.q_b, a.k_a, a.k_b, a.v_a, a.v_b = fs
+        a.C = coprod[0].shape[3]
+        ms = [m.detach().to(torch.float32).contiguous() for m in mix]
+        keep += ms
+        a.mix_qk, a.mix_v, a.str_qk, a.str_v = (m.data_ptr() for m in ms)
+    a.q_out, a.k_out, a.v_out = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    a.out_dtype = _DT[out_dtype]
+    a.out_sb, a.out_st, a.out_sh = q.stride()[:3]
+    bg = wg = None
+    if b_proj is not None:
+        bg = torch.empty(B, T, H, M, K, dtype=gate_dtype, device=dev)
+        a.b_proj, a.proj_a = _view(b_proj, True), _view(proj_a.unsqueeze(-1), False)
+        a.b_out = bg.data_ptr()
+        a.gate_sb, a.gate_st, a.gate_sh, a.gate_sm = bg.stride()[:4]
+    if w_proj is not None:
+        wg = torch.empty(B, T, H, M, V, dtype=gate_dtype, device=dev)
+        a.w_proj, a.proj_b = _view(w_proj, True), _view(proj_b.unsqueeze(-1), False)
+        a.w_out = wg.data_ptr()
+        a.wgate_sb, a.wgate_st, a.wgate_sh, a.wgate_sm = wg.stride()[:4]
+    a.gate_dtype = _DT[gate_dtype]
+    lib = L.load()
+    with torch.cuda.device(dev):
+        L.check(lib.gdnx_gdn3_prologue(C.byref(a), C.c_void_p(_stream(dev))), "gdnx_gdn3_prologue")
+    return (q, k, v), (bg, wg)

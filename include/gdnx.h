@@ -263,6 +263,41 @@ typedef struct {
  * Qwen3_5RMSNormGated call after KMD2NativeAttn._scan (gdn3/kmd2_native.py:176). */
 GDNX_API gdnx_status gdnx_epilogue(const gdnx_epilogue_args* args, void* stream);
 
+/* GDN3 projection prologue: the per-element work between the layer's input GEMMs
+ * and the scan.  Views as elsewhere ([B,T,H,(M|C,)D], last dim contiguous);
+ * `qkv` is the [B,T,3*H*K] qkv projection (sb, st used; channel (3h + p) K + c
+ * holds part p = q, k, v of head h).  A NULL coproduct factor skips the blend
+ * (dense features only); NULL b_proj / w_proj skips that gate. */
+typedef struct {
+  int64_t B, T, H, M, K, V;
+  int32_t C;                   /* coproduct rank (4 in the reference)            */
+  int32_t a_k, b_k, a_v, b_v;  /* a_k * b_k = K, a_v * b_v = V                   */
+  int32_t conv_k;              /* causal conv kernel size                        */
+  gdnx_view qkv;
+  const float* conv_w;         /* [3*H*K, conv_k] fp32 (depthwise Conv1d weight) */
+  gdnx_view q_a, q_b, k_a, k_b, v_a, v_b; /* [B,T,H,C,dim]; ss = stride of C      */
+  const float* mix_qk;         /* [H] raw blend logits (sigmoid applied here)    */
+  const float* mix_v;
+  const float* str_qk;         /* [H] strengths                                  */
+  const float* str_v;
+  gdnx_view b_proj, w_proj;    /* [B,T,H,M,K] / [B,T,H,M,V] gate pre-activations */
+  gdnx_view proj_a, proj_b;    /* [B,T,H] (dim 1)                                */
+  void* q_out;                 /* [B,T,H,K] (q, k), [B,T,H,V] (v), strides below */
+  void* k_out;
+  void* v_out;
+  int32_t out_dtype;
+  int64_t out_sb, out_st, out_sh;
+  void* b_out;                 /* [B,T,H,M,K] erase gates */
+  void* w_out;                 /* [B,T,H,M,V] write gates */
+  int32_t gate_dtype;
+  int64_t gate_sb, gate_st, gate_sh, gate_sm;
+  int64_t wgate_sb, wgate_st, wgate_sh, wgate_sm;
+} gdnx_prologue_args;
+
+/* Replaces the causal conv, coproduct blend and gate activations of
+ * GDN3LinearAttn.forward (gdn3/gdn3_upgrade.py:752-807, blend :201-250). */
+GDNX_API gdnx_status gdnx_gdn3_prologue(const gdnx_prologue_args* args, void* stream);
+
 GDNX_API const char* gdnx_status_string(gdnx_status s);
 
 /* Library build identification (for load checks). */

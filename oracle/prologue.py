@@ -3,8 +3,11 @@
 * ``braided_decay``   -- gdn3/gdn3_upgrade.py:809-822
 * ``lane_rope_table`` -- gdn3/gdn3_upgrade.py:342-376 (``_lane_rope_factors``)
 * ``apply_lane_rope`` -- gdn3/gdn3_upgrade.py:378-401 (``_apply_partial_rope``)
+* ``projection_prologue`` -- gdn3/gdn3_upgrade.py:752-807 and :201-250 (conv, coproduct blend, gates)
 """
 from __future__ import annotations
+
+import math
 
 import torch
 
@@ -90,3 +93,40 @@ def apply_lane_rope(x, K_model=None, rotary_factor=0.25, pos0: int = 0):
         lane[..., d:2 * d] = lane[..., :d] * s + x2 * c
         out[:, :, :, m, :] = lane
     return out
+
+
+def projection_prologue(qkv, conv_w, H, K, coprod=None, mix=None, b_proj=None, proj_a=None, w_proj=None,
+                        proj_b=None):
+    """GDN3 projection prologue after the GEMMs, restated op for op from
+    gdn3/gdn3_upgrade.py:752-807 (causal depthwise conv, split, gates) and
+    :201-250 (coproduct factors -> outer-product sum / sqrt(C), blend).
+    Returns ((q, k, v) [B,T,H,K], (b_gates, w_gates))."""
+    import torch.nn.functional as F
+    B, T = qkv.shape[:2]
+    ck = conv_w.shape[-1]
+    qkv_padded = F.pad(qkv.transpose(1, 2), (ck - 1, 0))
+    qkv_conv = F.conv1d(qkv_padded, conv_w, groups=3 * H * K).transpose(1, 2)
+    qkv_conv = qkv_conv.reshape(B, T, H, 3, K)
+    q, k, v = qkv_conv[:, :, :, 0], qkv_conv[:, :, :, 1], qkv_conv[:, :, :, 2]
+    if coprod is not None:
+        q_a, q_b, k_a, k_b, v_a, v_b = coprod
+        mix_qk, mix_v, str_qk, str_v = mix
+        C = q_a.shape[3]
+        sq = math.sqrt(C)
+        cp = lambda a_, b_: (torch.einsum('bthci,bthcj->bthcij', a_, b_).sum(dim=3) / sq).reshape(B, T, H, -1)
+        q_c, k_c, v_c = cp(q_a, q_b), cp(k_a, k_b), cp(v_a, v_b)
+        aqk = torch.sigmoid(mix_qk).view(1, 1, H, 1)
+        av = torch.sigmoid(mix_v).view(1, 1, H, 1)
+        sqk = str_qk.view(1, 1, H, 1)
+        sv = str_v.view(1, 1, H, 1)
+        q = (1 - aqk) * q + aqk * sqk * q_c
+        k = (1 - aqk) * k + aqk * sqk * k_c
+        v = (1 - av) * v + av * sv * v_c
+    bg = wg = None
+    if b_proj is not None:
+        M = b_proj.shape[3]
+        bg = torch.sigmoid(b_proj + proj_a.unsqueeze(3).expand(-1, -1, -1, M).unsqueeze(-1) * 0.1)
+    if w_proj is not None:
+        M = w_proj.shape[3]
+        wg = torch.sigmoid(w_proj + proj_b.unsqueeze(3).expand(-1, -1, -1, M).unsqueeze(-1) * 0.1)
+    return (q, k, v), (bg, wg)

@@ -25,6 +25,9 @@ seeded inputs, what they return:
 * ``epilogue.pt``      -- the GDN3 output epilogue (``forward`` lines 842-856 restated
   by calling the same torch ops on a module's ``norm`` parameter, set to random
   values) and ``Qwen3_5RMSNormGated`` from transformers on random inputs.
+* ``proj_prologue.pt`` -- the projection prologue of ``GDN3LinearAttn.forward``: the
+  reference's conv module and ``_generate_coproduct_channels`` on seeded weights,
+  and the gate activations (lines 797-807), with their post-GEMM inputs.
 * ``prologue.pt``      -- braided decay (``forward`` lines 809-822 restated by
   calling the same torch ops on the module's buffers) and ``_apply_partial_rope``.
 """
@@ -185,6 +188,48 @@ def make_epilogue():
                     y_kmd2=yk, z=z, weight=nm.weight.detach().clone(), out_kmd2=ok), HERE / 'epilogue.pt')
 
 
+def make_projection_prologue():
+    """Inputs after the layer's GEMMs and the outputs of the reference's own conv module,
+    ``_generate_coproduct_channels`` and gate formula (gdn3/gdn3_upgrade.py:747-807)."""
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(21)
+    L = _layer(128, 128, 16)
+    H, K, M, D = L.H, L.K, L.M, L.D
+    with torch.no_grad():
+        L.in_proj_qkv.copy_(torch.randn(L.in_proj_qkv.shape, generator=g) * 0.05)
+        L.conv1d.weight.copy_(torch.randn(L.conv1d.weight.shape, generator=g) * 0.5)
+        L.coprod_mix_qk.copy_(torch.randn(H, generator=g))
+        L.coprod_mix_v.copy_(torch.randn(H, generator=g))
+        L.coprod_strength_qk.copy_(1 + 0.2 * torch.randn(H, generator=g))
+        L.coprod_strength_v.copy_(1 + 0.2 * torch.randn(H, generator=g))
+        for w in (L.W_q_a, L.W_q_b, L.W_k_a, L.W_k_b, L.W_v_a, L.W_v_b):
+            w.copy_(torch.randn(w.shape, generator=g) * 0.3)
+        B, T = 2, 11
+        x = torch.randn(B, T, D, generator=g)
+        qkv = F.linear(x, L.in_proj_qkv)
+        qkv_padded = F.pad(qkv.transpose(1, 2), (L.conv_kernel_size - 1, 0))
+        qkv_conv = L.conv1d(qkv_padded).transpose(1, 2).reshape(B, T, H, 3, K)
+        q, k, v_raw = qkv_conv[:, :, :, 0, :], qkv_conv[:, :, :, 1, :], qkv_conv[:, :, :, 2, :]
+        qo, ko, vo = L._generate_coproduct_channels(q, k, v_raw, x)
+        fac = {}
+        for nm, w in (("q_a", L.W_q_a), ("q_b", L.W_q_b), ("k_a", L.W_k_a), ("k_b", L.W_k_b),
+                      ("v_a", L.W_v_a), ("v_b", L.W_v_b)):
+            fac[nm] = F.linear(x.float(), w.float().reshape(-1, D)).view(B, T, H, w.shape[1], w.shape[2])
+        b_proj = torch.randn(B, T, H, M, K, generator=g)
+        w_proj = torch.randn(B, T, H, M, K, generator=g)
+        proj_a = torch.randn(B, T, H, generator=g)
+        proj_b = torch.randn(B, T, H, generator=g)
+        pa = proj_a.unsqueeze(3).expand(-1, -1, -1, M).unsqueeze(-1).expand(-1, -1, -1, -1, K)
+        pb = proj_b.unsqueeze(3).expand(-1, -1, -1, M).unsqueeze(-1).expand(-1, -1, -1, -1, K)
+        bg = torch.sigmoid(b_proj + pa * 0.1)
+        wg = torch.sigmoid(w_proj + pb * 0.1)
+    torch.save(dict(H=H, K=K, M=M, qkv=qkv, conv_w=L.conv1d.weight.detach().clone(), factors=fac,
+                    mix=[L.coprod_mix_qk.detach().clone(), L.coprod_mix_v.detach().clone(),
+                         L.coprod_strength_qk.detach().clone(), L.coprod_strength_v.detach().clone()],
+                    b_proj=b_proj, w_proj=w_proj, proj_a=proj_a, proj_b=proj_b,
+                    q=qo, k=ko, v=vo, b_gates=bg, w_gates=wg), HERE / 'proj_prologue.pt')
+
+
 def make_prologue():
     g = torch.Generator().manual_seed(9)
     out = {}
@@ -209,7 +254,7 @@ if __name__ == '__main__':
     torch.manual_seed(0)
     makers = dict(gdn3_frozen=make_gdn3_frozen, gdn3_config0=make_gdn3_config0, kmd2=make_kmd2,
                   compaction=make_compaction, prologue=make_prologue, gdn3_kr_p256=make_kr_p256,
-                  epilogue=make_epilogue)
+                  epilogue=make_epilogue, proj_prologue=make_projection_prologue)
     only = sys.argv[2:]  # optional fixture names; default: all
     for name, fn in makers.items():
         if not only or name in only:

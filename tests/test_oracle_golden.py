@@ -123,3 +123,14 @@ def test_epilogues_bit_exact():
     c = _load("epilogue.pt")
     assert torch.equal(E.lane_route(c["y"], c["logits"], c["norm"]), c["out"])
     torch.testing.assert_close(E.rms_norm_gated(c["y_kmd2"], c["z"], c["weight"]), c["out_kmd2"], rtol=0, atol=0)
+
+
+def test_projection_prologue_matches_reference():
+    c = _load("proj_prologue.pt")
+    f = c["factors"]
+    (q, k, v), (bg, wg) = PR.projection_prologue(c["qkv"], c["conv_w"], c["H"], c["K"],
+                                                 coprod=[f[n] for n in ("q_a", "q_b", "k_a", "k_b", "v_a", "v_b")],
+                                                 mix=c["mix"], b_proj=c["b_proj"], proj_a=c["proj_a"],
+                                                 w_proj=c["w_proj"], proj_b=c["proj_b"])
+    for a, b in ((q, c["q"]), (k, c["k"]), (v, c["v"]), (bg, c["b_gates"]), (wg, c["w_gates"])):
+        torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-6)
