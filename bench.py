@@ -236,6 +236,7 @@ def main():
     ap.add_argument("--config4-slabs", type=int, default=8)
     ap.add_argument("--no-config4-ref-1gpu", dest="config4_ref_1gpu", action="store_false",
                     help="skip timing the full config-4 scan on rank 0 alone (N > 1)")
+    ap.add_argument("--dropins-B", type=int, default=None, help="override the drop-in legs' B (profiling runs only)")
     ap.add_argument("--no-dropins", dest="dropins", action="store_false",
                     help="skip the drop-in legs (module input forms)")
     args = ap.parse_args()
@@ -501,7 +502,7 @@ def main():
         from gdnx_b200 import kmd2_fast_scan
         from gdnx_b200.gdn3_upgrade import gdn3_recurrent_state
         import types
-        B, T, H, dk = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["K"]
+        B, T, H, dk = args.dropins_B or CFG1["B"], CFG1["T"], CFG1["H"], CFG1["K"]
         g = torch.Generator(device=dev).manual_seed(11 + rank)
         dropins = {}
         # KMD2NativeAttn.forward -> kmd2_fast_scan: fp32 q [B,T,H,4,dk] (scaled), k, v, per-channel g

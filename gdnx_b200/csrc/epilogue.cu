@@ -77,14 +77,16 @@ GDNX_DEV float half_sum(float x) {
 }
 
 // Lane routing: a half warp per row (8 channels per lane), two passes of two rows per
-// warp with every load of both passes issued before the arithmetic.
-template <int MT>
-__global__ void __launch_bounds__(NT) lane_route_kernel(const gdnx_epilogue_args a) {
+// warp with every load of both passes issued before the arithmetic.  bf16 scan outputs
+// stay packed in registers until they are summed, so four CTAs fit on an SM.
+template <int MT, bool BF16IN>
+__global__ void __launch_bounds__(NT, 4) lane_route_kernel(const gdnx_epilogue_args a) {
   const int lane = threadIdx.x & 31, hw = lane >> 4, c = 8 * (lane & 15);
   const int64_t rows = a.B * a.T * a.H;
   const int64_t base = ((int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5)) * 4;
   const int V = (int)a.V;
-  float y[2][MT][8], lg[2][MT];
+  uint4 raw[2][MT];
+  float lg[2][MT];
   int64_t rb[2], rt[2], rh[2];
   bool live[2];
 #pragma unroll
@@ -100,14 +102,13 @@ __global__ void __launch_bounds__(NT) lane_route_kernel(const gdnx_epilogue_args
     }
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
+      raw[p][m] = make_uint4(0u, 0u, 0u, 0u);
+      lg[p][m] = m < a.M ? 0.f : -INFINITY;  // lanes past M get zero weight
       if (live[p] && m < a.M) {
-        ld8f(a.y.ptr, a.y.dtype, rb[p] * a.y.sb + rt[p] * a.y.st + rh[p] * a.y.sh + m * a.y.sm + c, y[p][m]);
+        const int64_t off = rb[p] * a.y.sb + rt[p] * a.y.st + rh[p] * a.y.sh + m * a.y.sm + c;
+        if (BF16IN) raw[p][m] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.y.ptr) + off);
         lg[p][m] = ld_as_f32(a.router.ptr, a.router.dtype,
                              rb[p] * a.router.sb + rt[p] * a.router.st + rh[p] * a.router.sh + m * a.router.sm);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) y[p][m][e] = 0.f;
-        lg[p][m] = m < a.M ? 0.f : -INFINITY;  // lanes past M get zero weight
       }
     }
   }
@@ -126,8 +127,22 @@ __global__ void __launch_bounds__(NT) lane_route_kernel(const gdnx_epilogue_args
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       const float wm = w[m] / den;
+      float y[8];
+      if (BF16IN) {
+        const uint32_t u[4] = {raw[p][m].x, raw[p][m].y, raw[p][m].z, raw[p][m].w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wm, y[p][m][e], acc[e]);
+        for (int i = 0; i < 4; ++i) {
+          y[2 * i] = __uint_as_float(u[i] << 16);
+          y[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+        }
+      } else if (live[p] && m < a.M) {
+        ld8f(a.y.ptr, a.y.dtype, rb[p] * a.y.sb + rt[p] * a.y.st + rh[p] * a.y.sh + m * a.y.sm + c, y);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wm, y[e], acc[e]);
     }
     float ss = 0.f;
 #pragma unroll
@@ -144,7 +159,7 @@ __global__ void __launch_bounds__(NT) lane_route_kernel(const gdnx_epilogue_args
 }
 
 // Gated RMS norm: a half warp per row, four rows per warp, loads first.
-__global__ void __launch_bounds__(NT) rms_gated_kernel(const gdnx_epilogue_args a) {
+__global__ void __launch_bounds__(NT, 4) rms_gated_kernel(const gdnx_epilogue_args a) {
   const int lane = threadIdx.x & 31, hw = lane >> 4, c = 8 * (lane & 15);
   const int64_t rows = a.B * a.T * a.H;
   const int64_t base = ((int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5)) * 4;
@@ -199,14 +214,21 @@ gdnx_status launch_epilogue(const gdnx_epilogue_args& a, cudaStream_t st) {
   if (rows >= int64_t(0x7fffffff)) return GDNX_EUNSUPPORTED;
   if (a.kind == GDNX_EPILOGUE_RMS_GATED) {
     rms_gated_kernel<<<(unsigned)blocks, NT, 0, st>>>(a);
-  } else if (a.M == 1) {
-    lane_route_kernel<1><<<(unsigned)blocks, NT, 0, st>>>(a);
-  } else if (a.M == 2) {
-    lane_route_kernel<2><<<(unsigned)blocks, NT, 0, st>>>(a);
-  } else if (a.M <= 4) {
-    lane_route_kernel<4><<<(unsigned)blocks, NT, 0, st>>>(a);
   } else {
-    lane_route_kernel<8><<<(unsigned)blocks, NT, 0, st>>>(a);
+    const bool bf = a.y.dtype == GDNX_BF16;
+    if (a.M == 1) {
+      if (bf) lane_route_kernel<1, true><<<(unsigned)blocks, NT, 0, st>>>(a);
+      else lane_route_kernel<1, false><<<(unsigned)blocks, NT, 0, st>>>(a);
+    } else if (a.M == 2) {
+      if (bf) lane_route_kernel<2, true><<<(unsigned)blocks, NT, 0, st>>>(a);
+      else lane_route_kernel<2, false><<<(unsigned)blocks, NT, 0, st>>>(a);
+    } else if (a.M <= 4) {
+      if (bf) lane_route_kernel<4, true><<<(unsigned)blocks, NT, 0, st>>>(a);
+      else lane_route_kernel<4, false><<<(unsigned)blocks, NT, 0, st>>>(a);
+    } else {
+      if (bf) lane_route_kernel<8, true><<<(unsigned)blocks, NT, 0, st>>>(a);
+      else lane_route_kernel<8, false><<<(unsigned)blocks, NT, 0, st>>>(a);
+    }
   }
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
 }
