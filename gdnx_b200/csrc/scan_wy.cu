@@ -618,6 +618,36 @@ __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, cons
   if (tid == P_STORE_TID) bulk_wait_read();  // the Mq^T stores have read shared memory
 }
 
+// Timing probe (off by default): with GDNX_PHASE_PROBE defined, one thread per warp group adds
+// the cycles it spends in each wait of pass 2 to g_wy_probe, read by gdnx_debug_wy_probe:
+// [0] state group waiting for `ready`, [1] state group waiting for G2, [2] for G3,
+// [3] prologue waiting for its stage, [4] for G1, [5] for the previous chunk's G3 (y out),
+// [6] pass-2 CTA lifetime.
+#ifdef GDNX_PHASE_PROBE
+__device__ unsigned long long g_wy_probe[16];
+#define WY_TIMED(slot, cond, expr)                                  \
+  [&]() {                                                           \
+    if (!(cond)) return (expr);                                     \
+    const long long t0_ = clock64();                                \
+    auto r_ = (expr);                                               \
+    probe_acc[slot] += (unsigned long long)(clock64() - t0_);       \
+    return r_;                                                      \
+  }()
+#define WY_MARK(slot)                                                                 \
+  do {                                                                                \
+    if (tid == 0) {                                                                   \
+      const long long n_ = clock64();                                                 \
+      probe_acc[slot] += (unsigned long long)(n_ - pmark);                            \
+      pmark = n_;                                                                     \
+    }                                                                                 \
+  } while (0)
+#else
+#define WY_TIMED(slot, cond, expr) (expr)
+#define WY_MARK(slot) \
+  do {                \
+  } while (0)
+#endif
+
 // ------------------------------- pass 2 ------------------------------------
 constexpr int S_NT = 512;  // warps 0-7: state group, warps 8-15: prologue / output group
 constexpr int G_NT = 256;  // threads per group
@@ -720,6 +750,10 @@ GDNX_DEV bool group_any(int id, bool v) {
 
 __global__ void __launch_bounds__(S_NT, 1)
     wy_scan_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
+#ifdef GDNX_PHASE_PROBE
+  const long long t_life = clock64();
+  unsigned long long probe_acc[16] = {};
+#endif
   extern __shared__ uint8_t smraw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   float* sEL = reinterpret_cast<float*>(sm + S_OFF_PSC);  // [2][64] y factors / Qd factors
@@ -827,10 +861,14 @@ __global__ void __launch_bounds__(S_NT, 1)
   if (warp < 8) {
     // ======================= state group: S0 -> G2 -> W -> G3 =======================
     const int half = warp >> 2;
+#ifdef GDNX_PHASE_PROBE
+    long long pmark = clock64();
+#endif
     for (int64_t ch = 0; ch < nchunks; ++ch) {
       const int s = (int)(ch & 1);
-      bool ok = wait_or_abort(ready + s, (uint32_t)((ch >> 1) & 1), s_abort);
+      bool ok = WY_TIMED(0, tid == 0, wait_or_abort(ready + s, (uint32_t)((ch >> 1) & 1), s_abort));
       if (group_any(2, !ok)) break;
+      WY_MARK(7);  // tail of the previous chunk + the ready wait
       // S_tmem -> bf16 operand (times 2^ls when the chunk normalises the state), and the
       // TMEM write-back of a normalisation (exact path: also the chunk decay 2^{L_C})
       {
@@ -856,6 +894,7 @@ __global__ void __launch_bounds__(S_NT, 1)
       tc::fence_async_smem();
       tc::fence_before();
       if (group_any(2, *s_abort != 0)) break;
+      WY_MARK(8);  // conversion
       // G2: [W^T | y] += S0 [-Wk; Qd]^T  (W^T holds V^T T_w^T from G1, y was zeroed)
       const uint32_t kq = sbase + kq_off(s);
       if (tid == 0) {
@@ -869,9 +908,10 @@ __global__ void __launch_bounds__(S_NT, 1)
         }
         tc::commit(g2);
       }
-      ok = wait_or_abort(g2, (uint32_t)(ch & 1), s_abort);
+      ok = WY_TIMED(1, tid == 0, wait_or_abort(g2, (uint32_t)(ch & 1), s_abort));
       tc::fence_after();
       if (group_any(2, !ok)) break;
+      WY_MARK(9);  // G2 issue + wait
       // W^T -> bf16 A operand
       {
         float w[32];
@@ -894,6 +934,7 @@ __global__ void __launch_bounds__(S_NT, 1)
       tc::fence_async_smem();
       tc::fence_before();
       if (group_any(2, *s_abort != 0)) break;
+      WY_MARK(10);  // W read-out
       // G3: [y | S] or [S | y] += W^T [Mq^T | K] / [K | Mq^T]   (B MN-major; W^T carries the
       // decay factors on folded chunks, K carries them on the exact path)
       if (tid == 0) {
@@ -905,12 +946,13 @@ __global__ void __launch_bounds__(S_NT, 1)
           tc::mma_bf16(d, tc::smem_desc(sWT + k * 32, 16, 1024), tc::smem_desc(bb + k * 2048, KB, 1024), ID_G3, 1);
         tc::commit(g3 + s);
       }
-      ok = wait_or_abort(g3 + s, (uint32_t)((ch >> 1) & 1), s_abort);
+      ok = WY_TIMED(2, tid == 0, wait_or_abort(g3 + s, (uint32_t)((ch >> 1) & 1), s_abort));
       tc::fence_after();
       if (group_any(2, !ok)) break;
+      WY_MARK(11);  // G3 issue + wait
       // stage s is consumed: fetch chunk ch + 2 into it (a thread outside warp 0, which
       // issues the next MMAs; the others go on to the next chunk's wait)
-      if (tid == 32 && ch + 2 < nchunks) issue_stage(ch + 2);
+      if (tid == 32 && ch + 2 < nchunks) WY_TIMED(12, true, (issue_stage(ch + 2), 0));
     }
   } else {
     // ========== prologue / output group: RoPE, G1, -Wk, Qd, y zero, y out ==========
@@ -923,7 +965,7 @@ __global__ void __launch_bounds__(S_NT, 1)
     // consumed them; the next writer waits for the stores' reads).
     auto y_out = [&](int64_t c) -> bool {
       const int sp = (int)(c & 1);
-      const bool ok = wait_or_abort(g3 + sp, (uint32_t)((c >> 1) & 1), s_abort);
+      const bool ok = WY_TIMED(5, ptid == 0, wait_or_abort(g3 + sp, (uint32_t)((c >> 1) & 1), s_abort));
       tc::fence_after();
       if (group_any(1, !ok)) return false;
       const bool folded = sSF[sp].w != 0.f;  // y_i = 2^{L_i + ls} y_tmem on folded chunks
@@ -979,7 +1021,7 @@ __global__ void __launch_bounds__(S_NT, 1)
       const int64_t t0 = ch * C;
       char* kq = reinterpret_cast<char*>(sm + kq_off(s));
       const int qr = q_row(s), wr = wk_row(s);
-      bool ok = wait_or_abort(full + s, (uint32_t)((ch >> 1) & 1), s_abort);
+      bool ok = WY_TIMED(3, ptid == 0, wait_or_abort(full + s, (uint32_t)((ch >> 1) & 1), s_abort));
       if (group_any(1, !ok)) { alive = false; break; }
       const float* Lst = reinterpret_cast<const float*>(sm + S_OFF_L + s * 256);
       const float Lc = Lst[C - 1];
@@ -1055,7 +1097,7 @@ __global__ void __launch_bounds__(S_NT, 1)
                          tc::smem_desc(skq + kb * KB + k * 2048, KB, 1024), ID_WK, k > 0);
         tc::commit(g1);
       }
-      ok = wait_or_abort(g1, (uint32_t)(ch & 1), s_abort);
+      ok = WY_TIMED(4, ptid == 0, wait_or_abort(g1, (uint32_t)(ch & 1), s_abort));
       tc::fence_after();
       if (ptid == 0) bulk_wait_read();  // y stores of chunk ch - 2 have read the -Wk rows
       if (group_any(1, !ok)) { alive = false; break; }
@@ -1126,6 +1168,12 @@ __global__ void __launch_bounds__(S_NT, 1)
     tc::fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
+#ifdef GDNX_PHASE_PROBE
+  if (tid == 0) probe_acc[6] = (unsigned long long)(clock64() - t_life);
+  if (tid == 0 || tid == 32 || tid == G_NT)
+    for (int i = 0; i < 16; ++i)
+      if (probe_acc[i]) atomicAdd(&g_wy_probe[i], probe_acc[i]);
+#endif
 }
 
 // ------------------------------- host side ----------------------------------
@@ -1177,6 +1225,14 @@ bool make_map(const gdnx_view& v, const gdnx_scan_args& a, CUtensorMap* map, int
 }
 
 }  // namespace
+
+#ifdef GDNX_PHASE_PROBE
+extern "C" GDNX_API int gdnx_debug_wy_probe(unsigned long long* out8) {
+  if (cudaMemcpyFromSymbol(out8, g_wy_probe, 16 * sizeof(unsigned long long)) != cudaSuccess) return 1;
+  unsigned long long z[16] = {};
+  return cudaMemcpyToSymbol(g_wy_probe, z, sizeof(z)) == cudaSuccess ? 0 : 1;
+}
+#endif
 
 size_t wy_workspace_bytes(const gdnx_scan_args& a) {
   const int64_t N = a.B * a.H * a.M, nch = (a.T + C - 1) / C;
