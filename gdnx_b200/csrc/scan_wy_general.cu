@@ -78,6 +78,7 @@ struct GenParams {
   int64_t nchunks;
   char* rec;  // [N][nchunks][REC]
   int* err;
+  int64_t t_off, T_total;  // first token of this slab and the full sequence length (scores layout)
 };
 
 // Four consecutive elements (offset a multiple of 4, view 8/16-byte aligned) as fp32.
@@ -827,7 +828,8 @@ __global__ void __launch_bounds__(S_NT, 1) wyg_chain_kernel(const GenParams P) {
         if (ptid < 64) {
           const int i = ptid;
           if (i < nt)
-            a.scores[((b * a.T + c * C + i) * a.H + h) * a.M + m] = sKNc[64 * s + i] * sqrtf(sSum[64 * s + i]);
+            a.scores[((b * P.T_total + P.t_off + c * C + i) * a.H + h) * a.M + m] =
+                sKNc[64 * s + i] * sqrtf(sSum[64 * s + i]);
           sSum[64 * s + i] = 0.f;
         }
       }
@@ -892,10 +894,30 @@ bool wy_general_eligible(const gdnx_scan_args& a) {
   return true;
 }
 
-size_t wy_general_workspace_bytes(const gdnx_scan_args& a) {
+// Records are bounded: a long call runs as slabs of whole chunks, the state carried
+// between slabs in the workspace, so the workspace stays under about 1 GiB per call.
+constexpr size_t kMaxRecordBytes = size_t(1) << 30;
+
+int64_t slab_chunks(const gdnx_scan_args& a) {
   const int64_t N = a.B * a.H * a.M, nch = (a.T + C - 1) / C;
-  return ERR_BYTES + (size_t)N * nch * REC;
+  int64_t per = (int64_t)(kMaxRecordBytes / ((size_t)N * REC));
+  if (per < 1) per = 1;
+  return per < nch ? per : nch;
 }
+
+size_t wy_general_workspace_bytes(const gdnx_scan_args& a) {
+  const int64_t N = a.B * a.H * a.M, nch = (a.T + C - 1) / C, sc = slab_chunks(a);
+  size_t bytes = ERR_BYTES + (size_t)N * sc * REC;
+  if (sc < nch) bytes += (size_t)N * VD * KD * sizeof(float);  // state between slabs
+  return bytes;
+}
+
+namespace {
+int esize(int dtype) { return dtype == GDNX_F32 ? 4 : 2; }
+void shift_view(gdnx_view& v, int64_t t) {
+  if (v.ptr) v.ptr = reinterpret_cast<const char*>(v.ptr) + t * v.st * esize(v.dtype);
+}
+}  // namespace
 
 gdnx_status launch_wy_general(const gdnx_scan_args& a, cudaStream_t st) {
   GenParams P;
@@ -905,19 +927,39 @@ gdnx_status launch_wy_general(const gdnx_scan_args& a, cudaStream_t st) {
   P.vec_w = a.gate_w.dim != 1;
   P.chan_decay = a.decay.dim == KD && a.decay_kind != GDNX_DECAY_BRAIDED;
   P.scores = a.scores != nullptr;
-  P.nchunks = (a.T + C - 1) / C;
+  P.T_total = a.T;
   char* ws = reinterpret_cast<char*>(a.workspace);
   P.err = reinterpret_cast<int*>(ws);
   P.rec = ws + ERR_BYTES;
-  const int64_t N = a.B * a.H * a.M;
+  const int64_t N = a.B * a.H * a.M, nch = (a.T + C - 1) / C, sc = slab_chunks(a);
+  float* carry = sc < nch ? reinterpret_cast<float*>(ws + ERR_BYTES + (size_t)N * sc * REC) : nullptr;
   if (cudaMemsetAsync(ws, 0, ERR_BYTES, st) != cudaSuccess) return GDNX_ELAUNCH;
   if (cudaFuncSetAttribute(wyg_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM) != cudaSuccess ||
       cudaFuncSetAttribute(wyg_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess ||
       cudaFuncSetAttribute(wyg_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_SMEM) != cudaSuccess)
     return GDNX_ELAUNCH;
-  wyg_prep_kernel<<<(unsigned)(N * P.nchunks), P_NT, P_SMEM, st>>>(P);
-  wyg_chain_kernel<<<(unsigned)N, S_NT, S_SMEM, st>>>(P);
-  return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+  for (int64_t c0 = 0; c0 < nch; c0 += sc) {
+    const int64_t t_off = c0 * C, len = (a.T - t_off) < sc * C ? (a.T - t_off) : sc * C;
+    GenParams Q = P;
+    Q.t_off = t_off;
+    Q.nchunks = (len + C - 1) / C;
+    gdnx_scan_args& b = Q.a;
+    b.T = len;
+    shift_view(b.q, t_off);
+    shift_view(b.k, t_off);
+    shift_view(b.v, t_off);
+    shift_view(b.gate_e, t_off);
+    shift_view(b.gate_w, t_off);
+    shift_view(b.decay, t_off);
+    b.y = reinterpret_cast<char*>(a.y) + t_off * a.y_st * esize(a.y_dtype);
+    b.rope.pos0 = a.rope.pos0 + t_off;
+    b.state_in = c0 == 0 ? a.state_in : carry;
+    b.state_out = c0 + sc >= nch ? a.state_out : carry;
+    wyg_prep_kernel<<<(unsigned)(N * Q.nchunks), P_NT, P_SMEM, st>>>(Q);
+    wyg_chain_kernel<<<(unsigned)N, S_NT, S_SMEM, st>>>(Q);
+    if (cudaGetLastError() != cudaSuccess) return GDNX_ELAUNCH;
+  }
+  return GDNX_OK;
 }
 
 }  // namespace gdnx

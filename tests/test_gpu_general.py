@@ -189,3 +189,30 @@ def test_module_input_forms_launch_the_tensor_core_kernels():
     names = _kernel_names(lambda: ops.gdn3_scan(*bf))
     assert any("wyg_chain_kernel" in n for n in names), names
     assert not any("recurrent_scan_kernel" in n for n in names), names
+
+
+def test_long_call_runs_in_slabs_with_bounded_workspace():
+    """64 chains x 16,384 tokens needs 1.2 GB of records at once: the call runs as two
+    slabs carrying the state, its workspace stays near 1 GiB, and it matches the exact
+    recurrence (per-lane bf16 inputs, vector gates, scores-free GDN3)."""
+    B, T, H, M, K = 1, 16384, 16, 4, 128
+    g = torch.Generator(device=DEV).manual_seed(350)
+    bf = torch.bfloat16
+    q = torch.nn.functional.normalize(torch.randn(B, T, H, M, K, device=DEV, generator=g), dim=-1).to(bf)
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, M, K, device=DEV, generator=g), dim=-1).to(bf)
+    v = torch.randn(B, T, H, M, K, device=DEV, generator=g).to(bf)
+    bg = torch.sigmoid(torch.randn(B, T, H, M, K, device=DEV, generator=g)).to(bf)
+    wg = torch.sigmoid(torch.randn(B, T, H, M, K, device=DEV, generator=g)).to(bf)
+    dec = 0.9 + 0.099 * torch.rand(B, T, H, M, device=DEV, generator=g)
+    from gdnx_b200 import _lib as L
+    import ctypes as C
+    a = L.ScanArgs()
+    a.B, a.T, a.H, a.M, a.K, a.V = B, T, H, M, K, K
+    a.mode, a.algo, a.r_out, a.chunk = L.GDNX_MODE_GDN3, L.GDNX_ALGO_AUTO, 1, 64
+    a.q, a.k, a.v = ops._view(q, True), ops._view(k, True), ops._view(v, True)
+    a.gate_e, a.gate_w, a.decay = ops._view(bg, True), ops._view(wg, True), ops._view(dec.unsqueeze(-1), True)
+    need = L.load().gdnx_scan_workspace_bytes(C.byref(a))
+    assert need < (1 << 30) + (64 << 20)
+    y, S = ops.gdn3_scan(q, k, v, bg, wg, dec, return_state=True, out_dtype=torch.float32)
+    y2, S2 = ops.gdn3_scan(q, k, v, bg, wg, dec, return_state=True, out_dtype=torch.float32, algo="recurrent")
+    assert rel(y, y2) < TOL16 and rel(S, S2) < TOL16
