@@ -18,7 +18,7 @@ GDNX_ALGO_AUTO, GDNX_ALGO_RECURRENT, GDNX_ALGO_CHUNKED = 0, 1, 2
 GDNX_EPILOGUE_LANE_ROUTE, GDNX_EPILOGUE_RMS_GATED = 0, 1
 
 EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_fwd_noalloc", "gdnx_scan_noalloc_status", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
-            "gdnx_decode_step", "gdnx_epilogue", "gdnx_gdn3_prologue", "gdnx_status_string", "gdnx_version")
+            "gdnx_decode_step", "gdnx_epilogue", "gdnx_gdn3_prologue", "gdnx_scan_bwd", "gdnx_scan_bwd_workspace_bytes", "gdnx_status_string", "gdnx_version")
 
 
 class View(C.Structure):
@@ -45,6 +45,13 @@ class ScanArgs(C.Structure):
                 ("scores", C.c_void_p),
                 ("state_in", C.c_void_p), ("state_out", C.c_void_p),
                 ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class ScanBwdArgs(C.Structure):
+    _fields_ = [("fwd", ScanArgs), ("dy", View), ("dstate_out", C.c_void_p),
+                ("dq", C.c_void_p), ("dk", C.c_void_p), ("dv", C.c_void_p), ("dgate_e", C.c_void_p),
+                ("dgate_w", C.c_void_p), ("ddecay", C.c_void_p), ("dstate_in", C.c_void_p),
+                ("dout_mix", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
 
 
 class KrScanArgs(C.Structure):
@@ -124,6 +131,10 @@ def load(path: Path = LIB_PATH):
     lib.gdnx_epilogue.restype = C.c_int
     lib.gdnx_gdn3_prologue.argtypes = [C.POINTER(PrologueArgs), C.c_void_p]
     lib.gdnx_gdn3_prologue.restype = C.c_int
+    lib.gdnx_scan_bwd.argtypes = [C.POINTER(ScanBwdArgs), C.c_void_p]
+    lib.gdnx_scan_bwd.restype = C.c_int
+    lib.gdnx_scan_bwd_workspace_bytes.argtypes = [C.POINTER(ScanBwdArgs)]
+    lib.gdnx_scan_bwd_workspace_bytes.restype = C.c_size_t
     lib.gdnx_status_string.argtypes = [C.c_int]
     lib.gdnx_status_string.restype = C.c_char_p
     lib.gdnx_version.argtypes = []

@@ -254,6 +254,33 @@ gdnx_status gdnx_gdn3_prologue(const gdnx_prologue_args* a, void* stream) {
   return gdnx::launch_proj_prologue(*a, (cudaStream_t)stream);
 }
 
+size_t gdnx_scan_bwd_workspace_bytes(const gdnx_scan_bwd_args* a) {
+  if (!a || a->fwd.B <= 0 || a->fwd.T <= 0) return 0;
+  return gdnx::scan_bwd_workspace_bytes(*a);
+}
+
+gdnx_status gdnx_scan_bwd(const gdnx_scan_bwd_args* a, void* stream) {
+  if (!a) return GDNX_EINVAL;
+  const gdnx_scan_args& f = a->fwd;
+  if (f.B < 0 || f.T < 0 || f.H <= 0 || f.M <= 0) return GDNX_EINVAL;
+  if (f.B == 0 || f.T == 0) return GDNX_EUNSUPPORTED;  // nothing to differentiate through
+  gdnx_status s = check_common(f.B, f.H, f.M, f.K, f.V, f.mode, f.r_out, f.q, f.k, f.v, f.gate_e, f.gate_w,
+                               f.decay, f.decay_kind, f.rope, f.out_mix);
+  if (s != GDNX_OK) return s;
+  if (!gdnx::scan_bwd_supported(*a)) return GDNX_EUNSUPPORTED;
+  if (!view_ok(a->dy, (int)f.V)) return GDNX_EINVAL;
+  if (!is_device_ptr(a->dq) || !is_device_ptr(a->dk) || !is_device_ptr(a->dv) || !is_device_ptr(a->dgate_e) ||
+      !is_device_ptr(a->dgate_w) || !is_device_ptr(a->ddecay))
+    return GDNX_EINVAL;
+  if (f.state_in && !is_device_ptr(f.state_in)) return GDNX_EINVAL;
+  if (a->dstate_out && !is_device_ptr(a->dstate_out)) return GDNX_EINVAL;
+  if (a->dstate_in && !is_device_ptr(a->dstate_in)) return GDNX_EINVAL;
+  if (f.r_out > 1 && a->dout_mix && !is_device_ptr(a->dout_mix)) return GDNX_EINVAL;
+  const size_t need = gdnx::scan_bwd_workspace_bytes(*a);
+  if (a->workspace_bytes < need || !is_device_ptr(a->workspace)) return GDNX_EWORKSPACE;
+  return gdnx::launch_scan_bwd(*a, (cudaStream_t)stream);
+}
+
 gdnx_status gdnx_kr_scan_fwd(const gdnx_kr_scan_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
   const gdnx_scan_args& b = a->base;

@@ -11,6 +11,10 @@ gdnx_status launch_compact(const gdnx_compact_args& a, cudaStream_t st);
 gdnx_status launch_kr_scan(const gdnx_kr_scan_args& a, cudaStream_t st);
 gdnx_status launch_epilogue(const gdnx_epilogue_args& a, cudaStream_t st);
 gdnx_status launch_proj_prologue(const gdnx_prologue_args& a, cudaStream_t st);
+// Backward of the dense scan (scan_backward.cu).
+bool scan_bwd_supported(const gdnx_scan_bwd_args& a);
+size_t scan_bwd_workspace_bytes(const gdnx_scan_bwd_args& a);
+gdnx_status launch_scan_bwd(const gdnx_scan_bwd_args& a, cudaStream_t st);
 
 // Chunked tensor-core scan (dense GDN3 / KMD-2 with per-chain scalar decay).
 bool chunked_eligible(const gdnx_scan_args& a);

@@ -15,9 +15,10 @@ reads of the layer's attributes (``R``, ``P``, ``a_k``, ``b_k``, ``a_v``,
   (gdn3/gdn3_upgrade.py:679-682 on a CPU layer), uploaded once per (N, device).
 
 Use either :func:`patch_layer` on an existing reference layer, or
-:class:`GDN3ScanMixin` as the first base of a subclass.  The path is forward
-only: backward raises (the reference's training path is not part of this
-build).  Inputs must be CUDA tensors; there is no CPU fallback.
+:class:`GDN3ScanMixin` as the first base of a subclass.  Under autograd,
+sequences without compaction (T < P) backpropagate through the exact fp32
+backward kernel (``gdnx_scan_bwd``); with compaction backward raises.  Inputs
+must be CUDA tensors; there is no CPU fallback.
 """
 from __future__ import annotations
 
@@ -69,7 +70,13 @@ def gdn3_recurrent_state(layer, q_features, k_features, v_features, b_gates, w_g
     f32 = lambda x: x if x.dtype in (torch.float32, torch.bfloat16, torch.float16) else x.float()
     args = [f32(t) for t in (q_features, k_features, v_features, b_gates, w_gates)]
     dec = f32(decay_factors)
+    train = torch.is_grad_enabled() and any(t.requires_grad for t in (q_features, k_features, v_features, b_gates,
+                                                                     w_gates, decay_factors))
     if T < P:
+        if train:  # exact fp32 backward kernel behind autograd (no compaction reaches the outputs)
+            y, _ = ops.gdn3_scan_train(*args, dec, decay_kind="gamma")
+            layer._last_comp_err = torch.zeros((), device=y.device)
+            return y
         y = ops.gdn3_scan(*args, dec, decay_kind="gamma", out_dtype=torch.float32)
         layer._last_comp_err = torch.zeros((), device=y.device)
     else:

@@ -10,7 +10,8 @@ Shapes (research/kernel_ab/ref_scan.py:8-18): q [B,T,H,r_out,dk], k/g
 [B,T,H,dk] (g per key channel), v [B,T,H,dv], beta_e/beta_w [B,T,H],
 out_mix [H,r_out] when r_out > 1.  Returns y [B,T,H,dv] fp32; scores
 [B,T,H] = |k| |beta_w v - beta_e k^T S| (detached), as
-research/kmd2_ablation/exact_cache.py:1283-1292.  Forward only.
+research/kmd2_ablation/exact_cache.py:1283-1292.  Under autograd the backward runs
+on the exact fp32 backward kernel (``gdnx_scan_bwd``).
 """
 from __future__ import annotations
 
@@ -20,10 +21,14 @@ from . import ops
 
 
 def _scan_core(q, k, v, g, beta_e, beta_w, out_mix=None, *, return_scores):
+    r_out = q.shape[3]
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad
                                        for t in (q, k, v, g, beta_e, beta_w, out_mix)):
-        raise RuntimeError("gdnx_b200: kmd2 scan kernels are forward-only; call under torch.no_grad()")
-    r_out = q.shape[3]
+        # training: the exact fp32 backward kernel (gdnx_scan_bwd) behind autograd
+        mix = out_mix if r_out > 1 else None
+        if return_scores:
+            return ops.kmd2_scan_train(q, k, v, g, beta_e, beta_w, mix, scores=True)
+        return ops.kmd2_scan_train(q, k, v, g, beta_e, beta_w, mix), None
     mix = out_mix if r_out > 1 else None
     if return_scores:
         y, sc = ops.kmd2_scan(q, k, v, g, beta_e, beta_w, mix, scores=True)

@@ -628,3 +628,145 @@ def gdn3_prologue(qkv, conv_w, *, H: int, K: int, M: int, coprod=None, mix=None,
     with torch.cuda.device(dev):
         L.check(lib.gdnx_gdn3_prologue(C.byref(a), C.c_void_p(_stream(dev))), "gdnx_gdn3_prologue")
     return (q, k, v), (bg, wg)
+
+
+# ----------------------------------------------------------------------------
+# backward of the dense scan (autograd)
+# ----------------------------------------------------------------------------
+
+def _scan_bwd(a, dy, dstate_out, B, T, H, M, K, V, r_out, de, dw, ddim, device):
+    """Run gdnx_scan_bwd for forward arguments ``a``; returns per-chain-token gradients
+    dq [B,T,H,M,r,K], dk, dv, dge [B,T,H,M,de], dgw, ddec, dstate_in, dmix (fp32)."""
+    f32 = dict(dtype=torch.float32, device=device)
+    dq = torch.empty(B, T, H, M, r_out, K, **f32)
+    dk = torch.empty(B, T, H, M, K, **f32)
+    dv = torch.empty(B, T, H, M, V, **f32)
+    dge = torch.empty(B, T, H, M, de, **f32)
+    dgw = torch.empty(B, T, H, M, dw, **f32)
+    ddec = torch.empty(B, T, H, M, ddim, **f32)
+    dst = torch.empty(B * H * M, V, K, **f32)
+    dmix = torch.zeros(H, r_out, **f32) if r_out > 1 else None
+    g = L.ScanBwdArgs()
+    g.fwd = a
+    dyc = dy.contiguous()
+    g.dy = _view(dyc, True)
+    dso = None
+    if dstate_out is not None:
+        dso = dstate_out.detach().to(torch.float32).contiguous()
+        g.dstate_out = dso.data_ptr()
+    g.dq, g.dk, g.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    g.dgate_e, g.dgate_w, g.ddecay = dge.data_ptr(), dgw.data_ptr(), ddec.data_ptr()
+    g.dstate_in = dst.data_ptr()
+    if dmix is not None:
+        g.dout_mix = dmix.data_ptr()
+    lib = L.load()
+    need = lib.gdnx_scan_bwd_workspace_bytes(C.byref(g))
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device=device)
+    g.workspace, g.workspace_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(device):
+        L.check(lib.gdnx_scan_bwd(C.byref(g), C.c_void_p(_stream(device))), "gdnx_scan_bwd")
+    return dq, dk, dv, dge, dgw, ddec, dst, dmix
+
+
+def _sum_to(g, t):
+    """Reduce a per-chain-token gradient to the shape of the input it belongs to (lane-shared
+    or broadcast inputs take the sum), in the input's dtype."""
+    if t is None:
+        return None
+    if g.shape != t.shape:
+        if g.dim() == t.dim() + 1:  # lane dim absent in the input
+            g = g.sum(dim=3)
+        g = g.sum_to_size(t.shape)
+    return g.to(t.dtype)
+
+
+class _GDN3ScanFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, b_gate, w_gate, decay, state, decay_kind, algo):
+        y, S = gdn3_scan(q, k, v, b_gate, w_gate, decay, decay_kind=decay_kind, state=state, return_state=True,
+                         out_dtype=torch.float32, algo=algo)
+        ctx.save_for_backward(q, k, v, b_gate, w_gate, decay, state)
+        ctx.decay_kind = decay_kind
+        return y, S
+
+    @staticmethod
+    def backward(ctx, dy, dS):
+        q, k, v, b_gate, w_gate, decay, state = ctx.saved_tensors
+        B, T, H = k.shape[:3]
+        M = b_gate.shape[3]
+        K, V = k.shape[-1], v.shape[-1]
+        qx, kx, vx = _lanes_expand(q, M), _lanes_expand(k, M), _lanes_expand(v, M)
+        bg, wg = _gate(b_gate, K), _gate(w_gate, V)
+        dec = decay.unsqueeze(-1) if decay.dim() == 4 else decay
+        a = L.ScanArgs()
+        a.B, a.T, a.H, a.M, a.K, a.V = B, T, H, M, K, V
+        a.mode, a.algo, a.r_out, a.chunk = L.GDNX_MODE_GDN3, L.GDNX_ALGO_RECURRENT, 1, 64
+        a.q, a.k, a.v = _view(qx, True), _view(kx, True), _view(vx, True)
+        a.gate_e, a.gate_w, a.decay = _view(bg, True), _view(wg, True), _view(dec, True)
+        _fill_decay(a, dec, ctx.decay_kind, BRAID_RATES, DECAY_CLAMP)
+        if state is not None:
+            a.state_in = state.data_ptr()
+        if dy is None:
+            dy = torch.zeros(B, T, H, M, V, device=k.device)
+        dq, dk, dv, dge, dgw, ddec, dst, _ = _scan_bwd(a, dy, dS, B, T, H, M, K, V, 1, bg.shape[-1], wg.shape[-1],
+                                                       dec.shape[-1], k.device)
+        dq = dq[:, :, :, :, 0]
+        dge = dge.reshape(bg.shape) if b_gate.dim() == 5 else dge[..., 0]
+        dgw = dgw.reshape(wg.shape) if w_gate.dim() == 5 else dgw[..., 0]
+        ddec = ddec.reshape(dec.shape) if decay.dim() == 5 else ddec[..., 0]
+        return (_sum_to(dq, q), _sum_to(dk, k), _sum_to(dv, v), _sum_to(dge, b_gate), _sum_to(dgw, w_gate),
+                _sum_to(ddec, decay), dst if state is not None else None, None, None)
+
+
+class _KMD2ScanFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta_e, beta_w, out_mix, scores):
+        outs = kmd2_scan(q, k, v, g, beta_e, beta_w, out_mix, scores=scores)
+        ctx.save_for_backward(q, k, v, g, beta_e, beta_w, out_mix)
+        if scores:
+            y, sc = outs
+            ctx.mark_non_differentiable(sc)
+            return y, sc
+        return outs, None
+
+    @staticmethod
+    def backward(ctx, dy, dsc):
+        q, k, v, g, beta_e, beta_w, out_mix = ctx.saved_tensors
+        B, T, H, r_out, dk_ = q.shape
+        dv_ = v.shape[-1]
+        a = L.ScanArgs()
+        a.B, a.T, a.H, a.M, a.K, a.V = B, T, H, 1, dk_, dv_
+        a.mode, a.algo, a.r_out, a.chunk = L.GDNX_MODE_KMD2, L.GDNX_ALGO_RECURRENT, r_out, 64
+        a.q = _view(q, False, slots=True)
+        a.k, a.v = _view(k, False), _view(v, False)
+        a.gate_e, a.gate_w = _view(beta_e.unsqueeze(-1), False), _view(beta_w.unsqueeze(-1), False)
+        gg = g if g.dim() == 4 else g.unsqueeze(-1)
+        a.decay = _view(gg, False)
+        _fill_decay(a, gg, "gamma", BRAID_RATES, DECAY_CLAMP)
+        mix = None
+        if r_out > 1:
+            mix = out_mix.detach().to(torch.float32).contiguous()
+            a.out_mix = mix.data_ptr()
+        dyl = dy.unsqueeze(3)  # [B,T,H,1,V]
+        dq, dk, dv, dge, dgw, ddec, _, dmix = _scan_bwd(a, dyl, None, B, T, H, 1, dk_, dv_, r_out, 1, 1,
+                                                        gg.shape[-1], k.device)
+        dq = dq[:, :, :, 0]
+        ddec = ddec[:, :, :, 0] if g.dim() == 4 else ddec[:, :, :, 0, 0]
+        dmix_out = dmix.to(out_mix.dtype) if (r_out > 1 and out_mix is not None) else None
+        return (dq.to(q.dtype), dk[:, :, :, 0].to(k.dtype), dv[:, :, :, 0].to(v.dtype), ddec.to(g.dtype),
+                dge[:, :, :, 0, 0].to(beta_e.dtype), dgw[:, :, :, 0, 0].to(beta_w.dtype), dmix_out, None)
+
+
+def kmd2_scan_train(q, k, v, g, beta_e, beta_w, out_mix=None, *, scores: bool = False):
+    """Differentiable KMD-2 scan (forward on the scan kernels, backward by ``gdnx_scan_bwd``).
+    Shapes as :func:`kmd2_scan`.  Returns y [B,T,H,dv] (and detached scores [B,T,H] if asked)."""
+    y, sc = _KMD2ScanFn.apply(q, k, v, g, beta_e, beta_w, out_mix, scores)
+    return (y, sc) if scores else y
+
+
+def gdn3_scan_train(q, k, v, b_gate, w_gate, decay, *, decay_kind="gamma", state=None, algo="auto"):
+    """Differentiable dense GDN3 scan: forward on the scan kernels, backward by the exact fp32
+    reverse-mode kernel (``gdnx_scan_bwd``).  Shapes as :func:`gdn3_scan` (no lane RoPE: rotate
+    q/k before the call, as the reference module does).  Returns ``(y [B,T,H,M,V] fp32,
+    final state [B*H*M, V, K])``."""
+    return _GDN3ScanFn.apply(q, k, v, b_gate, w_gate, decay, state, decay_kind, algo)

@@ -233,6 +233,33 @@ typedef struct {
 
 GDNX_API gdnx_status gdnx_decode_step(const gdnx_decode_args* args, void* stream);
 
+/* Backward of the dense scan (exact fp32 reverse mode, states recomputed from
+ * checkpoints).  `fwd` holds the forward call's arguments (q, k, v, gates, decay,
+ * r_out, out_mix, state_in); its y, scores, state_out and workspace are ignored.
+ * Lane RoPE and braided decays are not supported (GDNX_EUNSUPPORTED); K = V = 128.
+ * Gradients are written per chain-token (the lane dim always present, fp32,
+ * contiguous); inputs shared across lanes or broadcast take the sum over those dims. */
+typedef struct {
+  gdnx_scan_args fwd;
+  gdnx_view dy;               /* [B,T,H,M,V] gradient of y                              */
+  const float* dstate_out;    /* optional [N,V,K] gradient of the final state           */
+  float* dq;                  /* [B,T,H,M,r_out,K]                                       */
+  float* dk;                  /* [B,T,H,M,K]                                             */
+  float* dv;                  /* [B,T,H,M,V]                                             */
+  float* dgate_e;             /* [B,T,H,M,gate_e.dim]                                    */
+  float* dgate_w;             /* [B,T,H,M,gate_w.dim]                                    */
+  float* ddecay;              /* [B,T,H,M,decay.dim]                                     */
+  float* dstate_in;           /* optional [N,V,K] gradient of the initial state         */
+  float* dout_mix;            /* [H, r_out] when r_out > 1, accumulated (zero it first) */
+  void* workspace;            /* see gdnx_scan_bwd_workspace_bytes                       */
+  size_t workspace_bytes;
+} gdnx_scan_bwd_args;
+
+/* Replaces the backward of kmd2_fast_scan.scan (its _TrsmFn, gdn3/kmd2_fast_scan.py:103-160)
+ * and autograd through GDN3LinearAttn._gdn3_recurrent_state without compaction. */
+GDNX_API size_t gdnx_scan_bwd_workspace_bytes(const gdnx_scan_bwd_args* args);
+GDNX_API gdnx_status gdnx_scan_bwd(const gdnx_scan_bwd_args* args, void* stream);
+
 /* Output epilogues of the recurrent layers (one pass over the scan output). */
 typedef enum {
   /* GDN3 lane routing + head norm (gdn3/gdn3_upgrade.py:842-856):
