@@ -519,7 +519,21 @@ def main():
             "call": "kmd2_fast_scan.scan_with_update_norm", "shape": f"B={B},T={T},H={H},r_out=4,dk=dv={dk} fp32, "
             "per-channel decay, scores", "kernels": "wyg_prep_kernel + wyg_chain_kernel", "ms": kms,
             "tok_per_s": B * T / (kms * 1e-3), "tflops": kf / (kms * 1e-3) / 1e12}
-        del q, k, v, gd, be, bw
+        # training step of the same call: forward + exact fp32 backward (gdnx_scan_bwd)
+        for t_ in (q, k, v, gd, be, bw, mix):
+            t_.requires_grad_(True)
+        gyk = torch.randn(B, T, H, dk, device=dev, generator=g)
+
+        def kmd2_train():
+            yk = kmd2_fast_scan.scan(q, k, v, gd, be, bw, mix)
+            yk.backward(gyk)
+
+        tms = timed(kmd2_train, 2, 1, stream, barrier)
+        dropins["kmd2_fast_scan_fwd_bwd"] = {
+            "call": "kmd2_fast_scan.scan + backward (autograd)", "shape": dropins["kmd2_fast_scan"]["shape"],
+            "kernels": "wyg_prep_kernel + wyg_chain_kernel + scan_bwd_kernel", "ms": tms,
+            "tok_per_s": B * T / (tms * 1e-3)}
+        del q, k, v, gd, be, bw, gyk
         # GDN3LinearAttn with bf16 features: per-lane rotated q/k, vector erase/write gates
         M = CFG1["M"]
         bf = torch.bfloat16

@@ -42,8 +42,10 @@ struct BwdParams {
 };
 
 // Per-token vectors staged in shared memory for one 8-token sub-block.
+constexpr int MAXR = 4;  // query slots staged for the out_mix gradient (more are read from global)
 struct Tok {
   float q[KD], k[KD], h[KD], u[VD], G[KD], dy[VD], b[KD], w[VD], v[VD];
+  float qs[MAXR][KD];
   float ce, cw, kh, pad;
 };
 
@@ -84,35 +86,56 @@ GDNX_DEV void stage(const BwdParams& P, Tok* tk, float* graw, int64_t b, int64_t
   const float be = P.vec_e ? 0.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m));
   const float bw = P.vec_w ? 0.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m));
   const float sg = P.chan_decay ? 0.f : ld_as_f32(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
+  // every global load first (four channels per lane), then the shared-memory writes: the
+  // stores go through a generic reference, so loads issued after them would be serialised
+  float qv[4] = {0.f, 0.f, 0.f, 0.f}, qsv[MAXR][4], kv[4], vv[4], bvv[4], wvv[4], rv[4], dyv[4];
+  const int rs = a.r_out <= 1 ? 1 : (a.r_out < MAXR ? a.r_out : MAXR);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int c = lane + 32 * i;
-    float q = 0.f;
-    if (a.r_out <= 1) {
-      q = ld_as_f32(a.q.ptr, a.q.dtype, view_off(a.q, b, t, h, m) + c);
-    } else {
-      for (int r = 0; r < a.r_out; ++r)
-        q += a.out_mix[h * a.r_out + r] * ld_as_f32(a.q.ptr, a.q.dtype, view_off(a.q, b, t, h, m, r) + c);
+#pragma unroll
+    for (int r = 0; r < MAXR; ++r)
+      qsv[r][i] = r < rs ? ld_as_f32(a.q.ptr, a.q.dtype, view_off(a.q, b, t, h, m, r) + c) : 0.f;
+    kv[i] = ld_as_f32(a.k.ptr, a.k.dtype, view_off(a.k, b, t, h, m) + c);
+    vv[i] = ld_as_f32(a.v.ptr, a.v.dtype, view_off(a.v, b, t, h, m) + c);
+    bvv[i] = P.vec_e ? ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m) + c) : be;
+    wvv[i] = P.vec_w ? ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m) + c) : bw;
+    rv[i] = P.chan_decay ? ld_as_f32(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m) + c) : sg;
+    dyv[i] = with_dy ? ld_as_f32(P.a.dy.ptr, P.a.dy.dtype, view_off(P.a.dy, b, t, h, m) + c) : 0.f;
+  }
+  if (a.r_out <= 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qv[i] = qsv[0][i];
+  } else {
+    for (int r = 0; r < a.r_out; ++r) {
+      const float mix = a.out_mix[h * a.r_out + r];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float qr = r < MAXR ? qsv[r < MAXR ? r : 0][i]
+                                  : ld_as_f32(a.q.ptr, a.q.dtype, view_off(a.q, b, t, h, m, r) + lane + 32 * i);
+        qv[i] = fmaf(mix, qr, qv[i]);
+      }
     }
-    const float k = ld_as_f32(a.k.ptr, a.k.dtype, view_off(a.k, b, t, h, m) + c);
-    const float v = ld_as_f32(a.v.ptr, a.v.dtype, view_off(a.v, b, t, h, m) + c);
-    const float bv = P.vec_e ? ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m) + c) : be;
-    const float wv = P.vec_w ? ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m) + c) : bw;
-    const float raw = P.chan_decay ? ld_as_f32(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m) + c) : sg;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = lane + 32 * i;
     float f, df;
-    decay_factor_grad(raw, a.decay_kind, P.kmd2 != 0, &f, &df);
-    const float hv = P.kmd2 ? k : bv * k;
-    T.q[c] = q;
-    T.k[c] = k;
+    decay_factor_grad(rv[i], a.decay_kind, P.kmd2 != 0, &f, &df);
+    const float hv = P.kmd2 ? kv[i] : bvv[i] * kv[i];
+    T.q[c] = qv[i];
+#pragma unroll
+    for (int r = 0; r < MAXR; ++r) T.qs[r][c] = qsv[r][i];
+    T.k[c] = kv[i];
     T.h[c] = hv;
-    T.b[c] = bv;
-    T.w[c] = wv;
-    T.v[c] = v;
-    T.u[c] = P.kmd2 ? v : wv * v;
+    T.b[c] = bvv[i];
+    T.w[c] = wvv[i];
+    T.v[c] = vv[i];
+    T.u[c] = P.kmd2 ? vv[i] : wvv[i] * vv[i];
     T.G[c] = f;
     graw[warp * KD + c] = df;
-    if (with_dy) T.dy[c] = ld_as_f32(P.a.dy.ptr, P.a.dy.dtype, view_off(P.a.dy, b, t, h, m) + c);
-    kh = fmaf(k, hv, kh);
+    T.dy[c] = dyv[i];
+    kh = fmaf(kv[i], hv, kh);
   }
   kh = warp_sum(kh);
   if (lane == 0) {
@@ -245,12 +268,28 @@ GDNX_DEV void write_token_grads(const BwdParams& P, const Tok& T, const float (*
     for (int r = 0; r < a.r_out; ++r) {
       float acc = 0.f;
       for (int c = lane; c < KD; c += 32)
-        acc += ld_as_f32(a.q.ptr, a.q.dtype, view_off(a.q, b, t, h, m, r) + c) * gv[0][c];
+        acc += (r < MAXR ? T.qs[r][c] : ld_as_f32(a.q.ptr, a.q.dtype, view_off(a.q, b, t, h, m, r) + c)) * gv[0][c];
       acc = warp_sum(acc);
       if (lane == 0) atomicAdd(A.dout_mix + h * a.r_out + r, acc);
     }
   }
 }
+
+#ifdef GDNX_PHASE_PROBE
+__device__ unsigned long long g_bwd_probe[8];
+#define BWD_MARK(slot)                                            \
+  do {                                                            \
+    if (threadIdx.x == 0) {                                       \
+      const long long n_ = clock64();                             \
+      pacc[slot] += (unsigned long long)(n_ - pmark);             \
+      pmark = n_;                                                 \
+    }                                                             \
+  } while (0)
+#else
+#define BWD_MARK(slot) \
+  do {                 \
+  } while (0)
+#endif
 
 // shared memory
 struct BwdSmem {
@@ -277,6 +316,10 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
   float* subs = P.sub + (size_t)n * SUB * STATE;
   float* ring = P.ring + (size_t)n * (SUB + 1) * STATE;
   float S[32];
+#ifdef GDNX_PHASE_PROBE
+  long long pmark = clock64();
+  unsigned long long pacc[8] = {};
+#endif
 
   // ---- forward sweep: state at every block start ----
   if (a.state_in) ld_state(a.state_in + (size_t)n * STATE, v, qd, S);
@@ -295,6 +338,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
     }
   }
 
+  BWD_MARK(0);
   // ---- reverse sweep ----
   float dS[32];
   if (A.dstate_out) ld_state(A.dstate_out + (size_t)n * STATE, v, qd, dS);
@@ -316,6 +360,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
       for (int j = 0; j < SUB; ++j) fwd_step(S, sm.tk[j], v, qd);
       __syncthreads();
     }
+    BWD_MARK(1);
     for (int sb = nsub - 1; sb >= 0; --sb) {
       const int64_t t0 = tb + SUB * sb;
       const int nt = (int)((T - t0) < SUB ? (T - t0) : SUB);
@@ -330,6 +375,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
       }
       float Sc[32];
       ld_state(ring + nt * STATE, v, qd, Sc);  // S_t of the first reverse step
+      BWD_MARK(2);
 #pragma unroll 1
       for (int j = nt - 1; j >= 0; --j) {
         const Tok& Tk = sm.tk[j];
@@ -402,7 +448,9 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
           }
           if (qd == 0) sm.dd[j & 1][v] = ddr;
         }
+        BWD_MARK(3);
         __syncthreads();
+        BWD_MARK(4);
         {
           const int vec = tid >> 7, c = tid & 127;
           float acc = 0.f;
@@ -411,6 +459,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
           sm.gvec[vec][c] = acc;
         }
         __syncthreads();
+        BWD_MARK(5);
         // per-token gradients
         float dcw = 0.f, dce = 0.f;
 #pragma unroll
@@ -423,14 +472,27 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
         write_token_grads(P, Tk, sm.gvec, sm.dd[j & 1], &sm.graw[j][0], dcw, dce, ct, b, t, h, m, tid, warp, lane);
 #pragma unroll
         for (int e = 0; e < 32; ++e) Sc[e] = Sp[e];
+        BWD_MARK(6);
       }
       __syncthreads();
     }
   }
   if (A.dstate_in) st_state(A.dstate_in + (size_t)n * STATE, v, qd, dS);
+#ifdef GDNX_PHASE_PROBE
+  if (threadIdx.x == 0)
+    for (int i = 0; i < 8; ++i) atomicAdd(&g_bwd_probe[i], pacc[i]);
+#endif
 }
 
 }  // namespace
+
+#ifdef GDNX_PHASE_PROBE
+extern "C" GDNX_API int gdnx_debug_bwd_probe(unsigned long long* out8) {
+  if (cudaMemcpyFromSymbol(out8, g_bwd_probe, 8 * sizeof(unsigned long long)) != cudaSuccess) return 1;
+  unsigned long long z[8] = {};
+  return cudaMemcpyToSymbol(g_bwd_probe, z, sizeof(z)) == cudaSuccess ? 0 : 1;
+}
+#endif
 
 bool scan_bwd_supported(const gdnx_scan_bwd_args& A) {
   const gdnx_scan_args& a = A.fwd;
