@@ -418,8 +418,16 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) part[e] = dS[e] * d;
         colreduce_store(part, &sm.red[1][warp][0], lane, qd);
-        // dh = -ce P^T dd;  dP = dS - ce dd h^T;  dG = colsum(dP (.) S_{t-1});  dS <- dP G
-        float pg[32];
+        // dh = -ce P^T dd
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 g = *reinterpret_cast<const float4*>(Tk.G + colof(qd, i));
+          const float g4[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) part[4 * i + e] = -Sp[4 * i + e] * g4[e] * ced;
+        }
+        colreduce_store(part, &sm.red[2][warp][0], lane, qd);
+        // dP = dS - ce dd h^T;  dG = colsum(dP (.) S_{t-1});  dS <- dP G
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int c = colof(qd, i);
@@ -429,14 +437,12 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int x = 4 * i + e;
-            part[x] = -Sp[x] * g4[e] * ced;
             const float dP = fmaf(-ced, h4[e], dS[x]);
-            pg[x] = dP * Sp[x];
+            part[x] = dP * Sp[x];
             dS[x] = dP * g4[e];
           }
         }
-        colreduce_store(part, &sm.red[2][warp][0], lane, qd);
-        colreduce_store(pg, &sm.red[3][warp][0], lane, qd);
+        colreduce_store(part, &sm.red[3][warp][0], lane, qd);
         // dcw = dd.u, dce = -dd.m (one thread per row contributes)
         {
           float s0 = qd == 0 ? ddr * Tk.u[v] : 0.f, s1 = qd == 0 ? -ddr * mrow : 0.f;
