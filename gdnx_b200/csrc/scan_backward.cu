@@ -195,17 +195,20 @@ GDNX_DEV void st_state(float* base, int v, int qd, const float* S) {
 // Reduce a 32-value column partial over the eight rows of a warp (lane bits 2-4) by
 // halving exchanges (28 shuffles); the lane ends with four consecutive columns, which
 // it stores to red[col .. col + 3].
-GDNX_DEV void colreduce_store(float* a, float* red, int lane, int qd) {
+template <int O>
+GDNX_DEV void halve(float* a, int lane) {
+  const bool up = (lane & O) != 0;
 #pragma unroll
-  for (int o = 16, n = 16; o >= 4; o >>= 1, n >>= 1) {
-    const bool up = (lane & o) != 0;
-#pragma unroll
-    for (int e = 0; e < n; ++e) {
-      const float send = up ? a[e] : a[e + n];
-      const float keep = up ? a[e + n] : a[e];
-      a[e] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-    }
+  for (int e = 0; e < O; ++e) {
+    const float send = up ? a[e] : a[e + O];
+    const float keep = up ? a[e + O] : a[e];
+    a[e] = keep + __shfl_xor_sync(0xffffffffu, send, O);
   }
+}
+GDNX_DEV void colreduce_store(float* a, float* red, int lane, int qd) {
+  halve<16>(a, lane);
+  halve<8>(a, lane);
+  halve<4>(a, lane);
   const int i = 4 * ((lane >> 4) & 1) + 2 * ((lane >> 3) & 1) + ((lane >> 2) & 1);
   *reinterpret_cast<float4*>(red + colof(qd, i)) = make_float4(a[0], a[1], a[2], a[3]);
 }
@@ -303,8 +306,10 @@ struct BwdSmem {
 };
 
 __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
-  extern __shared__ uint8_t smraw[];
-  BwdSmem& sm = *reinterpret_cast<BwdSmem*>((reinterpret_cast<uintptr_t>(smraw) + 15) & ~uintptr_t(15));
+  // the dynamic shared block is 16-byte aligned; deriving the struct from it without an
+  // integer round trip keeps the accesses in the shared address space
+  extern __shared__ __align__(16) uint8_t smraw[];
+  BwdSmem& sm = *reinterpret_cast<BwdSmem*>(smraw);
   const gdnx_scan_bwd_args& A = P.a;
   const gdnx_scan_args& a = A.fwd;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -330,8 +335,10 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
     st_state(ckpt + blk * STATE, v, qd, S);
     if (blk == P.nblk - 1) break;  // the last block's end state is not needed
     for (int64_t t0 = blk * BLK; t0 < (blk + 1) * BLK; t0 += SUB) {
+      BWD_MARK(0);
       stage(P, sm.tk, &sm.graw[0][0], b, h, m, t0, SUB, warp, lane, false);
       __syncthreads();
+      BWD_MARK(7);
 #pragma unroll 1
       for (int j = 0; j < SUB; ++j) fwd_step(S, sm.tk[j], v, qd);
       __syncthreads();
