@@ -197,7 +197,7 @@ GDNX_DEV void finish_chain(const DecParams& P, int64_t n, int lane, const ChainR
 
 __global__ void __launch_bounds__(256, 1) decode128_kernel(const DecParams P) {
   extern __shared__ uint8_t smraw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 127) & ~uintptr_t(127));
+  uint8_t* sm = tc::align_smem(smraw, 128);
   float* stage_f = reinterpret_cast<float*>(sm);                       // kStages x 128 x 128
   float* vecs = reinterpret_cast<float*>(sm + kStages * kStateBytes);  // kWarps x 2 x 128
   float* ropeC = vecs + kWarps * 2 * K;                                // [4 lanes][64 pairs]

@@ -76,7 +76,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
 
 __global__ void __launch_bounds__(NT, 1) chunked_scan_kernel(const ChunkParams P) {
   extern __shared__ uint8_t smraw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = tc::align_smem(smraw, 1024);
   char* cKQ = reinterpret_cast<char*>(sm + OFF_KQ);
   char* cS0 = reinterpret_cast<char*>(sm + OFF_S0);
   char* cRHS = reinterpret_cast<char*>(sm + OFF_RHS);

@@ -152,7 +152,7 @@ GDNX_DEV void subst_block16(float* A, int B0, int c, float* x) {
 
 __global__ void __launch_bounds__(P_NT, 3) wy_prep_kernel(const WyParams P, const __grid_constant__ WyScanMaps maps) {
   extern __shared__ uint8_t smraw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = tc::align_smem(smraw, 1024);
   char* cKQ = reinterpret_cast<char*>(sm + P_OFF_KQ);
   float* sA = reinterpret_cast<float*>(sm + P_OFF_A);
   float* sL = reinterpret_cast<float*>(sm + P_OFF_SC);  // [2][64] log2 decay prefix
@@ -755,7 +755,7 @@ __global__ void __launch_bounds__(S_NT, 1)
   unsigned long long probe_acc[16] = {};
 #endif
   extern __shared__ uint8_t smraw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = tc::align_smem(smraw, 1024);
   float* sEL = reinterpret_cast<float*>(sm + S_OFF_PSC);  // [2][64] y factors / Qd factors
   float* sFK = sEL + 128;                                  // [2][64] W factors / K' factors
   float4* sSF = reinterpret_cast<float4*>(sm + S_OFF_SF);

@@ -188,7 +188,7 @@ GDNX_DEV void subst16(float* A, int B0, int c) {
 
 __global__ void __launch_bounds__(P_NT, 2) wyg_prep_kernel(const GenParams P) {
   extern __shared__ uint8_t smraw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = tc::align_smem(smraw, 1024);
   char* cHQ = reinterpret_cast<char*>(sm + P_OFF_HQ);
   char* cH0 = reinterpret_cast<char*>(sm + P_OFF_H0);
   char* cU = reinterpret_cast<char*>(sm + P_OFF_U);
@@ -613,7 +613,7 @@ GDNX_DEV uint32_t t_y(int s) { return 192u + 128u * (uint32_t)s; }
 
 __global__ void __launch_bounds__(S_NT, 1) wyg_chain_kernel(const GenParams P) {
   extern __shared__ uint8_t smraw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = tc::align_smem(smraw, 1024);
   float* sKNc = reinterpret_cast<float*>(sm + S_OFF_KN);  // [2][64]
   float* sSum = sKNc + 128;                               // [2][64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S_OFF_BAR);

@@ -26,6 +26,15 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// `raw` (a dynamic shared-memory array) advanced to the next `align`-byte boundary.  The
+// padding is computed from the 32-bit shared address and added to the array pointer, so
+// accesses through the result stay in the shared state space (an integer round trip
+// through a generic address would make them generic loads and stores, which the
+// compiler must also order against global memory).
+__device__ __forceinline__ uint8_t* align_smem(uint8_t* raw, uint32_t align) {
+  return raw + ((align - (smem_u32(raw) & (align - 1))) & (align - 1));
+}
+
 // byte offset of 16-byte chunk `c` (along K) of row `r` in a K-major SW128 tile
 // with `rows` rows per 64-element K block
 __device__ __forceinline__ uint32_t sw128(int r, int c, int rows) {
