@@ -211,84 +211,94 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
   // Bm = Q^T R   (q x n), Bm[c][j]
   col_times(Qm, Bm, 1, n);
   __syncthreads();
-  // One-sided Jacobi on W = Bm^T (n x q): lane holds rows lane and lane+32.
-  if (warp == 0) {
-    float w0[kCompMaxQ], w1[kCompMaxQ];
+  // One-sided Jacobi on W = Bm^T (n x q), columns c of W = rows of Bm in shared memory.
+  // Each round s = 1..7 rotates the four disjoint pairs (i, i ^ s); warps 0-3 take one pair
+  // each (lane: rows lane and lane + 32), the accumulated rotation J (q x q, row-major in
+  // shared memory) alongside, and meet at a 128-thread barrier between rounds.
+  float* Js = Gs;  // the sketch's space is free once Bm is formed: J [8][8], then the sweep flags
+  volatile float* flags = Js + kCompMaxQ * kCompMaxQ;  // [4] per-warp max off, [4] Frobenius parts
+  if (warp < 4) {
     const bool r0 = lane < n, r1 = lane + 32 < n;
+    // Frobenius scale of W: rotations below fp32 resolution of the whole matrix are skipped,
+    // so near-zero (noise) columns cannot keep a sweep alive
+    float fp = 0.f;
+    for (int c = 2 * warp; c < 2 * warp + 2; ++c)
+      if (c < q) {
+        const float a0 = r0 ? Bm[c * n + lane] : 0.f, a1 = r1 ? Bm[c * n + lane + 32] : 0.f;
+        fp += a0 * a0 + a1 * a1;
+      }
+    fp = warp_sum(fp);
+    if (lane == 0) flags[4 + warp] = fp;
+    for (int c = lane; c < kCompMaxQ * kCompMaxQ; c += 32) Js[c] = (c / kCompMaxQ == c % kCompMaxQ) ? 1.f : 0.f;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const float fro = flags[4] + flags[5] + flags[6] + flags[7];
+    for (int sweep = 0; sweep < 30; ++sweep) {
+      float off = 0.f;
+      for (int sr = 1; sr < kCompMaxQ; ++sr) {
+        // this warp's pair: the warp-th i with i < (i ^ sr)
+        int i = 0, found = -1;
+#pragma unroll
+        for (int ii = 0; ii < kCompMaxQ; ++ii)
+          if (ii < (ii ^ sr)) {
+            if (++found == warp) i = ii;
+          }
+        const int j = i ^ sr;
+        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+        if (j < q) {
+          a0 = r0 ? Bm[i * n + lane] : 0.f;
+          a1 = r1 ? Bm[i * n + lane + 32] : 0.f;
+          b0 = r0 ? Bm[j * n + lane] : 0.f;
+          b1 = r1 ? Bm[j * n + lane + 32] : 0.f;
+        }
+        float al = a0 * a0 + a1 * a1, be = b0 * b0 + b1 * b1, ga = a0 * b0 + a1 * b1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          al += __shfl_xor_sync(0xffffffffu, al, o);
+          be += __shfl_xor_sync(0xffffffffu, be, o);
+          ga += __shfl_xor_sync(0xffffffffu, ga, o);
+        }
+        // thresholds on squares (no square roots): ga^2 against 1e-12 al be
+        const float p2 = al * be, g2 = ga * ga;
+        const bool rot = j < q && p2 > 1e-37f && g2 > 1e-12f * p2 && fabsf(ga) > 1e-9f * fro;
+        if (rot) {
+          off = fmaxf(off, __fdividef(g2, p2));
+          // the sweep corrects rotation-parameter rounding; |2 ga| > 1e-6 sqrt(al be) keeps zeta in range
+          const float zeta = __fdividef(be - al, 2.f * ga);
+          const float w1z = fmaf(zeta, zeta, 1.f);
+          const float t = copysignf(__fdividef(1.f, fabsf(zeta) + w1z * rsqrtf(w1z)), zeta);
+          const float cs = rsqrtf(fmaf(t, t, 1.f)), sn = cs * t;
+          if (r0) {
+            Bm[i * n + lane] = cs * a0 - sn * b0;
+            Bm[j * n + lane] = sn * a0 + cs * b0;
+          }
+          if (r1) {
+            Bm[i * n + lane + 32] = cs * a1 - sn * b1;
+            Bm[j * n + lane + 32] = sn * a1 + cs * b1;
+          }
+          if (lane < q) {
+            const float ja = Js[lane * kCompMaxQ + i], jb = Js[lane * kCompMaxQ + j];
+            Js[lane * kCompMaxQ + i] = cs * ja - sn * jb;
+            Js[lane * kCompMaxQ + j] = sn * ja + cs * jb;
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      if (lane == 0) flags[warp] = off;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const float offall = fmaxf(fmaxf(flags[0], flags[1]), fmaxf(flags[2], flags[3]));
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // every warp has read the flags
+      if (offall < 4e-12f) break;  // (ga^2 / al be) < (2e-6)^2: columns orthogonal to fp32 working accuracy
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const bool r0 = lane < n, r1 = lane + 32 < n;
+    float w0[kCompMaxQ], w1[kCompMaxQ], jr[kCompMaxQ];
 #pragma unroll
     for (int c = 0; c < kCompMaxQ; ++c) {
       w0[c] = (c < q && r0) ? Bm[c * n + lane] : 0.f;
       w1[c] = (c < q && r1) ? Bm[c * n + lane + 32] : 0.f;
-    }
-    // J = I (row `lane` of J kept by lanes < q)
-    float jr[kCompMaxQ];
-#pragma unroll
-    for (int c = 0; c < kCompMaxQ; ++c) jr[c] = (lane == c) ? 1.f : 0.f;
-    // Frobenius scale of W: rotations below fp32 resolution of the whole matrix
-    // are skipped, so near-zero (noise) columns cannot keep a sweep alive
-    float fro = 0.f;
-#pragma unroll
-    for (int c = 0; c < kCompMaxQ; ++c) fro += w0[c] * w0[c] + w1[c] * w1[c];
-    fro = warp_sum(fro);
-    for (int sweep = 0; sweep < 30; ++sweep) {
-      float off = 0.f;
-      // rounds s = 1..7 rotate the four disjoint pairs (i, i ^ s): their column dot
-      // products are reduced together
-#pragma unroll
-      for (int sr = 1; sr < kCompMaxQ; ++sr) {
-        float al[kCompMaxQ / 2], be[kCompMaxQ / 2], ga[kCompMaxQ / 2];
-#pragma unroll
-        for (int u = 0, i = 0; i < kCompMaxQ; ++i) {
-          const int j = i ^ sr;
-          if (j < i) continue;
-          al[u] = w0[i] * w0[i] + w1[i] * w1[i];
-          be[u] = w0[j] * w0[j] + w1[j] * w1[j];
-          ga[u] = w0[i] * w0[j] + w1[i] * w1[j];
-          ++u;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-          for (int u = 0; u < kCompMaxQ / 2; ++u) {
-            al[u] += __shfl_xor_sync(0xffffffffu, al[u], o);
-            be[u] += __shfl_xor_sync(0xffffffffu, be[u], o);
-            ga[u] += __shfl_xor_sync(0xffffffffu, ga[u], o);
-          }
-        }
-        // rotation parameters of the four pairs, branch-free (a skipped pair gets cs = 1,
-        // sn = 0) so the pairs' dependent chains interleave
-        float csv[kCompMaxQ / 2], snv[kCompMaxQ / 2];
-#pragma unroll
-        for (int u = 0, i = 0; i < kCompMaxQ; ++i) {
-          const int j = i ^ sr;
-          if (j < i) continue;
-          const int uu = u++;
-          // thresholds on squares (no square roots): ga^2 against 1e-12 al be
-          const float p2 = al[uu] * be[uu], g2 = ga[uu] * ga[uu];
-          const bool rot = j < q && p2 > 1e-37f && g2 > 1e-12f * p2 && fabsf(ga[uu]) > 1e-9f * fro;
-          off = rot ? fmaxf(off, __fdividef(g2, p2)) : off;
-          // the sweep corrects rotation-parameter rounding; |2 ga| > 1e-6 sqrt(al be) keeps zeta in range
-          const float zeta = __fdividef(be[uu] - al[uu], 2.f * ga[uu]);
-          const float w1z = fmaf(zeta, zeta, 1.f);
-          const float t = copysignf(__fdividef(1.f, fabsf(zeta) + w1z * rsqrtf(w1z)), zeta);
-          const float cs = rsqrtf(fmaf(t, t, 1.f));
-          csv[uu] = rot ? cs : 1.f;
-          snv[uu] = rot ? cs * t : 0.f;
-        }
-#pragma unroll
-        for (int u = 0, i = 0; i < kCompMaxQ; ++i) {
-          const int j = i ^ sr;
-          if (j < i) continue;
-          const int uu = u++;
-          const float cs = csv[uu], sn = snv[uu];
-          float a0 = w0[i], b0 = w0[j], a1 = w1[i], b1 = w1[j];
-          w0[i] = cs * a0 - sn * b0; w0[j] = sn * a0 + cs * b0;
-          w1[i] = cs * a1 - sn * b1; w1[j] = sn * a1 + cs * b1;
-          const float ja = jr[i], jb = jr[j];
-          jr[i] = cs * ja - sn * jb; jr[j] = sn * ja + cs * jb;
-        }
-      }
-      if (off < 4e-12f) break;  // (ga^2 / al be) < (2e-6)^2: columns orthogonal to fp32 working accuracy
+      jr[c] = lane < kCompMaxQ ? Js[lane * kCompMaxQ + c] : 0.f;
     }
     // singular values, descending order (selection; q <= 8)
     float sv[kCompMaxQ];
