@@ -16,6 +16,7 @@ GDNX_MODE_GDN3, GDNX_MODE_KMD2 = 0, 1
 GDNX_DECAY_GAMMA, GDNX_DECAY_LOG, GDNX_DECAY_BRAIDED = 0, 1, 2
 GDNX_ALGO_AUTO, GDNX_ALGO_RECURRENT, GDNX_ALGO_CHUNKED = 0, 1, 2
 GDNX_EPILOGUE_LANE_ROUTE, GDNX_EPILOGUE_RMS_GATED = 0, 1
+GDNX_COMPACT_SVD, GDNX_COMPACT_SKETCH = 0, 1
 
 EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_fwd_noalloc", "gdnx_scan_noalloc_status", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
             "gdnx_decode_step", "gdnx_epilogue", "gdnx_gdn3_prologue", "gdnx_scan_bwd", "gdnx_scan_bwd_workspace_bytes", "gdnx_status_string", "gdnx_version")
@@ -59,14 +60,15 @@ class KrScanArgs(C.Structure):
                 ("R", C.c_int32), ("P", C.c_int32), ("a_v", C.c_int32), ("a_k", C.c_int32),
                 ("b_v", C.c_int32), ("b_k", C.c_int32), ("slow_decay", C.c_float),
                 ("sketch", C.c_void_p), ("A", C.c_void_p), ("Bk", C.c_void_p),
-                ("U", C.c_void_p), ("Vb", C.c_void_p), ("slot", C.c_void_p), ("comp_err", C.c_void_p)]
+                ("U", C.c_void_p), ("Vb", C.c_void_p), ("slot", C.c_void_p), ("comp_err", C.c_void_p),
+                ("compact_mode", C.c_int32)]
 
 
 class CompactArgs(C.Structure):
     _fields_ = [("N", C.c_int64), ("R", C.c_int32), ("P", C.c_int32), ("V", C.c_int32), ("K", C.c_int32),
                 ("a_v", C.c_int32), ("a_k", C.c_int32), ("b_v", C.c_int32), ("b_k", C.c_int32),
                 ("slow_decay", C.c_float), ("sketch", C.c_void_p), ("A", C.c_void_p), ("Bk", C.c_void_p),
-                ("U", C.c_void_p), ("Vb", C.c_void_p), ("err", C.c_void_p)]
+                ("U", C.c_void_p), ("Vb", C.c_void_p), ("err", C.c_void_p), ("compact_mode", C.c_int32)]
 
 
 class DecodeArgs(C.Structure):

@@ -38,7 +38,8 @@ __global__ void __launch_bounds__(kThreads) compact_kernel(const CompParams P) {
   add_residual_rmat(Rm, a.U + n * a.V * a.P, a.Vb + n * a.K * a.P, nullptr, a.V, a.K, a.P, tileU, tileV, d);
   add_kron_rmat(Rm, A_s, B_s, d);
   __syncthreads();
-  const float err = compact_core(Rm, A_s, B_s, a.sketch + n * d.n * d.q, work, d);
+  const int sk = a.compact_mode == GDNX_COMPACT_SKETCH;
+  const float err = compact_core(Rm, A_s, B_s, a.sketch + n * d.n * (sk ? d.R : d.q), work, d, sk);
   for (int i = threadIdx.x; i < d.R * d.m; i += kThreads) Ag[i] = A_s[i];
   for (int i = threadIdx.x; i < d.R * d.n; i += kThreads) Bg[i] = B_s[i];
   if (a.err && threadIdx.x == 0) a.err[n] = err;

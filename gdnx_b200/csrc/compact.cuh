@@ -63,9 +63,15 @@ GDNX_DEV float block_sum(float x, float* red) {
 // Returns err (discarded energy, not clamped) to every thread.  Rm (m x ld)
 // is read only.  A_s [R][m], B_s [R][n] hold the current (true) factors and
 // are overwritten with the blended ones.  G is [n][q] in global memory.
+//
+// sketch = 1 selects the reference's compact_mode "sketch" / "sketch_noqr"
+// (gdn3/gdn3_upgrade.py:579-596; the two modes run the same code there):
+//   Y = R G (G is [n][R]) ; Q = Y with unit columns (norms clamped at 1e-12)
+//   Bm = Q^T R (R x n) ; b_r = |Bm_r| (clamped at 1e-12)
+//   A_svd_r = Q_r b_r ,  B_svd_r = Bm_r / b_r ;  same blend ;  err = 0
 template <class CD>
 GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float* G,
-                            float* work, const CD d) {
+                            float* work, const CD d, int sketch = 0) {
   const int tid = threadIdx.x, nt = blockDim.x;
   const int lane = tid % 32, warp = tid / 32;
   const int m = d.m, n = d.n, q = d.q, R = d.R;
@@ -78,15 +84,22 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
   float* J = Gs + kCompMaxN * kCompMaxQ;
   float* red = J + kCompMaxQ * kCompMaxQ;  // 64 floats
 
-  // energy
-  float e = 0.f;
-  for (int idx = tid; idx < m * n; idx += nt) {
-    const float x = Rm[(idx / n) * ld + idx % n];
-    e += x * x;
+  // energy (the sketch mode reports none)
+  float total = 0.f;
+  if (!sketch) {
+    float e = 0.f;
+    for (int idx = tid; idx < m * n; idx += nt) {
+      const float x = Rm[(idx / n) * ld + idx % n];
+      e += x * x;
+    }
+    total = block_sum(e, red);
+    for (int idx = tid; idx < n * q; idx += nt) Gs[idx] = G[idx];
+  } else {  // G is [n][R]: the product below runs on q columns, the ones past R zero
+    for (int idx = tid; idx < n * q; idx += nt) {
+      const int j = idx / q, c = idx % q;
+      Gs[idx] = c < R ? G[j * R + c] : 0.f;
+    }
   }
-  const float total = block_sum(e, red);
-
-  for (int idx = tid; idx < n * q; idx += nt) Gs[idx] = G[idx];
   __syncthreads();
   static_assert(CD::q == kCompMaxQ, "register-blocked products assume q = 8");
   // Y = R X (m x 8) for X = G or Z (n x 8): one thread per row i, X rows broadcast
@@ -146,6 +159,41 @@ GDNX_DEV float compact_core(const float* Rm, float* A_s, float* B_s, const float
   };
   row_times(Gs);
   __syncthreads();
+  if (sketch) {
+    // column norms of Y (warp c < R), then Q = Y / |Y_c| in place (columns past R stay 0)
+    if (warp < R) {
+      float s2 = 0.f;
+      for (int i = lane; i < m; i += 32) s2 = fmaf(Y[i * q + warp], Y[i * q + warp], s2);
+      s2 = warp_sum(s2);
+      if (lane == 0) red[warp] = fmaxf(sqrtf(s2), 1e-12f);
+    }
+    __syncthreads();
+    for (int idx = tid; idx < m * q; idx += nt) {
+      const int c = idx % q;
+      Qm[idx] = c < R ? Y[idx] / red[c] : 0.f;
+    }
+    __syncthreads();
+    col_times(Qm, Bm, 1, n);  // Bm = Q^T R, rows past R zero
+    __syncthreads();
+    if (warp < R) {
+      float s2 = 0.f;
+      for (int j = lane; j < n; j += 32) s2 = fmaf(Bm[warp * n + j], Bm[warp * n + j], s2);
+      s2 = warp_sum(s2);
+      if (lane == 0) red[8 + warp] = fmaxf(sqrtf(s2), 1e-12f);
+    }
+    __syncthreads();
+    const float dd = d.delta, od = 1.f - d.delta;
+    for (int idx = tid; idx < R * m; idx += nt) {
+      const int r = idx / m, i = idx % m;
+      A_s[idx] = dd * A_s[idx] + od * (Qm[i * q + r] * red[8 + r]);
+    }
+    for (int idx = tid; idx < R * n; idx += nt) {
+      const int r = idx / n, j = idx % n;
+      B_s[idx] = dd * B_s[idx] + od * (Bm[r * n + j] / red[8 + r]);
+    }
+    __syncthreads();
+    return 0.f;
+  }
   for (int it = 0; it < 2; ++it) {
     col_times(Y, Z, 8, 1);  // Z = R^T Y
     __syncthreads();

@@ -199,6 +199,7 @@ gdnx_status gdnx_compact(const gdnx_compact_args* a, void* stream) {
       !is_device_ptr(a->U) || !is_device_ptr(a->Vb))
     return GDNX_EINVAL;
   if (a->err && !is_device_ptr(a->err)) return GDNX_EINVAL;
+  if (a->compact_mode != GDNX_COMPACT_SVD && a->compact_mode != GDNX_COMPACT_SKETCH) return GDNX_EINVAL;
   return gdnx::launch_compact(*a, (cudaStream_t)stream);
 }
 
@@ -296,6 +297,7 @@ gdnx_status gdnx_kr_scan_fwd(const gdnx_kr_scan_args* a, void* stream) {
       !is_device_ptr(a->U) || !is_device_ptr(a->Vb) || !is_device_ptr(a->slot))
     return GDNX_EINVAL;
   if (a->comp_err && !is_device_ptr(a->comp_err)) return GDNX_EINVAL;
+  if (a->compact_mode != GDNX_COMPACT_SVD && a->compact_mode != GDNX_COMPACT_SKETCH) return GDNX_EINVAL;
   return gdnx::launch_kr_scan(*a, (cudaStream_t)stream);
 }
 

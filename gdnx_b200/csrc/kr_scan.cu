@@ -111,7 +111,8 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   float* Vg = A.Vb + n * (int64_t)K * Pn;
   float* Ag = A.A + n * (int64_t)R * d.m;
   float* Bg = A.Bk + n * (int64_t)R * d.n;
-  const float* Gg = A.sketch + n * (int64_t)d.n * d.q;
+  const int sketch_mode = A.compact_mode == GDNX_COMPACT_SKETCH;
+  const float* Gg = A.sketch + n * (int64_t)d.n * (sketch_mode ? d.R : d.q);
 
   for (int i = tid; i < R * d.m; i += kNT) A_s[i] = Ag[i];
   for (int i = tid; i < R * d.n; i += kNT) B_s[i] = Bg[i];
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       rebuild();                      // Rm = rearrange(U Vb^T), Rs exact again
       add_kron_rmat(Rm, A_s, B_s, d);
       __syncthreads();
-      err_acc += compact_core(Rm, A_s, B_s, Gg, work, d);
+      err_acc += compact_core(Rm, A_s, B_s, Gg, work, d, sketch_mode);
       p = 0;
       __syncthreads();
       build_kron();

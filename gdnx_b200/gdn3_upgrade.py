@@ -10,9 +10,11 @@ reads of the layer's attributes (``R``, ``P``, ``a_k``, ``b_k``, ``a_v``,
   the residual buffer is exactly the dense state and the dense scan kernel
   runs (``gdnx_scan_fwd``);
 * otherwise the Kronecker-residual kernel with in-kernel compaction runs
-  (``gdnx_kr_scan_fwd``).  Its Gaussian sketch is the one the reference draws:
-  ``torch.randn(N, b_v*b_k, q)`` from a CPU generator seeded 1234
-  (gdn3/gdn3_upgrade.py:679-682 on a CPU layer), uploaded once per (N, device).
+  (``gdnx_kr_scan_fwd``), by the layer's ``compact_mode`` ("svd", or "sketch" /
+  "sketch_noqr": gdn3/gdn3_upgrade.py:81,579-596).  Its Gaussian sketch is the one
+  the reference draws: ``torch.randn(N, b_v*b_k, q)`` from a CPU generator seeded
+  1234 (gdn3/gdn3_upgrade.py:679-682 on a CPU layer; q = R in the sketch modes,
+  :556-563), uploaded once per (N, q, device).
 
 Use either :func:`patch_layer` on an existing reference layer, or
 :class:`GDN3ScanMixin` as the first base of a subclass.  Under autograd,
@@ -60,9 +62,9 @@ def gdn3_recurrent_state(layer, q_features, k_features, v_features, b_gates, w_g
     Also sets ``layer._last_comp_err`` (on device) like the reference
     (gdn3/gdn3_upgrade.py:523-528).
     """
-    mode = getattr(layer, "compact_mode", "svd")
-    if mode != "svd":
-        raise NotImplementedError(f"gdnx_b200: compact_mode={mode!r} is not implemented (only 'svd')")
+    mode = str(getattr(layer, "compact_mode", "svd")).lower()
+    if mode not in ("svd", "sketch", "sketch_noqr"):
+        raise ValueError(f"gdnx_b200: unknown compact_mode {mode!r} (svd, sketch, sketch_noqr)")
     B, T, H, M, K = q_features.shape
     V = v_features.shape[-1]
     R, P = int(layer.R), int(layer.P)
@@ -81,11 +83,10 @@ def gdn3_recurrent_state(layer, q_features, k_features, v_features, b_gates, w_g
         layer._last_comp_err = torch.zeros((), device=y.device)
     else:
         N = B * H * M
-        q = min(R + 4, dims[0] * dims[1], dims[2] * dims[3])
-        G = reference_sketch(N, dims[2] * dims[3], q, q_features.device)
+        G = reference_sketch(N, dims[2] * dims[3], ops.sketch_width(R, dims, mode), q_features.device)
         st = ops.KRState.zeros(N, R, P, dims, V, K, q_features.device)
         y = ops.gdn3_kr_scan(*args, dec, st, G, P=P, R=R, dims=dims, slow_decay=float(layer.slow_decay),
-                             decay_kind="gamma", out_dtype=torch.float32)
+                             decay_kind="gamma", out_dtype=torch.float32, compact_mode=mode)
         layer._last_comp_err = st.err.sum().clamp(min=0.0)
     grads = [t for t in (q_features, k_features, v_features, b_gates, w_gates, decay_factors) if t.requires_grad]
     if torch.is_grad_enabled() and grads:

@@ -342,18 +342,38 @@ class KRState:
                        torch.zeros(N, dtype=torch.int32, device=device), torch.zeros(N, **f))
 
 
+_COMPACT_MODES = {"svd": L.GDNX_COMPACT_SVD, "sketch": L.GDNX_COMPACT_SKETCH, "sketch_noqr": L.GDNX_COMPACT_SKETCH}
+
+
+def sketch_width(R: int, dims, compact_mode: str = "svd") -> int:
+    """Columns of the compaction sketch G: min(R + 4, a_v a_k, b_v b_k) for the SVD
+    (gdn3/gdn3_upgrade.py:599), R for "sketch" / "sketch_noqr" (:580)."""
+    if compact_mode not in _COMPACT_MODES:
+        raise ValueError(f"unknown compact_mode {compact_mode!r} (svd, sketch, sketch_noqr)")
+    a_v, a_k, b_v, b_k = dims
+    return R if compact_mode != "svd" else min(R + 4, a_v * a_k, b_v * b_k)
+
+
+def _check_sketch(sketch, N, R, dims, compact_mode):
+    want = (N, dims[2] * dims[3], sketch_width(R, dims, compact_mode))
+    if tuple(sketch.shape) != want:
+        raise ValueError(f"sketch must be {list(want)} for compact_mode={compact_mode!r}, got {list(sketch.shape)}")
+
+
 def gdn3_kr_scan(q, k, v, b_gate, w_gate, decay, state: KRState, sketch: torch.Tensor, *,
                  P: int, R: int = 4, dims=(16, 16, 8, 8), slow_decay: float = 0.97,
                  decay_kind: str = "gamma", rope: Optional[LaneRope] = None,
                  out_dtype: Optional[torch.dtype] = None, braid_rates=BRAID_RATES,
-                 braid_clamp=DECAY_CLAMP):
+                 braid_clamp=DECAY_CLAMP, compact_mode: str = "svd"):
     """GDN3-KR scan continuing ``state`` in place.  Shapes as ``gdn3_scan``;
-    ``sketch`` is the compaction sketch G [N, b_v*b_k, q] (fp32)."""
+    ``sketch`` is the compaction sketch G [N, b_v*b_k, sketch_width(R, dims, compact_mode)]
+    (fp32).  ``compact_mode`` is the reference layer's ``GDN3_COMPACT_MODE``."""
     B, T, H = k.shape[:3]
     M = b_gate.shape[3]
     K, V = k.shape[-1], v.shape[-1]
     N = B * H * M
     _require_cuda(q, k, v, b_gate, w_gate, decay, sketch)
+    _check_sketch(sketch, N, R, dims, compact_mode)
     for t in (state.A, state.Bk, state.U, state.Vb, state.err, sketch):
         if t.dtype != torch.float32 or not t.is_contiguous():
             raise ValueError("KR state and sketch must be contiguous fp32")
@@ -381,16 +401,19 @@ def gdn3_kr_scan(q, k, v, b_gate, w_gate, decay, state: KRState, sketch: torch.T
     ka.A, ka.Bk, ka.U, ka.Vb = (state.A.data_ptr(), state.Bk.data_ptr(), state.U.data_ptr(),
                                 state.Vb.data_ptr())
     ka.slot, ka.comp_err = state.slot.data_ptr(), state.err.data_ptr()
+    ka.compact_mode = _COMPACT_MODES[compact_mode]
     lib = L.load()
     with torch.cuda.device(q.device):
         L.check(lib.gdnx_kr_scan_fwd(C.byref(ka), C.c_void_p(_stream(q.device))), "gdnx_kr_scan_fwd")
     return y
 
 
-def compact(A, Bk, U, Vb, sketch, *, dims=(16, 16, 8, 8), slow_decay: float = 0.97):
-    """One compaction per chain, in place on A and Bk; returns per-chain discarded energy [N]."""
+def compact(A, Bk, U, Vb, sketch, *, dims=(16, 16, 8, 8), slow_decay: float = 0.97, compact_mode: str = "svd"):
+    """One compaction per chain, in place on A and Bk; returns per-chain discarded energy [N]
+    (zeros in the sketch modes, like the reference)."""
     _require_cuda(A, Bk, U, Vb, sketch)
     N, R = A.shape[:2]
+    _check_sketch(sketch, N, R, dims, compact_mode)
     V, P = U.shape[1:]
     K = Vb.shape[1]
     for t in (A, Bk, U, Vb, sketch):
@@ -403,6 +426,7 @@ def compact(A, Bk, U, Vb, sketch, *, dims=(16, 16, 8, 8), slow_decay: float = 0.
     ca.slow_decay = slow_decay
     ca.sketch, ca.A, ca.Bk, ca.U, ca.Vb, ca.err = (sketch.data_ptr(), A.data_ptr(), Bk.data_ptr(),
                                                   U.data_ptr(), Vb.data_ptr(), err.data_ptr())
+    ca.compact_mode = _COMPACT_MODES[compact_mode]
     lib = L.load()
     with torch.cuda.device(A.device):
         L.check(lib.gdnx_compact(C.byref(ca), C.c_void_p(_stream(A.device))), "gdnx_compact")

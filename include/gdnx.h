@@ -171,6 +171,14 @@ GDNX_API gdnx_status gdnx_scan_fwd_noalloc(const gdnx_scan_args* args, void* str
  * gdnx_scan_fwd_noalloc call clears it.  No counterpart in the reference. */
 GDNX_API gdnx_status gdnx_scan_noalloc_status(int32_t* device_error, void* stream);
 
+/* Compaction methods: the rearrangement SVD (randomised range finder, power
+ * iterations, QR, SVD of the projection; gdn3/gdn3_upgrade.py:598-629 and
+ * :650-719) and the reference's GDN3_COMPACT_MODE "sketch" / "sketch_noqr"
+ * (one sketch product, column / row normalisation, no SVD;
+ * gdn3/gdn3_upgrade.py:579-596). */
+#define GDNX_COMPACT_SVD 0
+#define GDNX_COMPACT_SKETCH 1
+
 /* Kronecker-residual (GDN3-KR) scan with periodic compaction. */
 typedef struct {
   gdnx_scan_args base;        /* mode must be GDN3; state_in/state_out unused      */
@@ -186,6 +194,8 @@ typedef struct {
   float* Vb;                  /* [N,K,P]       */
   int32_t* slot;              /* [N] slot pointer p (int32)                          */
   float* comp_err;            /* optional [N] accumulated discarded energy           */
+  int32_t compact_mode;       /* GDNX_COMPACT_SVD (0) or GDNX_COMPACT_SKETCH; with the
+                                 sketch mode `sketch` is G [N, b_v*b_k, R]           */
 } gdnx_kr_scan_args;
 
 /* Replaces GDN3LinearAttn._gdn3_recurrent_state with compaction
@@ -206,7 +216,10 @@ typedef struct {
   float* Bk;                  /* [N,R,b_v,b_k] in/out */
   const float* U;             /* [N,V,P] */
   const float* Vb;            /* [N,K,P] */
-  float* err;                 /* optional [N]: discarded energy of this call (written) */
+  float* err;                 /* optional [N]: discarded energy of this call (written;
+                                 0 in the sketch mode, like the reference)           */
+  int32_t compact_mode;       /* GDNX_COMPACT_SVD (0) or GDNX_COMPACT_SKETCH; with the
+                                 sketch mode `sketch` is G [N, b_v*b_k, R]           */
 } gdnx_compact_args;
 
 GDNX_API gdnx_status gdnx_compact(const gdnx_compact_args* args, void* stream);

@@ -16,6 +16,8 @@ recurrences (each function cites the reference ``file:line`` it follows):
   (``research/kmd2_ablation/exact_cache.py:1231-1295``) + final state.
 * ``recurrence.compact_call``   -- one rearrangement-SVD compaction
   (``gdn3/gdn3_upgrade.py:650-719``) with the Gaussian sketch supplied.
+* ``recurrence.compact_sketch_call`` -- the ``compact_mode`` "sketch" /
+  "sketch_noqr" compaction (``gdn3/gdn3_upgrade.py:579-596``).
 * ``prologue``                  -- braided decay and lane RoPE
   (``gdn3/gdn3_upgrade.py:342-401, 809-822``).
 * ``inputs``                    -- seeded synthetic inputs for the five

@@ -141,6 +141,31 @@ def compact_call(A, Bk, U, Vb, dims: KronDims, slow_decay: float = 0.97,
     return A_new, B_new, U, Vb, err
 
 
+def compact_sketch_call(A, Bk, U, Vb, dims: KronDims, slow_decay: float = 0.97,
+                        G: Optional[torch.Tensor] = None):
+    """One compaction in the reference's ``compact_mode`` "sketch" / "sketch_noqr"
+    (the two are the same code): restates ``_compact_fast``'s sketch branch
+    (gdn3/gdn3_upgrade.py:565-596).  ``G`` is ``[N, n, R]`` (the reference draws it
+    with ``R`` columns, seed 1234).  Returns ``(A_new, B_new, U, Vb, err)`` with
+    ``err`` = 0 like the reference.
+    """
+    N, R = A.shape[0], A.shape[1]
+    R_mat = rearranged_matrix(A, Bk, U, Vb, dims)
+    n = R_mat.shape[-1]
+    if G is None:
+        G = sketch_matrix(N, n, R, R_mat.dtype)
+    Y = R_mat @ G
+    q_scale = Y.square().sum(1).sqrt().clamp_min(1e-12)
+    Q = Y / q_scale[:, None, :]
+    Bm = Q.transpose(-2, -1) @ R_mat
+    b_scale = Bm.square().sum(-1).sqrt().clamp_min(1e-12)
+    A_svd = (Q * b_scale[:, None, :]).permute(0, 2, 1).reshape(N, R, dims.a_v, dims.a_k)
+    B_svd = (Bm / b_scale[:, :, None]).reshape(N, R, dims.b_v, dims.b_k)
+    A_new = slow_decay * A + (1 - slow_decay) * A_svd
+    B_new = slow_decay * Bk + (1 - slow_decay) * B_svd
+    return A_new, B_new, U, Vb, torch.zeros((), dtype=R_mat.dtype)
+
+
 # --------------------------------------------------------------------------
 # GDN3 Kronecker-residual scan (gdn3/_reference_recurrence.py:33-94)
 # --------------------------------------------------------------------------
@@ -158,13 +183,17 @@ class KRState:
 def gdn3_kr_scan(q, k, v, bg, wg, dec, *, R: int = 4, P: int = 16,
                  dims: KronDims = KronDims(), slow_decay: float = 0.97,
                  G: Optional[torch.Tensor] = None, canon_signs: bool = False,
-                 state: Optional[KRState] = None, dtype=torch.float32):
+                 state: Optional[KRState] = None, dtype=torch.float32, compact_mode: str = 'svd'):
     """Frozen GDN3-KR token loop returning ``(Y [B,T,H,M,V], KRState)``.
 
     Mirrors ``reference_recurrent_state`` (gdn3/_reference_recurrence.py:33-94)
     op for op.  ``state`` (optional) continues from a previous call instead of
-    the zero state, which is what a decode step needs.
+    the zero state, which is what a decode step needs.  ``compact_mode`` "sketch"
+    (or "sketch_noqr") compacts with :func:`compact_sketch_call` instead, the
+    reference layer's ``GDN3_COMPACT_MODE`` choice (gdn3/gdn3_upgrade.py:81,579).
     """
+    if compact_mode not in ('svd', 'sketch', 'sketch_noqr'):
+        raise ValueError(f'unknown compact_mode {compact_mode!r}')
     B, T, H, M, K = q.shape
     V = v.shape[-1]
     N = B * H * M
@@ -208,8 +237,11 @@ def gdn3_kr_scan(q, k, v, bg, wg, dec, *, R: int = 4, P: int = 16,
         p += 1
         if p >= P:
             with torch.no_grad():
-                A, Bk, U, Vb, err = compact_call(A, Bk, U, Vb, dims, slow_decay,
-                                                 G=G, canon_signs=canon_signs)
+                if compact_mode == 'svd':
+                    A, Bk, U, Vb, err = compact_call(A, Bk, U, Vb, dims, slow_decay,
+                                                     G=G, canon_signs=canon_signs)
+                else:
+                    A, Bk, U, Vb, err = compact_sketch_call(A, Bk, U, Vb, dims, slow_decay, G=G)
             comp_err = comp_err + err
             p = 0
     Y = torch.stack(outs, 0).reshape(T, B, H, M, V).permute(1, 0, 2, 3, 4).contiguous()

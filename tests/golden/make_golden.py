@@ -17,6 +17,9 @@ seeded inputs, what they return:
 * ``kmd2.pt``          -- ``research/kernel_ab/ref_scan.scan`` and
   ``research/kmd2_ablation/exact_cache.reference_scan_with_scores``.
 * ``compaction.pt``    -- one ``GDN3LinearAttn._compact_vec`` call.
+* ``compaction_sketch.pt`` -- one ``GDN3LinearAttn._compact_fast`` call with
+  ``compact_mode`` "sketch" and one with "sketch_noqr" (CPU layer, so its sketch
+  comes from the CPU generator, seed 1234).
 * ``gdn3_kr_p256.pt``  -- the frozen loop at config 2's compaction period
   (P = 256, R = 4, A 16x16 (x) B 8x8, d = 128, one head of four lanes, bf16-rounded
   config-2 inputs, T = 1024: four compactions) -- every 8th token and the last
@@ -163,6 +166,23 @@ def make_compaction():
                     slow_decay=L.slow_decay), HERE / 'compaction.pt')
 
 
+def make_compaction_sketch():
+    g = torch.Generator().manual_seed(6)
+    N, R, V, K, P = 6, 4, 128, 128, 32
+    L = _layer(K, V, P)
+    A = torch.randn(N, R, 16, 16, generator=g) * 0.1
+    Bk = torch.randn(N, R, 8, 8, generator=g) * 0.1
+    U = torch.randn(N, V, P, generator=g) * 0.2
+    Vb = torch.randn(N, K, P, generator=g) * 0.2
+    out = {}
+    for mode in ('sketch', 'sketch_noqr'):
+        L.compact_mode = mode
+        with torch.no_grad():
+            An, Bn, Uo, Vo, err = L._compact_fast(A, Bk, U, Vb)
+        out[mode] = dict(A_new=An, B_new=Bn, err=err)
+    torch.save(dict(inputs=[A, Bk, U, Vb], slow_decay=L.slow_decay, **out), HERE / 'compaction_sketch.pt')
+
+
 def make_epilogue():
     import torch.nn.functional as F
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5RMSNormGated
@@ -253,7 +273,7 @@ if __name__ == '__main__':
     sys.path.insert(0, REF)
     torch.manual_seed(0)
     makers = dict(gdn3_frozen=make_gdn3_frozen, gdn3_config0=make_gdn3_config0, kmd2=make_kmd2,
-                  compaction=make_compaction, prologue=make_prologue, gdn3_kr_p256=make_kr_p256,
+                  compaction=make_compaction, compaction_sketch=make_compaction_sketch, prologue=make_prologue, gdn3_kr_p256=make_kr_p256,
                   epilogue=make_epilogue, proj_prologue=make_projection_prologue)
     only = sys.argv[2:]  # optional fixture names; default: all
     for name, fn in makers.items():

@@ -24,3 +24,16 @@ def test_kmd2_fast_scan_signatures():
 def test_gdn3_recurrent_state_signature():
     params = list(inspect.signature(gdn3_upgrade.gdn3_recurrent_state).parameters)
     assert params == ["layer", "q_features", "k_features", "v_features", "b_gates", "w_gates", "decay_factors"]
+
+
+def test_compaction_sketch_widths():
+    """Sketch columns per compact_mode: min(R+4, m, n) for the SVD (gdn3/gdn3_upgrade.py:599),
+    R for "sketch" / "sketch_noqr" (:580); unknown modes are rejected."""
+    import pytest
+    from gdnx_b200 import ops
+    assert ops.sketch_width(4, (16, 16, 8, 8), "svd") == 8
+    assert ops.sketch_width(4, (2, 2, 2, 2), "svd") == 4
+    assert ops.sketch_width(4, (16, 16, 8, 8), "sketch") == 4
+    assert ops.sketch_width(4, (16, 16, 8, 8), "sketch_noqr") == 4
+    with pytest.raises(ValueError):
+        ops.sketch_width(4, (16, 16, 8, 8), "eigh")

@@ -107,6 +107,15 @@ def test_compaction_bit_exact():
     assert torch.equal(err, c["err"])
 
 
+@pytest.mark.parametrize("mode", ["sketch", "sketch_noqr"])
+def test_compaction_sketch_mode_bit_exact(mode):
+    c = _load("compaction_sketch.pt")
+    A, Bk, U, Vb = c["inputs"]
+    An, Bn, _, _, err = R.compact_sketch_call(A, Bk, U, Vb, R.KronDims(), c["slow_decay"])
+    assert torch.equal(An, c[mode]["A_new"]) and torch.equal(Bn, c[mode]["B_new"])
+    assert float(err) == 0.0 and float(c[mode]["err"]) == 0.0
+
+
 @pytest.mark.parametrize("rf", [0.25, 0.5])
 def test_lane_rope_bit_exact(rf):
     c = _load("prologue.pt")[f"rope_rf{rf}"]
