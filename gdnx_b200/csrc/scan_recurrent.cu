@@ -46,8 +46,9 @@ struct RecSmem {
   static constexpr int kFloats = kTok + kOut;
 };
 
+// Two CTAs per SM at K = 128 (the row state alone is 64 registers a thread).
 template <int K, int V, int TPR>
-__global__ void __launch_bounds__(V * TPR)
+__global__ void __launch_bounds__(V * TPR, K >= 128 ? 2 : 1)
 recurrent_scan_kernel(const RecParams P) {
   using SM = RecSmem<K, V>;
   constexpr int NT = V * TPR;
@@ -80,17 +81,57 @@ recurrent_scan_kernel(const RecParams P) {
   for (int64_t t0 = 0; t0 < a.T; t0 += kTB) {
     const int nt = (int)((a.T - t0) < kTB ? (a.T - t0) : kTB);
     // ---------------- stage nt tokens (one warp per token) ----------------
+    // Every global load of a token is issued before any of them is used, so a staged token
+    // costs about one memory round trip instead of one per loop iteration.
     for (int tt = warp; tt < nt; tt += NW) {
       const int64_t t = t0 + tt;
       float* tok = sm + tt * SM::kPer;
       float* sk = tok + SM::kK;
       float* sq = tok + SM::kQ;
+      constexpr int KL = (K + 31) / 32, VL = (V + 31) / 32;
       const int64_t ko = view_off(a.k, b, t, h, m);
-      for (int i = lane; i < K; i += 32) sk[i] = ld_as_f32(a.k.ptr, a.k.dtype, ko + i);
-      if (a.r_out <= 1) {
-        const int64_t qo = view_off(a.q, b, t, h, m);
-        for (int i = lane; i < K; i += 32) sq[i] = ld_as_f32(a.q.ptr, a.q.dtype, qo + i);
-      } else {
+      const int64_t qo = view_off(a.q, b, t, h, m);
+      const int64_t eo = a.gate_e.ptr ? view_off(a.gate_e, b, t, h, m) : 0;
+      const int64_t vo = view_off(a.v, b, t, h, m);
+      const int64_t wo = a.gate_w.ptr ? view_off(a.gate_w, b, t, h, m) : 0;
+      const int64_t dof = view_off(a.decay, b, t, h, m);
+      float rk[KL], rq[KL], re[KL], rd[KL], rv[VL], rw[VL];
+#pragma unroll
+      for (int c = 0; c < KL; ++c) {
+        const int i = lane + 32 * c;
+        rk[c] = rq[c] = re[c] = rd[c] = 0.f;
+        if (i < K) {
+          rk[c] = ld_as_f32(a.k.ptr, a.k.dtype, ko + i);
+          if (a.r_out <= 1) rq[c] = ld_as_f32(a.q.ptr, a.q.dtype, qo + i);
+          if (P.vec_e) re[c] = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo + i);
+          if (P.chan_decay) rd[c] = ld_as_f32(a.decay.ptr, a.decay.dtype, dof + i);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < VL; ++c) {
+        const int i = lane + 32 * c;
+        rv[c] = 0.f;
+        rw[c] = 1.f;
+        if (i < V) {
+          rv[c] = ld_as_f32(a.v.ptr, a.v.dtype, vo + i);
+          if (P.vec_w) rw[c] = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo + i);
+        }
+      }
+      // scalar gates (every lane loads them: uniform, and in flight with the rows above)
+      const bool sc_e = P.kmd2 || !P.vec_e, sc_w = P.kmd2 || !P.vec_w;
+      const float ge = sc_e ? ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo) : 1.f;
+      const float gw = sc_w ? ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo) : 1.f;
+      const float gam = P.chan_decay ? 1.0f
+                                     : decay_factor(a.decay, a.decay_kind, dof, !P.kmd2, a.braid_rates, a.braid_clamp);
+#pragma unroll
+      for (int c = 0; c < KL; ++c) {
+        const int i = lane + 32 * c;
+        if (i < K) {
+          sk[i] = rk[c];
+          if (a.r_out <= 1) sq[i] = rq[c];
+        }
+      }
+      if (a.r_out > 1) {
         for (int i = lane; i < K; i += 32) {
           float acc = 0.f;
           for (int r = 0; r < a.r_out; ++r)
@@ -105,50 +146,51 @@ recurrent_scan_kernel(const RecParams P) {
       __syncwarp();
       // erase key, dots
       float kh = 0.f, kq = 0.f, kk = 0.f;
-      const int64_t eo = a.gate_e.ptr ? view_off(a.gate_e, b, t, h, m) : 0;
-      for (int i = lane; i < K; i += 32) {
-        const float kv = sk[i];
-        float hv = kv;
-        if (P.vec_e) {
-          hv = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo + i) * kv;
-          tok[SM::kH + i] = hv;
+#pragma unroll
+      for (int c = 0; c < KL; ++c) {
+        const int i = lane + 32 * c;
+        if (i < K) {
+          const float kv = sk[i];
+          float hv = kv;
+          if (P.vec_e) {
+            hv = re[c] * kv;
+            tok[SM::kH + i] = hv;
+          }
+          kh += kv * hv;
+          kq += kv * sq[i];
+          kk += kv * kv;
         }
-        kh += kv * hv;
-        kq += kv * sq[i];
-        kk += kv * kv;
       }
       kh = warp_sum(kh);
       kq = warp_sum(kq);
       kk = warp_sum(kk);
       // write value
-      const int64_t vo = view_off(a.v, b, t, h, m);
-      const int64_t wo = a.gate_w.ptr ? view_off(a.gate_w, b, t, h, m) : 0;
-      for (int i = lane; i < V; i += 32) {
-        float uv = ld_as_f32(a.v.ptr, a.v.dtype, vo + i);
-        if (P.vec_w) uv *= ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo + i);
-        tok[SM::kU + i] = uv;
+#pragma unroll
+      for (int c = 0; c < VL; ++c) {
+        const int i = lane + 32 * c;
+        if (i < V) tok[SM::kU + i] = P.vec_w ? rv[c] * rw[c] : rv[c];
       }
-      // decay
-      const int64_t dof = view_off(a.decay, b, t, h, m);
-      float gam = 1.0f;
+      // per-channel decay
       if (P.chan_decay) {
-        for (int i = lane; i < K; i += 32) {
-          float g = ld_as_f32(a.decay.ptr, a.decay.dtype, dof + i);
-          if (a.decay_kind == GDNX_DECAY_LOG) g = expf(g);
-          if (!P.kmd2) g = fminf(fmaxf(g, 0.f), 1.f);
-          tok[SM::kD + i] = g;
+#pragma unroll
+        for (int c = 0; c < KL; ++c) {
+          const int i = lane + 32 * c;
+          if (i < K) {
+            float g = rd[c];
+            if (a.decay_kind == GDNX_DECAY_LOG) g = expf(g);
+            if (!P.kmd2) g = fminf(fmaxf(g, 0.f), 1.f);
+            tok[SM::kD + i] = g;
+          }
         }
-      } else {
-        gam = decay_factor(a.decay, a.decay_kind, dof, !P.kmd2, a.braid_rates, a.braid_clamp);
       }
       if (lane == 0) {
         float ce, cw;
         if (P.kmd2) {
-          ce = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
-          cw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo);
+          ce = ge;
+          cw = gw;
         } else {
-          const float be = P.vec_e ? 1.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
-          const float bw = P.vec_w ? 1.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo);
+          const float be = P.vec_e ? 1.f : ge;
+          const float bw = P.vec_w ? 1.f : gw;
           const float c = P.vec_e ? kh : be * kh;   // k . h
           const float al = stable_alpha(c);
           ce = al * be;
