@@ -209,11 +209,42 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       float* sk = tk + SMT::kTokK;
       float* sh = tk + SMT::kTokH;
       float* sq = tk + SMT::kTokQ;
-      const int64_t ko = view_off(a.k, b, t, h, m), qo = view_off(a.q, b, t, h, m);
+      const int64_t ko = view_off(a.k, b, t, h, m), qo = view_off(a.q, b, t, h, m), vo = view_off(a.v, b, t, h, m);
+      const int64_t eo = view_off(a.gate_e, b, t, h, m), wo = view_off(a.gate_w, b, t, h, m);
       const __nv_bfloat16* raw = rawst + tt * kRawPer;
-      for (int i = lane; i < K; i += 32) {
-        sk[i] = raw_ok ? __bfloat162float(raw[i]) : ld_as_f32(a.k.ptr, a.k.dtype, ko + i);
-        sq[i] = raw_ok ? __bfloat162float(raw[K + i]) : ld_as_f32(a.q.ptr, a.q.dtype, qo + i);
+      // every global load of the token first (one memory round trip), uses after
+      constexpr int KW = (K + 31) / 32, VW = (V + 31) / 32;
+      float rk[KW], rq[KW], re[KW], rv[VW], rw[VW];
+#pragma unroll
+      for (int c = 0; c < KW; ++c) {
+        const int i = lane + 32 * c;
+        rk[c] = rq[c] = re[c] = 0.f;
+        if (i < K) {
+          rk[c] = raw_ok ? __bfloat162float(raw[i]) : ld_as_f32(a.k.ptr, a.k.dtype, ko + i);
+          rq[c] = raw_ok ? __bfloat162float(raw[K + i]) : ld_as_f32(a.q.ptr, a.q.dtype, qo + i);
+          if (P.vec_e) re[c] = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo + i);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < VW; ++c) {
+        const int i = lane + 32 * c;
+        rv[c] = rw[c] = 0.f;
+        if (i < V) {
+          rv[c] = raw_ok ? __bfloat162float(raw[2 * K + i]) : ld_as_f32(a.v.ptr, a.v.dtype, vo + i);
+          if (P.vec_w) rw[c] = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo + i);
+        }
+      }
+      const float be = P.vec_e ? 1.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
+      const float bw = P.vec_w ? 1.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo);
+      const float gdec = decay_factor(a.decay, a.decay_kind, view_off(a.decay, b, t, h, m), true, a.braid_rates,
+                                      a.braid_clamp);
+#pragma unroll
+      for (int c = 0; c < KW; ++c) {
+        const int i = lane + 32 * c;
+        if (i < K) {
+          sk[i] = rk[c];
+          sq[i] = rq[c];
+        }
       }
       __syncwarp();
       if (dpairs > 0) {
@@ -221,27 +252,27 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
         rope_row_table(sq, dpairs, ropeC + tt * 64, ropeS + tt * 64, lane);
       }
       __syncwarp();
-      const int64_t eo = view_off(a.gate_e, b, t, h, m), wo = view_off(a.gate_w, b, t, h, m);
-      const float be = P.vec_e ? 1.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
-      const float bw = P.vec_w ? 1.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo);
       float kh = 0.f, kq = 0.f;
-      for (int i = lane; i < K; i += 32) {
-        const float hv = (P.vec_e ? ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo + i) : be) * sk[i];
-        sh[i] = hv;
-        kh += sk[i] * hv;
-        kq += sk[i] * sq[i];
+#pragma unroll
+      for (int c = 0; c < KW; ++c) {
+        const int i = lane + 32 * c;
+        if (i < K) {
+          const float hv = (P.vec_e ? re[c] : be) * sk[i];
+          sh[i] = hv;
+          kh += sk[i] * hv;
+          kq += sk[i] * sq[i];
+        }
       }
       kh = warp_sum(kh);
       kq = warp_sum(kq);
-      const int64_t vo = view_off(a.v, b, t, h, m);
-      for (int i = lane; i < V; i += 32) {
-        const float wv = P.vec_w ? ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo + i) : bw;
-        tk[SMT::kTokU + i] = wv * (raw_ok ? __bfloat162float(raw[2 * K + i]) : ld_as_f32(a.v.ptr, a.v.dtype, vo + i));
+#pragma unroll
+      for (int c = 0; c < VW; ++c) {
+        const int i = lane + 32 * c;
+        if (i < V) tk[SMT::kTokU + i] = (P.vec_w ? rw[c] : bw) * rv[c];
       }
       if (lane == 0) {
         float* sc = tk + SMT::kTokSc;
-        sc[0] = decay_factor(a.decay, a.decay_kind, view_off(a.decay, b, t, h, m), true, a.braid_rates,
-                             a.braid_clamp);
+        sc[0] = gdec;
         sc[1] = stable_alpha(kh);
         sc[2] = kq;
       }
