@@ -493,6 +493,24 @@ def main():
             krs[f"P{P}"] = {"ms_per_call": kms, "tok_per_s": kc["B"] * kc["T"] * world / (kms * 1e-3),
                             "tflops_by_formula": kf / (kms * 1e-3) / 1e12,
                             "tc_frac": kf / (kms * 1e-3) / 1e12 / peaks["bf16"]}
+        del kin
+        # the GDN3 drop-in on what GDN3LinearAttn.forward passes: fp32 per-lane q/k/v, vector gates
+        import types
+        from gdnx_b200.gdn3_upgrade import gdn3_recurrent_state
+        g2 = torch.Generator(device=dev).manual_seed(20 + rank)
+        shp = (kc["B"], kc["T"], kc["H"], kc["M"], kc["K"])
+        qx = torch.nn.functional.normalize(torch.randn(*shp, device=dev, generator=g2), dim=-1)
+        kx = torch.nn.functional.normalize(torch.randn(*shp, device=dev, generator=g2), dim=-1)
+        vx = torch.randn(*shp, device=dev, generator=g2)
+        bg = torch.sigmoid(torch.randn(*shp, device=dev, generator=g2))
+        wg = torch.sigmoid(torch.randn(*shp, device=dev, generator=g2))
+        dec = 0.78 + 0.219 * torch.rand(*shp[:4], device=dev, generator=g2)
+        layer = types.SimpleNamespace(R=4, P=256, a_v=16, a_k=16, b_v=8, b_k=8, slow_decay=0.97, compact_mode="svd")
+        dms = timed(lambda: gdn3_recurrent_state(layer, qx, kx, vx, bg, wg, dec), 2, 3, stream, barrier)
+        krs["dropin_P256_fp32_vector_gates"] = {
+            "call": "gdn3_upgrade.gdn3_recurrent_state (T >= P: KR kernel)", "ms_per_call": dms,
+            "tok_per_s": kc["B"] * kc["T"] * world / (dms * 1e-3)}
+        del qx, kx, vx, bg, wg, dec
         kr = {"metric": "KR prefill tok/s (config 2)", "B": 1, "T": kc["T"], "H": 16, "M": 4,
               "state": "A 16x16 (x) B 8x8, R=4, + U,V 128xP, delta=0.97", **krs}
 
