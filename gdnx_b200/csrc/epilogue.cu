@@ -3,6 +3,8 @@
 //   GDN3 lane routing (gdn3/gdn3_upgrade.py:842-856):
 //     w_m = softmax_m(router_logits[b,t,h,:]);  r = sum_m w_m y[b,t,h,m,:]
 //     out = r / max(|r|_2, 1e-6) * sqrt(V) * norm
+//     [* silu(z[b,t,h,:]) with an output gate z: the layer's Qwen3.5 gate when
+//      H V = D, i.e. no _agg_proj between the two (gdn3/gdn3_upgrade.py:861-871)]
 //   KMD-2 gated RMS norm (Qwen3_5RMSNormGated, gdn3/kmd2_native.py:66,176):
 //     out = weight * y * rsqrt(mean(y^2) + eps) * silu(z)
 //
@@ -78,9 +80,9 @@ GDNX_DEV float half_sum(float x) {
 
 // Lane routing: a half warp per row (8 channels per lane), two passes of two rows per
 // warp with every load of both passes issued before the arithmetic.  bf16 scan outputs
-// stay packed in registers until they are summed, so four CTAs fit on an SM.
-template <int MT, bool BF16IN>
-__global__ void __launch_bounds__(NT, 4) lane_route_kernel(const gdnx_epilogue_args a) {
+// stay packed in registers until they are summed, so four CTAs fit on an SM (two with eight lanes).
+template <int MT, bool BF16IN, bool GATE>
+__global__ void __launch_bounds__(NT, MT >= 8 ? 2 : 4) lane_route_kernel(const gdnx_epilogue_args a) {
   const int lane = threadIdx.x & 31, hw = lane >> 4, c = 8 * (lane & 15);
   const int64_t rows = a.B * a.T * a.H;
   const int64_t base = ((int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5)) * 4;
@@ -153,6 +155,12 @@ __global__ void __launch_bounds__(NT, 4) lane_route_kernel(const gdnx_epilogue_a
       float o[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = acc[e] * sc * (a.weight ? a.weight[c + e] : 1.f);
+      if (GATE) {
+        float z[8];
+        ld8f(a.gate.ptr, a.gate.dtype, rb[p] * a.gate.sb + rt[p] * a.gate.st + rh[p] * a.gate.sh + c, z);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] *= z[e] / (1.f + expf(-z[e]));
+      }
       st8f(a.out, a.out_dtype, rb[p] * a.out_sb + rt[p] * a.out_st + rh[p] * a.out_sh + c, o);
     }
   }
@@ -205,6 +213,23 @@ __global__ void __launch_bounds__(NT, 4) rms_gated_kernel(const gdnx_epilogue_ar
   }
 }
 
+template <bool GATE>
+void launch_route(const gdnx_epilogue_args& a, bool bf, int64_t blocks, cudaStream_t st) {
+  if (a.M == 1) {
+    if (bf) lane_route_kernel<1, true, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+    else lane_route_kernel<1, false, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+  } else if (a.M == 2) {
+    if (bf) lane_route_kernel<2, true, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+    else lane_route_kernel<2, false, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+  } else if (a.M <= 4) {
+    if (bf) lane_route_kernel<4, true, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+    else lane_route_kernel<4, false, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+  } else {
+    if (bf) lane_route_kernel<8, true, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+    else lane_route_kernel<8, false, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+  }
+}
+
 }  // namespace
 
 gdnx_status launch_epilogue(const gdnx_epilogue_args& a, cudaStream_t st) {
@@ -216,19 +241,8 @@ gdnx_status launch_epilogue(const gdnx_epilogue_args& a, cudaStream_t st) {
     rms_gated_kernel<<<(unsigned)blocks, NT, 0, st>>>(a);
   } else {
     const bool bf = a.y.dtype == GDNX_BF16;
-    if (a.M == 1) {
-      if (bf) lane_route_kernel<1, true><<<(unsigned)blocks, NT, 0, st>>>(a);
-      else lane_route_kernel<1, false><<<(unsigned)blocks, NT, 0, st>>>(a);
-    } else if (a.M == 2) {
-      if (bf) lane_route_kernel<2, true><<<(unsigned)blocks, NT, 0, st>>>(a);
-      else lane_route_kernel<2, false><<<(unsigned)blocks, NT, 0, st>>>(a);
-    } else if (a.M <= 4) {
-      if (bf) lane_route_kernel<4, true><<<(unsigned)blocks, NT, 0, st>>>(a);
-      else lane_route_kernel<4, false><<<(unsigned)blocks, NT, 0, st>>>(a);
-    } else {
-      if (bf) lane_route_kernel<8, true><<<(unsigned)blocks, NT, 0, st>>>(a);
-      else lane_route_kernel<8, false><<<(unsigned)blocks, NT, 0, st>>>(a);
-    }
+    if (a.gate.ptr) launch_route<true>(a, bf, blocks, st);
+    else launch_route<false>(a, bf, blocks, st);
   }
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
 }

@@ -218,6 +218,7 @@ gdnx_status gdnx_epilogue(const gdnx_epilogue_args* a, void* stream) {
   if (a->kind == GDNX_EPILOGUE_LANE_ROUTE) {
     if (a->M < 1 || a->M > 8) return GDNX_EINVAL;
     if (!is_device_ptr(a->router.ptr) || !dtype_ok(a->router.dtype) || a->router.dim != 1) return GDNX_EINVAL;
+    if (a->gate.ptr && !vec_ok(a->gate, a->V)) return GDNX_EINVAL;  // optional output gate
   } else {
     if (!vec_ok(a->gate, a->V) || !(a->eps >= 0.f)) return GDNX_EINVAL;
   }

@@ -545,12 +545,15 @@ def noalloc_status(device=None) -> int:
 # ----------------------------------------------------------------------------
 
 def lane_route(y: torch.Tensor, router_logits: torch.Tensor, norm: Optional[torch.Tensor] = None, *,
-               out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+               gate: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+               out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
     """GDN3 lane routing and per-head norm in one pass (gdn3/gdn3_upgrade.py:842-856):
     ``softmax`` over the lanes of ``router_logits [B,T,H,M]``, the weighted lane sum of
-    ``y [B,T,H,M,V]``, then ``F.normalize(., dim=-1, eps=1e-6) * sqrt(V) * norm``.
-    Returns ``[B,T,H,V]`` (``out_dtype`` defaults to ``y``'s)."""
-    _require_cuda(y, router_logits, norm, out)
+    ``y [B,T,H,M,V]``, then ``F.normalize(., dim=-1, eps=1e-6) * sqrt(V) * norm``; with
+    ``gate`` (the layer's output-gate pre-activation, ``[B,T,H*V]`` or ``[B,T,H,V]``) also
+    ``* silu(gate)``, which is the layer's next step when ``H*V == D`` (no ``_agg_proj``,
+    :861-871).  Returns ``[B,T,H,V]`` (``out_dtype`` defaults to ``y``'s)."""
+    _require_cuda(y, router_logits, norm, gate, out)
     B, T, H, M, V = y.shape
     out = out if out is not None else torch.empty(B, T, H, V, dtype=out_dtype or y.dtype, device=y.device)
     a = L.EpilogueArgs()
@@ -558,6 +561,9 @@ def lane_route(y: torch.Tensor, router_logits: torch.Tensor, norm: Optional[torc
     a.kind = L.GDNX_EPILOGUE_LANE_ROUTE
     a.y = _view(y, True)
     a.router = _view(router_logits.unsqueeze(-1), True)
+    if gate is not None:
+        gate = gate.view(B, T, H, V) if gate.dim() == 3 else gate
+        a.gate = _view(gate, False)
     w = None
     if norm is not None:
         w = norm.detach().to(torch.float32).contiguous()

@@ -277,7 +277,8 @@ GDNX_API gdnx_status gdnx_scan_bwd(const gdnx_scan_bwd_args* args, void* stream)
 typedef enum {
   /* GDN3 lane routing + head norm (gdn3/gdn3_upgrade.py:842-856):
    *   w = softmax_m(router[b,t,h,:]); r = sum_m w_m y[b,t,h,m,:];
-   *   out = r / max(|r|, 1e-6) * sqrt(V) * weight                              */
+   *   out = r / max(|r|, 1e-6) * sqrt(V) * weight  [* silu(gate) when `gate` is
+   *   set: the layer's output gate where H V = D (no _agg_proj), :861-871]     */
   GDNX_EPILOGUE_LANE_ROUTE = 0,
   /* KMD-2 gated RMS norm (Qwen3_5RMSNormGated; gdn3/kmd2_native.py:66,176):
    *   out = weight * y * rsqrt(mean(y^2) + eps) * silu(gate)                   */
@@ -291,7 +292,7 @@ typedef struct {
   float eps;                  /* RMS_GATED */
   gdnx_view y;                /* [B,T,H,M,V] (LANE_ROUTE) or [B,T,H,V] (RMS_GATED)      */
   gdnx_view router;           /* [B,T,H,M] router logits, dim 1 (LANE_ROUTE)           */
-  gdnx_view gate;             /* [B,T,H,V] gate z (RMS_GATED)                           */
+  gdnx_view gate;             /* [B,T,H,V] gate z (RMS_GATED; optional in LANE_ROUTE)   */
   const float* weight;        /* [V] fp32 device: the layer's norm weight; NULL = ones  */
   void* out;                  /* [B,T,H,V] */
   int32_t out_dtype;

@@ -72,3 +72,18 @@ def test_lane_route_lane_counts(M):
     norm = 1 + 0.1 * torch.randn(128, generator=g)
     out = ops.lane_route(y.to(DEV), logits.to(DEV), norm.to(DEV))
     assert rel(out, E.lane_route(y, logits, norm)) < 1e-5
+
+
+@pytest.mark.parametrize("M,dtype", [(4, torch.bfloat16), (2, torch.float32)])
+def test_lane_route_with_output_gate(M, dtype):
+    """The layer's output gate fused into the routing (H*V == D: no _agg_proj), the gate
+    given as the [B,T,H*V] projection output."""
+    g = torch.Generator().manual_seed(40 + M)
+    B, T, H, V = 2, 13, 3, 128
+    y = torch.randn(B, T, H, M, V, generator=g).to(dtype)
+    logits = torch.randn(B, T, H, M, generator=g)
+    norm = 1 + 0.1 * torch.randn(V, generator=g)
+    z = torch.randn(B, T, H * V, generator=g).to(dtype)
+    out = ops.lane_route(y.to(DEV), logits.to(DEV), norm.to(DEV), gate=z.to(DEV), out_dtype=torch.float32)
+    ref = E.lane_route(y.float(), logits, norm, gate=z.float().view(B, T, H, V))
+    assert rel(out, ref) < 1e-5
