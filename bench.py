@@ -234,6 +234,7 @@ def main():
     ap.add_argument("--no-config4", dest="config4", action="store_false", help="skip the config-4 sharded prefill leg")
     ap.add_argument("--config4-T", type=int, default=None, help="override config-4 T (smoke runs only)")
     ap.add_argument("--config4-slabs", type=int, default=8)
+    ap.add_argument("--no-peer-gather", action="store_true", help="skip the fused routing + peer-store gather leg")
     ap.add_argument("--no-config4-ref-1gpu", dest="config4_ref_1gpu", action="store_false",
                     help="skip timing the full config-4 scan on rank 0 alone (N > 1)")
     ap.add_argument("--dropins-B", type=int, default=None, help="override the drop-in legs' B (profiling runs only)")
@@ -394,13 +395,44 @@ def main():
             stream.wait_stream(comm)
 
         ms4e = timed(scan_route_gather, 3, 3, stream, barrier)
+        # the same pipeline with the routing kernel storing its rows straight into every
+        # rank's copy of the full routed output over NVLink (one fused kernel per slab, no
+        # separate all-gather), one small all-reduce at the end as the completion barrier
+        ms4p = None
+        if dist and sh.axis == "batch" and not args.no_peer_gather:
+            from gdnx_b200.distributed import PeerBuffer
+            Bl, T4, H4, V4 = lc["B"], lc["T"], lc["H"], lc["V"]
+            pbuf = PeerBuffer((world * Bl, T4, H4, V4), torch.bfloat16, dev)
+            flag = torch.zeros(1, device=dev)
+            dests = [pbuf.dest(rank * Bl * T4 * H4 * V4 + i * Ts * H4 * V4, (Bl - 1) * T4 * H4 * V4 + Ts * H4 * V4)
+                     for i in range(slabs)]
+
+            def scan_route_scatter():
+                state = st
+                for i in range(slabs):
+                    if i >= 2:
+                        stream.wait_event(ev_comm[i % 2])  # ybuf [i % 2] consumed
+                    state = slab(i, state)
+                    ev_scan[i % 2].record(stream)
+                    with torch.cuda.stream(comm):
+                        comm.wait_event(ev_scan[i % 2])
+                        sl = slice(i * Ts, (i + 1) * Ts)
+                        ops.lane_route_scatter(ybuf[i % 2], router[:, sl], dests[i], (T4 * H4 * V4, H4 * V4, V4),
+                                               torch.bfloat16, norm)
+                        ev_comm[i % 2].record(comm)
+                with torch.cuda.stream(comm):
+                    dist.all_reduce(flag)  # every rank's rows have landed everywhere
+                stream.wait_stream(comm)
+
+            ms4p = timed(scan_route_scatter, 3, 3, stream, barrier)
+            pbuf.close()
         ms4g = None
         if dist:
             ms4g = timed(lambda: dist.all_gather_into_tensor(gbuf[0], rbuf[0]), 3, 1, stream, barrier) * slabs
-        vals = torch.tensor([ms4, ms4e, ms4g or 0.0], device=dev)
+        vals = torch.tensor([ms4, ms4e, ms4g or 0.0, ms4p or 0.0], device=dev)
         if dist:
             dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-        ms4, ms4e, ms4g = vals.tolist()
+        ms4, ms4e, ms4g, ms4p = vals.tolist()
         tok4 = c4["B"] * c4["T"]
         f4 = c4["B"] * c4["T"] * c4["H"] * c4["M"] * chunk_flops_per_chain_token(128, 128, 64)
         gathered = world * rbuf[0].numel() * rbuf[0].element_size() * slabs  # bytes of the full routed output
@@ -412,7 +444,11 @@ def main():
                 "allgather_ms_serial": ms4g if dist else None,
                 "allgather_bytes_total": gathered if dist else None,
                 "nccl_busbw_gbs": (gathered * (world - 1) / world / (ms4g * 1e-3) / 1e9) if dist else None,
-                "collective": "nccl all_gather_into_tensor of routed slabs on a comm stream" if dist else None}
+                "collective": "nccl all_gather_into_tensor of routed slabs on a comm stream" if dist else None,
+                "e2e_ms_pipelined_peer": ms4p or None,
+                "e2e_tok_per_s_peer": (tok4 / (ms4p * 1e-3)) if ms4p else None,
+                "peer_gather": ("gdnx_epilogue_scatter: routing + stores into every rank's copy over NVLink "
+                                "(CUDA IPC peer mappings), one all-reduce barrier per step") if ms4p else None}
         if dist and args.config4_ref_1gpu:
             # the same full config-4 scan on one GPU (rank 0), for the per-N speed-up
             t1 = torch.zeros(1, device=dev)

@@ -19,7 +19,9 @@ GDNX_EPILOGUE_LANE_ROUTE, GDNX_EPILOGUE_RMS_GATED = 0, 1
 GDNX_COMPACT_SVD, GDNX_COMPACT_SKETCH = 0, 1
 
 EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_fwd_noalloc", "gdnx_scan_noalloc_status", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
-            "gdnx_decode_step", "gdnx_epilogue", "gdnx_gdn3_prologue", "gdnx_scan_bwd", "gdnx_scan_bwd_workspace_bytes", "gdnx_status_string", "gdnx_version")
+            "gdnx_decode_step", "gdnx_epilogue", "gdnx_gdn3_prologue", "gdnx_scan_bwd", "gdnx_scan_bwd_workspace_bytes", "gdnx_status_string", "gdnx_version",
+            "gdnx_epilogue_scatter", "gdnx_device_alloc", "gdnx_device_free", "gdnx_ipc_handle", "gdnx_ipc_open",
+            "gdnx_ipc_close")
 
 
 class View(C.Structure):
@@ -135,6 +137,18 @@ def load(path: Path = LIB_PATH):
     lib.gdnx_gdn3_prologue.restype = C.c_int
     lib.gdnx_scan_bwd.argtypes = [C.POINTER(ScanBwdArgs), C.c_void_p]
     lib.gdnx_scan_bwd.restype = C.c_int
+    lib.gdnx_epilogue_scatter.argtypes = [C.POINTER(EpilogueArgs), C.POINTER(C.c_void_p), C.c_int32, C.c_void_p]
+    lib.gdnx_epilogue_scatter.restype = C.c_int
+    lib.gdnx_device_alloc.argtypes = [C.c_size_t, C.POINTER(C.c_void_p)]
+    lib.gdnx_device_alloc.restype = C.c_int
+    lib.gdnx_device_free.argtypes = [C.c_void_p]
+    lib.gdnx_device_free.restype = C.c_int
+    lib.gdnx_ipc_handle.argtypes = [C.c_void_p, C.c_void_p]
+    lib.gdnx_ipc_handle.restype = C.c_int
+    lib.gdnx_ipc_open.argtypes = [C.c_void_p, C.POINTER(C.c_void_p)]
+    lib.gdnx_ipc_open.restype = C.c_int
+    lib.gdnx_ipc_close.argtypes = [C.c_void_p]
+    lib.gdnx_ipc_close.restype = C.c_int
     lib.gdnx_scan_bwd_workspace_bytes.argtypes = [C.POINTER(ScanBwdArgs)]
     lib.gdnx_scan_bwd_workspace_bytes.restype = C.c_size_t
     lib.gdnx_status_string.argtypes = [C.c_int]

@@ -17,6 +17,12 @@
 namespace gdnx {
 namespace {
 
+// Destination buffers of the scattering routing (identical layouts, `a.out`'s strides).
+struct PeerOuts {
+  void* p[kMaxPeerOuts];
+  int n;
+};
+
 constexpr int NT = 256;  // 8 rows per CTA
 
 GDNX_DEV void ld4f(const void* p, int dtype, int64_t off, float* x) {
@@ -81,8 +87,13 @@ GDNX_DEV float half_sum(float x) {
 // Lane routing: a half warp per row (8 channels per lane), two passes of two rows per
 // warp with every load of both passes issued before the arithmetic.  bf16 scan outputs
 // stay packed in registers until they are summed, so four CTAs fit on an SM (two with eight lanes).
-template <int MT, bool BF16IN, bool GATE>
-__global__ void __launch_bounds__(NT, MT >= 8 ? 2 : 4) lane_route_kernel(const gdnx_epilogue_args a) {
+// With SCAT the routed rows are stored to every buffer of `outs` (this GPU's and its peers'
+// over NVLink: the routing fused with the all-gather of its output) instead of a.out, and
+// each thread fences at system scope after its stores, so that once the kernel has
+// completed its writes are visible to the peers.
+template <int MT, bool BF16IN, bool GATE, bool SCAT>
+__global__ void __launch_bounds__(NT, MT >= 8 ? 2 : 4) lane_route_kernel(const gdnx_epilogue_args a,
+                                                                         const PeerOuts outs) {
   const int lane = threadIdx.x & 31, hw = lane >> 4, c = 8 * (lane & 15);
   const int64_t rows = a.B * a.T * a.H;
   const int64_t base = ((int64_t)blockIdx.x * (NT / 32) + (threadIdx.x >> 5)) * 4;
@@ -161,9 +172,16 @@ __global__ void __launch_bounds__(NT, MT >= 8 ? 2 : 4) lane_route_kernel(const g
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[e] *= z[e] / (1.f + expf(-z[e]));
       }
-      st8f(a.out, a.out_dtype, rb[p] * a.out_sb + rt[p] * a.out_st + rh[p] * a.out_sh + c, o);
+      const int64_t oo = rb[p] * a.out_sb + rt[p] * a.out_st + rh[p] * a.out_sh + c;
+      if (SCAT) {
+#pragma unroll 1
+        for (int d = 0; d < outs.n; ++d) st8f(outs.p[d], a.out_dtype, oo, o);
+      } else {
+        st8f(a.out, a.out_dtype, oo, o);
+      }
     }
   }
+  if (SCAT) __threadfence_system();
 }
 
 // Gated RMS norm: a half warp per row, four rows per warp, loads first.
@@ -213,20 +231,20 @@ __global__ void __launch_bounds__(NT, 4) rms_gated_kernel(const gdnx_epilogue_ar
   }
 }
 
-template <bool GATE>
-void launch_route(const gdnx_epilogue_args& a, bool bf, int64_t blocks, cudaStream_t st) {
+template <bool GATE, bool SCAT>
+void launch_route(const gdnx_epilogue_args& a, const PeerOuts& o, bool bf, int64_t blocks, cudaStream_t st) {
   if (a.M == 1) {
-    if (bf) lane_route_kernel<1, true, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
-    else lane_route_kernel<1, false, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+    if (bf) lane_route_kernel<1, true, GATE, SCAT><<<(unsigned)blocks, NT, 0, st>>>(a, o);
+    else lane_route_kernel<1, false, GATE, SCAT><<<(unsigned)blocks, NT, 0, st>>>(a, o);
   } else if (a.M == 2) {
-    if (bf) lane_route_kernel<2, true, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
-    else lane_route_kernel<2, false, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+    if (bf) lane_route_kernel<2, true, GATE, SCAT><<<(unsigned)blocks, NT, 0, st>>>(a, o);
+    else lane_route_kernel<2, false, GATE, SCAT><<<(unsigned)blocks, NT, 0, st>>>(a, o);
   } else if (a.M <= 4) {
-    if (bf) lane_route_kernel<4, true, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
-    else lane_route_kernel<4, false, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+    if (bf) lane_route_kernel<4, true, GATE, SCAT><<<(unsigned)blocks, NT, 0, st>>>(a, o);
+    else lane_route_kernel<4, false, GATE, SCAT><<<(unsigned)blocks, NT, 0, st>>>(a, o);
   } else {
-    if (bf) lane_route_kernel<8, true, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
-    else lane_route_kernel<8, false, GATE><<<(unsigned)blocks, NT, 0, st>>>(a);
+    if (bf) lane_route_kernel<8, true, GATE, SCAT><<<(unsigned)blocks, NT, 0, st>>>(a, o);
+    else lane_route_kernel<8, false, GATE, SCAT><<<(unsigned)blocks, NT, 0, st>>>(a, o);
   }
 }
 
@@ -241,9 +259,27 @@ gdnx_status launch_epilogue(const gdnx_epilogue_args& a, cudaStream_t st) {
     rms_gated_kernel<<<(unsigned)blocks, NT, 0, st>>>(a);
   } else {
     const bool bf = a.y.dtype == GDNX_BF16;
-    if (a.gate.ptr) launch_route<true>(a, bf, blocks, st);
-    else launch_route<false>(a, bf, blocks, st);
+    PeerOuts none{};
+    if (a.gate.ptr) launch_route<true, false>(a, none, bf, blocks, st);
+    else launch_route<false, false>(a, none, bf, blocks, st);
   }
+  return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
+}
+
+}  // namespace gdnx
+
+namespace gdnx {
+
+gdnx_status launch_epilogue_scatter(const gdnx_epilogue_args& a, void* const* outs, int n, cudaStream_t st) {
+  const int64_t rows = a.B * a.T * a.H;
+  const int64_t blocks = (rows + 4 * (NT / 32) - 1) / (4 * (NT / 32));
+  if (rows >= int64_t(0x7fffffff) || n < 1 || n > kMaxPeerOuts) return GDNX_EUNSUPPORTED;
+  PeerOuts o{};
+  for (int d = 0; d < n; ++d) o.p[d] = outs[d];
+  o.n = n;
+  const bool bf = a.y.dtype == GDNX_BF16;
+  if (a.gate.ptr) launch_route<true, true>(a, o, bf, blocks, st);
+  else launch_route<false, true>(a, o, bf, blocks, st);
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
 }
 

@@ -1,5 +1,6 @@
 // C-ABI entry points: host-side validation and kernel dispatch.
 #include <cstdio>
+#include <cstring>
 #include <cuda_runtime.h>
 
 #include "gdnx.h"
@@ -227,6 +228,76 @@ gdnx_status gdnx_epilogue(const gdnx_epilogue_args* a, void* stream) {
   const int al = a->out_dtype == GDNX_F32 ? 16 : 8;
   if (reinterpret_cast<uintptr_t>(a->out) % al || a->out_sb % 8 || a->out_st % 8 || a->out_sh % 8) return GDNX_EINVAL;
   return gdnx::launch_epilogue(*a, (cudaStream_t)stream);
+}
+
+gdnx_status gdnx_epilogue_scatter(const gdnx_epilogue_args* a, void* const* outs, int32_t n_outs, void* stream) {
+  if (!a || !outs || n_outs < 1 || n_outs > gdnx::kMaxPeerOuts) return GDNX_EINVAL;
+  if (a->kind != GDNX_EPILOGUE_LANE_ROUTE) return GDNX_EINVAL;
+  const int al = a->out_dtype == GDNX_F32 ? 16 : 8;
+  for (int d = 0; d < n_outs; ++d)
+    if (!is_device_ptr(outs[d]) || reinterpret_cast<uintptr_t>(outs[d]) % al) return GDNX_EINVAL;
+  // the single-destination checks, on a copy whose `out` is the first destination
+  gdnx_epilogue_args one = *a;
+  one.out = outs[0];
+  if (one.B == 0 || one.T == 0) return GDNX_OK;
+  if (one.B < 0 || one.T < 0 || one.H <= 0 || one.V <= 0 || one.V > 128 || one.V % 8 || one.M < 1 || one.M > 8)
+    return GDNX_EINVAL;
+  if (!is_device_ptr(one.y.ptr) || !dtype_ok(one.y.dtype) || one.y.dim != one.V ||
+      reinterpret_cast<uintptr_t>(one.y.ptr) % 16 || one.y.sb % 8 || one.y.st % 8 || one.y.sh % 8 || one.y.sm % 8 ||
+      one.y.sb < 0 || one.y.st < 0 || one.y.sh < 0 || one.y.sm < 0)
+    return GDNX_EINVAL;
+  if (!is_device_ptr(one.router.ptr) || !dtype_ok(one.router.dtype) || one.router.dim != 1) return GDNX_EINVAL;
+  if (one.gate.ptr && (!is_device_ptr(one.gate.ptr) || !dtype_ok(one.gate.dtype) || one.gate.dim != one.V ||
+                       reinterpret_cast<uintptr_t>(one.gate.ptr) % 16 || one.gate.sb % 8 || one.gate.st % 8 ||
+                       one.gate.sh % 8))
+    return GDNX_EINVAL;
+  if (one.weight && !is_device_ptr(one.weight)) return GDNX_EINVAL;
+  if (!dtype_ok(one.out_dtype) || one.out_sb % 8 || one.out_st % 8 || one.out_sh % 8) return GDNX_EINVAL;
+  return gdnx::launch_epilogue_scatter(one, outs, n_outs, (cudaStream_t)stream);
+}
+
+gdnx_status gdnx_device_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return GDNX_EINVAL;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    *ptr = nullptr;
+    return GDNX_ELAUNCH;
+  }
+  return GDNX_OK;
+}
+
+gdnx_status gdnx_device_free(void* ptr) {
+  if (!ptr) return GDNX_OK;
+  return cudaFree(ptr) == cudaSuccess ? GDNX_OK : GDNX_EINVAL;
+}
+
+gdnx_status gdnx_ipc_handle(const void* base, void* handle) {
+  if (!base || !handle) return GDNX_EINVAL;
+  static_assert(sizeof(cudaIpcMemHandle_t) == GDNX_IPC_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(base)) != cudaSuccess) {
+    cudaGetLastError();
+    return GDNX_EINVAL;
+  }
+  memcpy(handle, &h, sizeof(h));
+  return GDNX_OK;
+}
+
+gdnx_status gdnx_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return GDNX_EINVAL;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    *ptr = nullptr;
+    return GDNX_EINVAL;
+  }
+  return GDNX_OK;
+}
+
+gdnx_status gdnx_ipc_close(void* ptr) {
+  if (!ptr) return GDNX_OK;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? GDNX_OK : GDNX_EINVAL;
 }
 
 gdnx_status gdnx_gdn3_prologue(const gdnx_prologue_args* a, void* stream) {

@@ -2,10 +2,12 @@
 
 Chains (b, h, m) are independent, so a rank scans its own rows of the batch
 (or, when the batch is smaller than the world, its own heads) with no
-data-path communication; the only collective is one all-gather of the
-per-lane outputs after the scan (``all_gather_into_tensor``, NCCL over
-NVLink/NVSwitch on GPUs, gloo in the CPU tests).  Every rank keeps all M
-lanes of its heads, so the lane-shared q/k/v reads stay local.
+data-path communication; the only exchange is one all-gather of the outputs
+after the scan: ``all_gather_into_tensor`` (NCCL over NVLink/NVSwitch on GPUs,
+gloo in the CPU tests), or -- for the routed GDN3 output -- the routing kernel
+itself storing its rows into every rank's copy of a :class:`PeerBuffer` over
+NVLink (``ops.lane_route_scatter``).  Every rank keeps all M lanes of its
+heads, so the lane-shared q/k/v reads stay local.
 """
 from __future__ import annotations
 
@@ -125,3 +127,80 @@ def gather_with_deadline(out: torch.Tensor, local: torch.Tensor, timeout_s: floa
         time.sleep(poll_s)
     work.wait()
     return out
+
+
+class PeerBuffer:
+    """One device buffer per rank of ``group`` (a node's GPUs, one process each), with
+    every rank holding the addresses of all ranks' copies: the buffer is ``cudaMalloc``'d
+    by the library, its CUDA IPC handle all-gathered through ``group`` and each peer's
+    copy mapped into this process (plain peer mappings over NVLink).
+
+    ``tensor`` is this rank's copy as a ``torch`` tensor of ``shape`` / ``dtype``;
+    ``dest(rank_offset_elems)`` gives the device addresses of element offset ``o`` in
+    every rank's copy, rank 0 first, after checking that ``extent`` elements from there
+    stay inside the buffer.  ``close()`` (collective) unmaps and frees.
+    """
+
+    def __init__(self, shape, dtype, device, group=None):
+        import ctypes as C
+        import torch.distributed as dist
+        from . import _lib as L
+        self._dist, self._group = dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("PeerBuffer: at most 8 ranks (one node)")
+        self.shape, self.dtype, self.device = tuple(shape), dtype, torch.device(device)
+        esz = torch.empty((), dtype=dtype).element_size()
+        self.numel = 1
+        for d in self.shape:
+            self.numel *= int(d)
+        self.esz = esz
+        nbytes = self.numel * esz
+        lib = L.load()
+        self._lib = lib
+        with torch.cuda.device(self.device):
+            p = C.c_void_p()
+            L.check(lib.gdnx_device_alloc(nbytes, C.byref(p)), "gdnx_device_alloc")
+            self.base = p.value
+            h = (C.c_uint8 * 64)()
+            L.check(lib.gdnx_ipc_handle(C.c_void_p(self.base), h), "gdnx_ipc_handle")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h), group=group)
+            self.ptrs = []
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    self.ptrs.append(self.base)
+                    continue
+                q = C.c_void_p()
+                L.check(lib.gdnx_ipc_open((C.c_uint8 * 64).from_buffer_copy(hb), C.byref(q)), "gdnx_ipc_open")
+                self.ptrs.append(q.value)
+
+        class _Raw:  # a zero-copy byte view of the buffer for torch
+            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (self.base, False), "version": 2}
+
+        self.tensor = torch.as_tensor(_Raw(), device=self.device).view(dtype).view(self.shape)
+
+    def dest(self, offset: int, extent: int):
+        """Device addresses of element ``offset`` in every rank's copy (``extent`` elements
+        from there must lie inside the buffer)."""
+        if offset < 0 or extent < 1 or offset + extent > self.numel:
+            raise ValueError(f"PeerBuffer: elements [{offset}, {offset + extent}) outside [0, {self.numel})")
+        return [p + offset * self.esz for p in self.ptrs]
+
+    def close(self):
+        """Collective: every rank's writes finish, every rank unmaps its peers' copies, and
+        only then does each rank free its own."""
+        if self.base is None:
+            return
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            self._dist.barrier(group=self._group)
+            for r, p in enumerate(self.ptrs):
+                if r != self.rank:
+                    self._lib.gdnx_ipc_close(p)
+            torch.cuda.synchronize()
+            self._dist.barrier(group=self._group)
+            self.tensor = None
+            self._lib.gdnx_device_free(self.base)
+        self.base = None

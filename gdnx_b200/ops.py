@@ -576,6 +576,37 @@ def lane_route(y: torch.Tensor, router_logits: torch.Tensor, norm: Optional[torc
     return out
 
 
+def lane_route_scatter(y: torch.Tensor, router_logits: torch.Tensor, dests, out_strides, out_dtype: torch.dtype,
+                       norm: Optional[torch.Tensor] = None, *, gate: Optional[torch.Tensor] = None) -> None:
+    """:func:`lane_route` with the routed rows stored to every device address in ``dests``
+    (this GPU's buffer and its peers', e.g. from ``distributed.PeerBuffer``): the routing
+    fused with the all-gather of its output.  ``out_strides`` are the element strides
+    (batch, token, head) of the destination layout; each destination must have room for
+    ``[B,T,H,V]`` there.  The peers may read the rows once a cross-GPU collective issued
+    after this call on the same stream has completed."""
+    _require_cuda(y, router_logits, norm, gate)
+    B, T, H, M, V = y.shape
+    a = L.EpilogueArgs()
+    a.B, a.T, a.H, a.M, a.V = B, T, H, M, V
+    a.kind = L.GDNX_EPILOGUE_LANE_ROUTE
+    a.y = _view(y, True)
+    a.router = _view(router_logits.unsqueeze(-1), True)
+    if gate is not None:
+        gate = gate.view(B, T, H, V) if gate.dim() == 3 else gate
+        a.gate = _view(gate, False)
+    w = None
+    if norm is not None:
+        w = norm.detach().to(torch.float32).contiguous()
+        a.weight = w.data_ptr()
+    a.out_dtype = _DT[out_dtype]
+    a.out_sb, a.out_st, a.out_sh = out_strides
+    arr = (C.c_void_p * len(dests))(*dests)
+    lib = L.load()
+    with torch.cuda.device(y.device):
+        L.check(lib.gdnx_epilogue_scatter(C.byref(a), arr, len(dests), C.c_void_p(_stream(y.device))),
+                "gdnx_epilogue_scatter")
+
+
 def rms_norm_gated(y: torch.Tensor, gate: torch.Tensor, weight: Optional[torch.Tensor] = None, *, eps: float = 1e-6,
                    out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
     """KMD-2 output norm (``Qwen3_5RMSNormGated`` as called at gdn3/kmd2_native.py:176):

@@ -304,6 +304,29 @@ typedef struct {
  * Qwen3_5RMSNormGated call after KMD2NativeAttn._scan (gdn3/kmd2_native.py:176). */
 GDNX_API gdnx_status gdnx_epilogue(const gdnx_epilogue_args* args, void* stream);
 
+/* The GDN3 lane routing (kind GDNX_EPILOGUE_LANE_ROUTE) fused with the all-gather
+ * of its output across the GPUs of a node: every routed row is stored to each of
+ * the n_outs (1..8) buffers `outs` -- this GPU's own and its peers', opened with
+ * gdnx_ipc_open -- at the offset `args->out_*` strides give it (args->out itself is
+ * not used), and each thread fences at system scope after its stores.  The peers
+ * may read the rows once this kernel has completed (order that by a collective
+ * or another cross-GPU signal issued after it).  Replaces lane routing followed by
+ * an all-gather of the routed [B,T,H,V] output; the reference has no multi-GPU path. */
+GDNX_API gdnx_status gdnx_epilogue_scatter(const gdnx_epilogue_args* args, void* const* outs, int32_t n_outs,
+                                           void* stream);
+
+/* Device buffers that other processes of the node can map (cudaMalloc'd, so their
+ * base address is what the IPC handle refers to), and the CUDA IPC handle calls on
+ * them: gdnx_ipc_handle writes GDNX_IPC_HANDLE_BYTES bytes; gdnx_ipc_open maps a
+ * peer's buffer into this process (peer access enabled on first use);
+ * gdnx_ipc_close unmaps it.  Plumbing for gdnx_epilogue_scatter. */
+#define GDNX_IPC_HANDLE_BYTES 64
+GDNX_API gdnx_status gdnx_device_alloc(size_t bytes, void** ptr);
+GDNX_API gdnx_status gdnx_device_free(void* ptr);
+GDNX_API gdnx_status gdnx_ipc_handle(const void* base, void* handle);
+GDNX_API gdnx_status gdnx_ipc_open(const void* handle, void** ptr);
+GDNX_API gdnx_status gdnx_ipc_close(void* ptr);
+
 /* GDN3 projection prologue: the per-element work between the layer's input GEMMs
  * and the scan.  Views as elsewhere ([B,T,H,(M|C,)D], last dim contiguous);
  * `qkv` is the [B,T,3*H*K] qkv projection (sb, st used; channel (3h + p) K + c
