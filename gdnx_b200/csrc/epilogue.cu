@@ -74,6 +74,17 @@ GDNX_DEV void ld8f(const void* p, int dtype, int64_t off, float* x) {
   ld4f(p, dtype, off + 4, x + 4);
 }
 GDNX_DEV void st8f(void* p, int dtype, int64_t off, const float* x) {
+  if (dtype == GDNX_BF16) {  // one 16-byte store
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 t = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&t);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p) + off) = u;
+    return;
+  }
   st4f(p, dtype, off, x);
   st4f(p, dtype, off + 4, x + 4);
 }

@@ -225,7 +225,7 @@ gdnx_status gdnx_epilogue(const gdnx_epilogue_args* a, void* stream) {
   }
   if (a->weight && !is_device_ptr(a->weight)) return GDNX_EINVAL;
   if (!is_device_ptr(a->out) || !dtype_ok(a->out_dtype)) return GDNX_EINVAL;
-  const int al = a->out_dtype == GDNX_F32 ? 16 : 8;
+  const int al = 16;  // 8-element rows are stored as 16-byte (bf16) or 2 x 16-byte (fp32) chunks
   if (reinterpret_cast<uintptr_t>(a->out) % al || a->out_sb % 8 || a->out_st % 8 || a->out_sh % 8) return GDNX_EINVAL;
   return gdnx::launch_epilogue(*a, (cudaStream_t)stream);
 }
@@ -233,7 +233,7 @@ gdnx_status gdnx_epilogue(const gdnx_epilogue_args* a, void* stream) {
 gdnx_status gdnx_epilogue_scatter(const gdnx_epilogue_args* a, void* const* outs, int32_t n_outs, void* stream) {
   if (!a || !outs || n_outs < 1 || n_outs > gdnx::kMaxPeerOuts) return GDNX_EINVAL;
   if (a->kind != GDNX_EPILOGUE_LANE_ROUTE) return GDNX_EINVAL;
-  const int al = a->out_dtype == GDNX_F32 ? 16 : 8;
+  const int al = 16;  // 8-element rows are stored as 16-byte (bf16) or 2 x 16-byte (fp32) chunks
   for (int d = 0; d < n_outs; ++d)
     if (!is_device_ptr(outs[d]) || reinterpret_cast<uintptr_t>(outs[d]) % al) return GDNX_EINVAL;
   // the single-destination checks, on a copy whose `out` is the first destination

@@ -287,7 +287,8 @@ typedef enum {
 
 typedef struct {
   int64_t B, T, H, M, V;      /* M <= 8 lanes (LANE_ROUTE); V <= 128, a multiple of 8;
-                                 y/gate/out strides multiples of 8 elements */
+                                 y/gate/out strides multiples of 8 elements, their
+                                 base addresses 16-byte aligned */
   int32_t kind;               /* gdnx_epilogue_kind */
   float eps;                  /* RMS_GATED */
   gdnx_view y;                /* [B,T,H,M,V] (LANE_ROUTE) or [B,T,H,V] (RMS_GATED)      */
