@@ -168,13 +168,21 @@ class PeerBuffer:
             handles = [None] * self.world
             dist.all_gather_object(handles, bytes(h), group=group)
             self.ptrs = []
-            for r, hb in enumerate(handles):
-                if r == self.rank:
-                    self.ptrs.append(self.base)
-                    continue
-                q = C.c_void_p()
-                L.check(lib.gdnx_ipc_open((C.c_uint8 * 64).from_buffer_copy(hb), C.byref(q)), "gdnx_ipc_open")
-                self.ptrs.append(q.value)
+            try:
+                for r, hb in enumerate(handles):
+                    if r == self.rank:
+                        self.ptrs.append(self.base)
+                        continue
+                    q = C.c_void_p()
+                    L.check(lib.gdnx_ipc_open((C.c_uint8 * 64).from_buffer_copy(hb), C.byref(q)), "gdnx_ipc_open")
+                    self.ptrs.append(q.value)
+            except Exception:  # undo this rank's mappings and buffer; the peers see the failure at their next collective
+                for r, ptr in enumerate(self.ptrs):
+                    if r != self.rank:
+                        lib.gdnx_ipc_close(C.c_void_p(ptr))
+                lib.gdnx_device_free(C.c_void_p(self.base))
+                self.base = None
+                raise
 
         class _Raw:  # a zero-copy byte view of the buffer for torch
             __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (self.base, False), "version": 2}
