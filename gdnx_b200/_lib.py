@@ -19,7 +19,7 @@ GDNX_EPILOGUE_LANE_ROUTE, GDNX_EPILOGUE_RMS_GATED = 0, 1
 GDNX_COMPACT_SVD, GDNX_COMPACT_SKETCH = 0, 1
 
 EXPORTED = ("gdnx_scan_fwd", "gdnx_scan_fwd_noalloc", "gdnx_scan_noalloc_status", "gdnx_scan_workspace_bytes", "gdnx_kr_scan_fwd", "gdnx_compact",
-            "gdnx_decode_step", "gdnx_epilogue", "gdnx_gdn3_prologue", "gdnx_scan_bwd", "gdnx_scan_bwd_workspace_bytes", "gdnx_status_string", "gdnx_version",
+            "gdnx_decode_step", "gdnx_epilogue", "gdnx_gdn3_prologue", "gdnx_kmd2_prologue", "gdnx_scan_bwd", "gdnx_scan_bwd_workspace_bytes", "gdnx_status_string", "gdnx_version",
             "gdnx_epilogue_scatter", "gdnx_device_alloc", "gdnx_device_free", "gdnx_ipc_handle", "gdnx_ipc_open",
             "gdnx_ipc_close")
 
@@ -105,6 +105,16 @@ class PrologueArgs(C.Structure):
                 ("wgate_sb", C.c_int64), ("wgate_st", C.c_int64), ("wgate_sh", C.c_int64), ("wgate_sm", C.c_int64)]
 
 
+class Kmd2PrologueArgs(C.Structure):
+    _fields_ = [("B", C.c_int64), ("T", C.c_int64), ("H", C.c_int64), ("dk", C.c_int64), ("dv", C.c_int64),
+                ("r_out", C.c_int32), ("conv_k", C.c_int32), ("mixed", View), ("conv_w", C.c_void_p),
+                ("b", View), ("a", View), ("theta", View),
+                ("dt_bias", C.c_void_p), ("A_log", C.c_void_p), ("decay_chan", C.c_void_p), ("bw_off", C.c_void_p),
+                ("q_slot_scale", C.c_void_p),
+                ("q_out", C.c_void_p), ("k_out", C.c_void_p), ("v_out", C.c_void_p), ("g_out", C.c_void_p),
+                ("beta_e_out", C.c_void_p), ("beta_w_out", C.c_void_p), ("theta_ws", C.c_void_p)]
+
+
 _lib = None
 
 
@@ -135,6 +145,8 @@ def load(path: Path = LIB_PATH):
     lib.gdnx_epilogue.restype = C.c_int
     lib.gdnx_gdn3_prologue.argtypes = [C.POINTER(PrologueArgs), C.c_void_p]
     lib.gdnx_gdn3_prologue.restype = C.c_int
+    lib.gdnx_kmd2_prologue.argtypes = [C.POINTER(Kmd2PrologueArgs), C.c_void_p]
+    lib.gdnx_kmd2_prologue.restype = C.c_int
     lib.gdnx_scan_bwd.argtypes = [C.POINTER(ScanBwdArgs), C.c_void_p]
     lib.gdnx_scan_bwd.restype = C.c_int
     lib.gdnx_epilogue_scatter.argtypes = [C.POINTER(EpilogueArgs), C.POINTER(C.c_void_p), C.c_int32, C.c_void_p]

@@ -300,6 +300,29 @@ gdnx_status gdnx_ipc_close(void* ptr) {
   return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? GDNX_OK : GDNX_EINVAL;
 }
 
+gdnx_status gdnx_kmd2_prologue(const gdnx_kmd2_prologue_args* a, void* stream) {
+  if (!a) return GDNX_EINVAL;
+  if (a->B < 0 || a->T < 0 || a->H <= 0 || a->dk != 128 || a->dv != 128 || a->r_out < 1 || a->r_out > 64 ||
+      a->conv_k < 1 || a->conv_k > 8)
+    return GDNX_EINVAL;
+  if (a->B == 0 || a->T == 0) return GDNX_OK;
+  const int64_t C = 2 * a->H * a->dk + a->H * a->dv;
+  auto view_ok = [](const gdnx_view& v, int64_t dim) {
+    return is_device_ptr(v.ptr) && dtype_ok(v.dtype) && v.dim == dim && v.sb >= 0 && v.st >= 0;
+  };
+  if (!view_ok(a->mixed, C) || !view_ok(a->b, a->H) || !view_ok(a->a, a->H) || !view_ok(a->theta, a->H * a->dk / 2))
+    return GDNX_EINVAL;
+  if (!is_device_ptr(a->conv_w) || !is_device_ptr(a->dt_bias) || !is_device_ptr(a->A_log) ||
+      !is_device_ptr(a->decay_chan) || !is_device_ptr(a->bw_off))
+    return GDNX_EINVAL;
+  if ((a->r_out > 1) != (a->q_slot_scale != nullptr) || (a->q_slot_scale && !is_device_ptr(a->q_slot_scale)))
+    return GDNX_EINVAL;
+  if (!is_device_ptr(a->q_out) || !is_device_ptr(a->k_out) || !is_device_ptr(a->v_out) || !is_device_ptr(a->g_out) ||
+      !is_device_ptr(a->beta_e_out) || !is_device_ptr(a->beta_w_out) || !is_device_ptr(a->theta_ws))
+    return GDNX_EINVAL;
+  return gdnx::launch_kmd2_prologue(*a, (cudaStream_t)stream);
+}
+
 gdnx_status gdnx_gdn3_prologue(const gdnx_prologue_args* a, void* stream) {
   if (!a) return GDNX_EINVAL;
   if (a->B < 0 || a->T < 0 || a->H <= 0 || a->M <= 0 || a->K <= 0 || a->V <= 0 || a->V > a->K) return GDNX_EINVAL;

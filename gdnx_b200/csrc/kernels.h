@@ -13,6 +13,7 @@ gdnx_status launch_epilogue(const gdnx_epilogue_args& a, cudaStream_t st);
 constexpr int kMaxPeerOuts = 8;  // destinations of the scattering lane routing
 gdnx_status launch_epilogue_scatter(const gdnx_epilogue_args& a, void* const* outs, int n, cudaStream_t st);
 gdnx_status launch_proj_prologue(const gdnx_prologue_args& a, cudaStream_t st);
+gdnx_status launch_kmd2_prologue(const gdnx_kmd2_prologue_args& a, cudaStream_t st);
 // Backward of the dense scan (scan_backward.cu).
 bool scan_bwd_supported(const gdnx_scan_bwd_args& a);
 size_t scan_bwd_workspace_bytes(const gdnx_scan_bwd_args& a);

@@ -691,6 +691,56 @@ def gdn3_prologue(qkv, conv_w, *, H: int, K: int, M: int, coprod=None, mix=None,
     return (q, k, v), (bg, wg)
 
 
+def kmd2_prologue(mixed, conv_w, b, a, theta, *, H: int, dt_bias, A_log, decay_chan, bw_off,
+                  q_slot_scale=None, r_out: int = 1, dk: int = 128, dv: int = 128):
+    """KMD-2 prologue (gdn3/kmd2_native.py:140-172) from the layer's GEMM outputs to its scan inputs.
+
+    ``mixed [B,T,2*H*dk+H*dv]`` (``in_proj_qkv`` output), ``conv_w`` (the depthwise ``Conv1d`` weight,
+    ``[C,1,k]``), ``b``, ``a [B,T,H]`` (``in_proj_b`` / ``in_proj_a`` outputs), ``theta [B,T,H*dk/2]``
+    (``rot_proj`` output); the module's ``dt_bias``, ``A_log``, ``decay_chan``, ``bw_off`` and, with
+    ``r_out > 1``, ``q_slot_scale [H,r_out,dk]``.  Returns ``(q [B,T,H,r_out,dk], k, v, g [B,T,H,dk],
+    beta_e, beta_w [B,T,H])`` in fp32 -- the arguments of ``KMD2NativeAttn._scan`` (``q`` squeezed to
+    ``[B,T,H,dk]`` slots of one when ``r_out == 1`` is up to the caller)."""
+    _require_cuda(mixed, conv_w, b, a, theta, dt_bias, A_log, decay_chan, bw_off, q_slot_scale)
+    B, T = mixed.shape[:2]
+    dev = mixed.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    q = torch.empty(B, T, H, r_out, dk, **f32)
+    k = torch.empty(B, T, H, dk, **f32)
+    v = torch.empty(B, T, H, dv, **f32)
+    g = torch.empty(B, T, H, dk, **f32)
+    be = torch.empty(B, T, H, **f32)
+    bw = torch.empty(B, T, H, **f32)
+    ws = torch.empty(B, T, H, dk // 2, **f32)
+    C_ = 2 * H * dk + H * dv
+    cw = conv_w.detach().reshape(C_, -1).to(torch.float32).contiguous()
+    params = [p.detach().to(torch.float32).contiguous() for p in (dt_bias, A_log, decay_chan, bw_off)]
+    qss = q_slot_scale.detach().to(torch.float32).contiguous() if (r_out > 1 and q_slot_scale is not None) else None
+    if (r_out > 1) != (qss is not None):
+        raise ValueError("q_slot_scale is required exactly when r_out > 1")
+
+    def view3(t, dim):
+        if t.stride(-1) != 1 or t.shape[-1] != dim:
+            raise ValueError("GEMM outputs must be [B,T,C] with a contiguous last dim")
+        vw = L.View()
+        vw.ptr, vw.dtype, vw.dim, vw.sb, vw.st = t.data_ptr(), _DT[t.dtype], dim, t.stride(0), t.stride(1)
+        return vw
+
+    args = L.Kmd2PrologueArgs()
+    args.B, args.T, args.H, args.dk, args.dv = B, T, H, dk, dv
+    args.r_out, args.conv_k = r_out, cw.shape[1]
+    args.mixed, args.conv_w = view3(mixed, C_), cw.data_ptr()
+    args.b, args.a, args.theta = view3(b, H), view3(a, H), view3(theta, H * dk // 2)
+    args.dt_bias, args.A_log, args.decay_chan, args.bw_off = (p.data_ptr() for p in params)
+    args.q_slot_scale = qss.data_ptr() if qss is not None else None
+    args.q_out, args.k_out, args.v_out, args.g_out = q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr()
+    args.beta_e_out, args.beta_w_out, args.theta_ws = be.data_ptr(), bw.data_ptr(), ws.data_ptr()
+    lib = L.load()
+    with torch.cuda.device(dev):
+        L.check(lib.gdnx_kmd2_prologue(C.byref(args), C.c_void_p(_stream(dev))), "gdnx_kmd2_prologue")
+    return q, k, v, g, be, bw
+
+
 # ----------------------------------------------------------------------------
 # backward of the dense scan (autograd)
 # ----------------------------------------------------------------------------

@@ -363,6 +363,40 @@ typedef struct {
  * GDN3LinearAttn.forward (gdn3/gdn3_upgrade.py:752-807, blend :201-250). */
 GDNX_API gdnx_status gdnx_gdn3_prologue(const gdnx_prologue_args* args, void* stream);
 
+/* KMD-2 prologue: everything between KMD2NativeAttn.forward's input GEMMs and its
+ * scan (gdn3/kmd2_native.py:140-172), from the GEMM outputs to the scan inputs:
+ *   depthwise causal conv (conv_k taps) + SiLU over the q|k|v channels of `mixed`;
+ *   q = normalize(q, eps 1e-6) / sqrt(dk), k = normalize(k, eps 1e-6), v as is;
+ *   beta_e = sigmoid(b), beta_w = sigmoid(b + bw_off[h]);
+ *   g[i] = min(exp(-exp(A_log[h]) softplus(a + dt_bias[h]) + decay_chan[h][i]), 1);
+ *   Theta = cumsum over t of softplus(theta) (per pair i < dk/2), and k and every
+ *   query slot q (1 + q_slot_scale[h][r]) rotated pairwise: (x_i, x_{i+dk/2}) ->
+ *   (x_i cos - x_{i+dk/2} sin, x_i sin + x_{i+dk/2} cos).
+ * Inputs are the GEMM outputs as views ([B,T,C]: sb, st used, channels contiguous);
+ * outputs fp32 contiguous.  dk = dv = 128, K-heads = V-heads = H. */
+typedef struct {
+  int64_t B, T, H, dk, dv;
+  int32_t r_out, conv_k;
+  gdnx_view mixed;             /* [B,T,2*H*dk + H*dv] in_proj_qkv output (dim = channel count) */
+  const float* conv_w;         /* [2*H*dk + H*dv, conv_k] fp32 (depthwise Conv1d weight) */
+  gdnx_view b, a;              /* [B,T,H] in_proj_b / in_proj_a outputs (dim = H)          */
+  gdnx_view theta;             /* [B,T,H*dk/2] rot_proj output, bias included (dim = H*dk/2) */
+  const float* dt_bias;        /* [H] */
+  const float* A_log;          /* [H] */
+  const float* decay_chan;     /* [H, dk] */
+  const float* bw_off;         /* [H] */
+  const float* q_slot_scale;   /* [H, r_out, dk], NULL when r_out == 1 */
+  float* q_out;                /* [B,T,H,r_out,dk] */
+  float* k_out;                /* [B,T,H,dk] */
+  float* v_out;                /* [B,T,H,dv] */
+  float* g_out;                /* [B,T,H,dk] */
+  float* beta_e_out;           /* [B,T,H] */
+  float* beta_w_out;           /* [B,T,H] */
+  float* theta_ws;             /* [B,T,H,dk/2] workspace: the cumulative angles */
+} gdnx_kmd2_prologue_args;
+
+GDNX_API gdnx_status gdnx_kmd2_prologue(const gdnx_kmd2_prologue_args* args, void* stream);
+
 GDNX_API const char* gdnx_status_string(gdnx_status s);
 
 /* Library build identification (for load checks). */

@@ -130,3 +130,38 @@ def projection_prologue(qkv, conv_w, H, K, coprod=None, mix=None, b_proj=None, p
         M = w_proj.shape[3]
         wg = torch.sigmoid(w_proj + proj_b.unsqueeze(3).expand(-1, -1, -1, M).unsqueeze(-1) * 0.1)
     return (q, k, v), (bg, wg)
+
+
+def kmd2_prologue(mixed, conv_w, b, a, theta, dt_bias, A_log, decay_chan, bw_off, q_slot_scale=None,
+                  *, H, dk=128, dv=128, r_out=1, conv_k=4):
+    """Restates ``KMD2NativeAttn.forward`` between its input GEMMs and ``_scan``
+    (gdn3/kmd2_native.py:140-172) op for op on the GEMM outputs.  Returns the ``_scan``
+    arguments ``(qs [B,T,H,r_out,dk], k, v, g, beta_e, beta_w)``."""
+    import torch.nn.functional as F
+    B, T = mixed.shape[:2]
+    key_dim, value_dim = H * dk, H * dv
+    x = mixed.transpose(1, 2)
+    x = F.silu(F.conv1d(x, conv_w, padding=conv_k - 1, groups=x.shape[1])[:, :, :T]).transpose(1, 2)
+    query, key, value = torch.split(x, [key_dim, key_dim, value_dim], dim=-1)
+    q = F.normalize(query.reshape(B, T, H, dk).float(), dim=-1, eps=1e-6)
+    k = F.normalize(key.reshape(B, T, H, dk).float(), dim=-1, eps=1e-6)
+    v = value.reshape(B, T, H, dv).float()
+    q = q * (dk ** -0.5)
+    b = b.float()
+    a = a.float()
+    beta_e = torch.sigmoid(b)
+    beta_w = torch.sigmoid(b + bw_off)
+    g_head = -A_log.float().exp() * F.softplus(a + dt_bias.float())
+    g = (g_head.unsqueeze(-1) + decay_chan).exp()
+    g = g.clamp(max=1.0)
+    th = F.softplus(theta).view(B, T, H, dk // 2).float()
+    Th = th.cumsum(dim=1)
+    cos, sin = Th.cos(), Th.sin()
+
+    def rope(zz, c, s):
+        z1, z2 = zz[..., :dk // 2], zz[..., dk // 2:]
+        return torch.cat([z1 * c - z2 * s, z1 * s + z2 * c], dim=-1)
+    k = rope(k, cos, sin)
+    qs = q.unsqueeze(3) * (1.0 + q_slot_scale)[None, None] if r_out > 1 else q.unsqueeze(3)
+    qs = rope(qs, cos.unsqueeze(-2), sin.unsqueeze(-2))
+    return qs, k, v, g, beta_e, beta_w

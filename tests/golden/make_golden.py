@@ -25,6 +25,10 @@ seeded inputs, what they return:
   config-2 inputs, T = 1024: four compactions) -- every 8th token and the last
   one, plus the relative L2 distance of the
   reference's own chunked ``_gdn3_recurrent_state`` from it (its floor).
+* ``kmd2_prologue.pt`` -- ``KMD2NativeAttn.forward`` (random parameters, r_out 4 and 1) with its
+  ``_scan`` replaced by a recorder: the GEMM outputs it starts from and the ``_scan`` arguments
+  the reference hands over (conv + SiLU, normalisation, gates, decays, cumulative rotation); and
+  the whole forward's output with the reference's own scan, with the parameters and input.
 * ``epilogue.pt``      -- the GDN3 output epilogue (``forward`` lines 842-856 restated
   by calling the same torch ops on a module's ``norm`` parameter, set to random
   values) and ``Qwen3_5RMSNormGated`` from transformers on random inputs.
@@ -183,6 +187,52 @@ def make_compaction_sketch():
     torch.save(dict(inputs=[A, Bk, U, Vb], slow_decay=L.slow_decay, **out), HERE / 'compaction_sketch.pt')
 
 
+def make_kmd2_prologue():
+    import importlib
+    out = {}
+    for r_out in (4, 1):
+        os.environ['GDN3_KMD2_ROUT'] = str(r_out)
+        import gdn3.kmd2_native as KN
+        importlib.reload(KN)
+        cfg = types.SimpleNamespace(hidden_size=32, linear_num_value_heads=2, linear_key_head_dim=128,
+                                    linear_value_head_dim=128, linear_num_key_heads=2, linear_conv_kernel_dim=4,
+                                    rms_norm_eps=1e-6)
+        L = KN.KMD2NativeAttn(cfg)
+        g = torch.Generator().manual_seed(20 + r_out)
+        with torch.no_grad():
+            for name, prm in L.named_parameters():
+                scale = {'rot_proj.bias': 0.5, 'A_log': 0.5, 'dt_bias': 1.0, 'decay_chan': 0.3, 'bw_off': 1.0,
+                         'q_slot_scale': 0.2, 'conv1d.weight': 0.4}.get(name, 0.15)
+                prm.copy_(torch.randn(prm.shape, generator=g) * scale)
+            L.rot_proj.bias.sub_(1.0)  # softplus about 0.3 rad per token: the rotation turns visibly
+        rec = {}
+
+        def recorder(q, k, v, gd, be, bw):
+            rec.update(q=q.detach().clone(), k=k.detach().clone(), v=v.detach().clone(), g=gd.detach().clone(),
+                       beta_e=be.detach().clone(), beta_w=bw.detach().clone())
+            return torch.zeros(k.shape[0], k.shape[1], k.shape[2], v.shape[-1])
+
+        L._scan = recorder
+        x = torch.randn(2, 24, 32, generator=g)
+        with torch.no_grad():
+            L(x)
+            gemm = dict(mixed=L.in_proj_qkv(x), b=L.in_proj_b(x), a=L.in_proj_a(x), theta=L.rot_proj(x))
+        prm = dict(conv_w=L.conv1d.weight.detach().clone(), dt_bias=L.dt_bias.detach().clone(),
+                   A_log=L.A_log.detach().clone(), decay_chan=L.decay_chan.detach().clone(),
+                   bw_off=L.bw_off.detach().clone(),
+                   q_slot_scale=L.q_slot_scale.detach().clone() if r_out > 1 else None)
+        # the whole forward with the reference's own token-loop scan, for the fused-forward drop-in
+        L2 = KN.KMD2NativeAttn(cfg)
+        L2.load_state_dict(L.state_dict())
+        with torch.no_grad():
+            y_fwd = L2(x)
+        out[f'r{r_out}'] = dict(H=2, r_out=r_out, gemm=gemm, params=prm, scan_args=rec, x=x,
+                                state_dict={k_: v_.detach().clone() for k_, v_ in L2.state_dict().items()},
+                                forward=y_fwd, eps=cfg.rms_norm_eps)
+    os.environ.pop('GDN3_KMD2_ROUT', None)
+    torch.save(out, HERE / 'kmd2_prologue.pt')
+
+
 def make_epilogue():
     import torch.nn.functional as F
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5RMSNormGated
@@ -274,7 +324,8 @@ if __name__ == '__main__':
     torch.manual_seed(0)
     makers = dict(gdn3_frozen=make_gdn3_frozen, gdn3_config0=make_gdn3_config0, kmd2=make_kmd2,
                   compaction=make_compaction, compaction_sketch=make_compaction_sketch, prologue=make_prologue, gdn3_kr_p256=make_kr_p256,
-                  epilogue=make_epilogue, proj_prologue=make_projection_prologue)
+                  epilogue=make_epilogue, proj_prologue=make_projection_prologue,
+                  kmd2_prologue=make_kmd2_prologue)
     only = sys.argv[2:]  # optional fixture names; default: all
     for name, fn in makers.items():
         if not only or name in only:

@@ -36,7 +36,8 @@ def test_library_loads_and_exports_every_declared_symbol():
 STRUCTS = {"gdnx_view": L.View, "gdnx_rope": L.Rope, "gdnx_scan_args": L.ScanArgs,
            "gdnx_kr_scan_args": L.KrScanArgs, "gdnx_compact_args": L.CompactArgs,
            "gdnx_decode_args": L.DecodeArgs, "gdnx_epilogue_args": L.EpilogueArgs,
-           "gdnx_prologue_args": L.PrologueArgs, "gdnx_scan_bwd_args": L.ScanBwdArgs}
+           "gdnx_prologue_args": L.PrologueArgs, "gdnx_scan_bwd_args": L.ScanBwdArgs,
+           "gdnx_kmd2_prologue_args": L.Kmd2PrologueArgs}
 
 
 def test_ctypes_layout_matches_c(tmp_path):

@@ -143,3 +143,14 @@ def test_projection_prologue_matches_reference():
                                                  w_proj=c["w_proj"], proj_b=c["proj_b"])
     for a, b in ((q, c["q"]), (k, c["k"]), (v, c["v"]), (bg, c["b_gates"]), (wg, c["w_gates"])):
         torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("case", ["r4", "r1"])
+def test_kmd2_prologue_bit_exact(case):
+    """The KMD-2 prologue restatement equals the arguments the reference's forward hands its _scan."""
+    c = _load("kmd2_prologue.pt")[case]
+    gm, pr, sa = c["gemm"], c["params"], c["scan_args"]
+    out = PR.kmd2_prologue(gm["mixed"], pr["conv_w"], gm["b"], gm["a"], gm["theta"], pr["dt_bias"], pr["A_log"],
+                           pr["decay_chan"], pr["bw_off"], pr["q_slot_scale"], H=c["H"], r_out=c["r_out"])
+    for o, n in zip(out, ["q", "k", "v", "g", "beta_e", "beta_w"]):
+        assert torch.equal(o, sa[n]), n
