@@ -641,7 +641,15 @@ __device__ unsigned long long g_wy_probe[16];
       pmark = n_;                                                                     \
     }                                                                                 \
   } while (0)
+#define WY_ISSUE_BEGIN() const long long iss0_ = clock64()
+#define WY_ISSUE_END(slot) probe_acc[slot] += (unsigned long long)(clock64() - iss0_)
 #else
+#define WY_ISSUE_BEGIN() \
+  do {                   \
+  } while (0)
+#define WY_ISSUE_END(slot) \
+  do {                     \
+  } while (0)
 #define WY_TIMED(slot, cond, expr) (expr)
 #define WY_MARK(slot) \
   do {                \
@@ -659,13 +667,13 @@ constexpr int G_NT = 256;  // threads per group
 // descriptor with LBO = the block stride.
 constexpr int KB = 24576;                        // K-block stride of a q/k tile
 constexpr int S_OFF_MQ0 = 0;                     // Mq^T stage 0 [64 j][64 i]
-constexpr int S_OFF_WT = 8192;                   // W^T [128 v][64 j]
+constexpr int S_OFF_WT = 8192;                   // (unused: W^T is an A operand in TMEM)
 constexpr int S_OFF_KQ0 = S_OFF_MQ0 + KB;        // stage 0 tile (2 blocks)
 constexpr int S_OFF_KQ1 = S_OFF_KQ0 + 2 * KB;    // stage 1 tile
 constexpr int S_OFF_MQ1 = S_OFF_KQ1 + 2 * KB;    // Mq^T stage 1
 constexpr int S_OFF_V = S_OFF_MQ1 + 8192;        // 2 stages x [2 vb][64 tokens][128 B]
 constexpr int S_OFF_TT = S_OFF_V + 2 * 16384;    // 2 stages x (T_e 8 KB | T_w 8 KB)
-constexpr int S_OFF_SB = S_OFF_TT + 2 * 16384;   // bf16 state [2 kb][128 v][128 B]
+constexpr int S_OFF_SB = S_OFF_TT + 2 * 16384;   // (unused: the bf16 state is in TMEM)
 constexpr int S_OFF_L = S_OFF_SB + 32768;        // 2 stages x L[64]
 constexpr int S_OFF_PSC = S_OFF_L + 512;         // 2 x 2^L, 2 x K' factor: 4 x 64 fp32
 constexpr int S_OFF_SF = S_OFF_PSC + 1024;       // 2 x {2^ls, rescale factor, rescale flag, -}
@@ -677,11 +685,14 @@ static_assert(S_OFF_KQ0 - KB == S_OFF_MQ0, "stage-0 Mq^T position");
 static_assert(S_SMEM <= 232448, "shared memory");
 constexpr uint32_t STAGE_TX = 6 * 8192 + 3 * 8192 + 256;
 
-// TMEM columns: W^T0 | y0 | state (128) | y1 | W^T1 | Wk (64), so that G2 writes
-// [W^T0 | y0] / [y1 | W^T1] and G3 writes [y0 | S] / [S | y1] with one MMA each.  Wk
+// TMEM columns: W^T0 | y0 | state (128) | y1 | W^T1 | Wk (64) | S bf16 (64), so that G2
+// writes [W^T0 | y0] / [y1 | W^T1] and G3 writes [y0 | S] / [S | y1] with one MMA each.  Wk
 // [64 j][128 k] is two M = 64 accumulators: k block kb in lanes 32 q + 16 kb + (j % 16)
 // of quadrant q = j / 16 (the M = 64 layout, the second block at lane offset 16).
-constexpr uint32_t T_W0 = 0, T_Y0 = 64, T_S = 128, T_Y1 = 256, T_W1 = 320, T_WK = 384;
+// The A operands of G2 (S0) and G3 (W^T) are read from TMEM: S0 packed as bf16 pairs in
+// the last 64 columns, W^T packed in place over its fp32 accumulator (tokens 32 h .. 32 h
+// + 31 in columns 32 h .. 32 h + 15 of the buffer), so neither goes through shared memory.
+constexpr uint32_t T_W0 = 0, T_Y0 = 64, T_S = 128, T_Y1 = 256, T_W1 = 320, T_WK = 384, T_SB = 448;
 
 // 16 TMEM lanes x 32 consecutive 32-bit columns in the 16x256b fragment layout:
 // for each 8-column group p, registers 4p..4p+3 hold (lane g, column 2(t%4)),
@@ -783,8 +794,7 @@ __global__ void __launch_bounds__(S_NT, 1)
   const float rsc = dpairs > 0 ? a.rope.scale[lm] : 0.f;
   const int64_t nchunks = P.nchunks;
   const uint32_t sbase = tc::smem_u32(sm);
-  const uint32_t sV = sbase + S_OFF_V, sTT = sbase + S_OFF_TT, sSB = sbase + S_OFF_SB;
-  const uint32_t sWT = sbase + S_OFF_WT, sLst = sbase + S_OFF_L;
+  const uint32_t sV = sbase + S_OFF_V, sTT = sbase + S_OFF_TT, sLst = sbase + S_OFF_L;
   const __nv_bfloat16* ttg = P.tt + n * nchunks * TT_ELEMS;
   const float* lsg = P.lsum + n * nchunks * C;
   // per-stage geometry (rows within a 192-row K block)
@@ -876,14 +886,12 @@ __global__ void __launch_bounds__(S_NT, 1)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int col = 64 * half + 32 * hh;
-          float vals[32], o[8];
+          float vals[32];
+          uint32_t pk[16];
           tc::tmem_ld32(tmem + T_S + lbase + col, vals);
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = vals[8 * q4 + e] * sf.x;
-            tc::st_chunk_bf16(reinterpret_cast<char*>(sm + S_OFF_SB), tc::sw128(row, col / 8 + q4, 128), o);
-          }
+          for (int e = 0; e < 16; ++e) pk[e] = tc::pack_bf16(vals[2 * e] * sf.x, vals[2 * e + 1] * sf.x);
+          tc::tmem_st16u(tmem + T_SB + lbase + col / 2, pk);
           if (sf.z != 0.f) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) vals[e] *= sf.y;
@@ -891,7 +899,6 @@ __global__ void __launch_bounds__(S_NT, 1)
           }
         }
       }
-      tc::fence_async_smem();
       tc::fence_before();
       if (group_any(2, *s_abort != 0)) break;
       WY_MARK(8);  // conversion
@@ -900,13 +907,14 @@ __global__ void __launch_bounds__(S_NT, 1)
       if (tid == 0) {
         tc::fence_after();
         const uint32_t d = tmem + (s ? T_Y1 : T_W0);
+        WY_ISSUE_BEGIN();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t ko = (k >> 2) * KB + (k & 3) * 32;
-          tc::mma_bf16(d, tc::smem_desc(sSB + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
-                       tc::smem_desc(kq + ko + 64 * 128, 16, 1024), ID_G2, 1);
+          tc::mma_bf16_ts(d, tmem + T_SB + 8 * k, tc::smem_desc(kq + ko + 64 * 128, 16, 1024), ID_G2, 1);
         }
         tc::commit(g2);
+        WY_ISSUE_END(13);
       }
       ok = WY_TIMED(1, tid == 0, wait_or_abort(g2, (uint32_t)(ch & 1), s_abort));
       tc::fence_after();
@@ -927,11 +935,12 @@ __global__ void __launch_bounds__(S_NT, 1)
             w[4 * e + 3] *= f.w;
           }
         }
-        char* wt = reinterpret_cast<char*>(sm + S_OFF_WT);
+        // packed in place: tokens 32 half + 2e, +1 in column 32 half + e of the W^T buffer
+        uint32_t pk[16];
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(wt, tc::sw128(row, 4 * half + q4, 128), w + 8 * q4);
+        for (int e = 0; e < 16; ++e) pk[e] = tc::pack_bf16(w[2 * e], w[2 * e + 1]);
+        tc::tmem_st16u(tmem + (s ? T_W1 : T_W0) + lbase + 32 * half, pk);
       }
-      tc::fence_async_smem();
       tc::fence_before();
       if (group_any(2, *s_abort != 0)) break;
       WY_MARK(10);  // W read-out
@@ -940,11 +949,14 @@ __global__ void __launch_bounds__(S_NT, 1)
       if (tid == 0) {
         tc::fence_after();
         const uint32_t d = tmem + (s ? T_S : T_Y0);
+        WY_ISSUE_BEGIN();
         const uint32_t bb = s ? kq : sbase + S_OFF_MQ0;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc::mma_bf16(d, tc::smem_desc(sWT + k * 32, 16, 1024), tc::smem_desc(bb + k * 2048, KB, 1024), ID_G3, 1);
+          tc::mma_bf16_ts(d, tmem + (s ? T_W1 : T_W0) + 32 * (k >> 1) + 8 * (k & 1),
+                          tc::smem_desc(bb + k * 2048, KB, 1024), ID_G3, 1);
         tc::commit(g3 + s);
+        WY_ISSUE_END(14);
       }
       ok = WY_TIMED(2, tid == 0, wait_or_abort(g3 + s, (uint32_t)((ch >> 1) & 1), s_abort));
       tc::fence_after();
