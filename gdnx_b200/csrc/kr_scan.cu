@@ -33,7 +33,7 @@ namespace gdnx {
 namespace {
 
 constexpr int kNT = kCompThreads;  // 256
-constexpr int kTB = 8;             // tokens staged per block (<= P handled by the block split)
+constexpr int kTB = 16;            // tokens staged per block (<= P handled by the block split)
 constexpr int kMaxP = 1024;
 
 struct KrParams {
