@@ -667,7 +667,7 @@ constexpr int G_NT = 256;  // threads per group
 // descriptor with LBO = the block stride.
 constexpr int KB = 24576;                        // K-block stride of a q/k tile
 constexpr int S_OFF_MQ0 = 0;                     // Mq^T stage 0 [64 j][64 i]
-constexpr int S_OFF_WT = 8192;                   // (unused: W^T is an A operand in TMEM)
+// (bytes 8192 .. KB - 1 are free: W^T is an A operand in TMEM)
 constexpr int S_OFF_KQ0 = S_OFF_MQ0 + KB;        // stage 0 tile (2 blocks)
 constexpr int S_OFF_KQ1 = S_OFF_KQ0 + 2 * KB;    // stage 1 tile
 constexpr int S_OFF_MQ1 = S_OFF_KQ1 + 2 * KB;    // Mq^T stage 1
