@@ -1,10 +1,13 @@
 // Memory-bound single-token decode step for K = V = 128 dense states.
 //
-// Persistent CTAs (one per SM, 8 warps) stream their chains' 64 KB fp32
-// states through three shared-memory stages with bulk asynchronous copies
-// (cp.async.bulk, completion counted on an mbarrier): the state of chain j+2
-// is in flight while chain j is updated in place in shared memory, and chain
-// j's updated state drains back to HBM with a bulk store.  The per-chain
+// Persistent CTAs (one per SM, 8 update warps + 1 copy warp) stream their
+// chains' 64 KB fp32 states through three shared-memory stages with bulk
+// asynchronous copies (cp.async.bulk, completion counted on an mbarrier): the
+// state of chain j+2 is in flight while chain j is updated in place in shared
+// memory, and chain j's updated state drains back to HBM with a bulk store.
+// The copy warp issues every load and store and waits for a stage's store to
+// have read it before refilling it; the update warps signal "stage updated" on
+// a second mbarrier and never wait for a store themselves.  The per-chain
 // vectors (q, k, v, gates, decay) of chain j+1 are loaded as raw bits into
 // registers before chain j's math and converted after it, so no dependent
 // global-memory latency sits on the per-chain path.  The lane-RoPE cos/sin
@@ -68,6 +71,9 @@ GDNX_DEV void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
 GDNX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 GDNX_DEV void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 GDNX_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+GDNX_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
+}
 GDNX_DEV void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(mbar), "r"(bytes) : "memory");
 }
@@ -195,14 +201,18 @@ GDNX_DEV void finish_chain(const DecParams& P, int64_t n, int lane, const ChainR
   }
 }
 
-__global__ void __launch_bounds__(256, 1) decode128_kernel(const DecParams P) {
+constexpr int kThreads = (kWarps + 1) * 32;  // eight update warps and one copy warp
+
+__global__ void __launch_bounds__(kThreads, 1) decode128_kernel(const DecParams P) {
   extern __shared__ uint8_t smraw[];
   uint8_t* sm = tc::align_smem(smraw, 128);
   float* stage_f = reinterpret_cast<float*>(sm);                       // kStages x 128 x 128
   float* vecs = reinterpret_cast<float*>(sm + kStages * kStateBytes);  // kWarps x 2 x 128
   float* ropeC = vecs + kWarps * 2 * K;                                // [4 lanes][64 pairs]
   float* ropeS = ropeC + 4 * 64;
-  uint64_t* full = reinterpret_cast<uint64_t*>(ropeS + 4 * 64);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ropeS + 4 * 64);  // [kStages] state loaded
+  uint64_t* done = full + kStages;                                 // [kStages] state updated in place
+  volatile int* s_abort = reinterpret_cast<volatile int*>(done + kStages);
 
   const gdnx_decode_args& a = P.a;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -212,7 +222,11 @@ __global__ void __launch_bounds__(256, 1) decode128_kernel(const DecParams P) {
   float* sq = sk + K;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) tc::mbar_init(&full[s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&done[s], kWarps);
+    }
+    *s_abort = 0;
   }
   if (a.rope.enable) {
     for (int idx = threadIdx.x; idx < 4 * 64; idx += blockDim.x) {
@@ -233,81 +247,87 @@ __global__ void __launch_bounds__(256, 1) decode128_kernel(const DecParams P) {
 #pragma unroll
     for (int p = 0; p < kStateBytes / kPiece; ++p) bulk_load(dst + p * kPiece, src + p * kPiece, kPiece, mb);
   };
-  if (threadIdx.x == 0) {
-    for (int64_t j = 0; j < nmine && j < kStages - 1; ++j) issue_load(j);
-  }
-
-  ChainRaw raw;
-  ChainVals cur;
-  if (nmine > 0) {
-    load_raw(P, chain_of(0), warp, lane, raw);
-    finish_chain(P, chain_of(0), lane, raw, sk, sq, ropeC, ropeS, cur);
-  }
-  bool ok = true;
-  int64_t consumed = 0;  // chains whose state load has been waited for
-  const int row0 = warp * kRowsPerWarp;
-  for (int64_t j = 0; j < nmine; ++j) {
-    const int64_t n = chain_of(j);
-    int64_t b, h, m;
-    chain_index(a, n, b, h, m);
-    const int s = (int)(j % kStages);
-    ok = tc::mbar_wait(&full[s], (uint32_t)((j / kStages) & 1), kWaitLimit);
-    if (__syncthreads_or(!ok)) break;
-    consumed = j + 1;
-    // next chain's vectors: raw loads now, consumed after this chain's math
-    if (j + 1 < nmine) load_raw(P, chain_of(j + 1), warp, lane, raw);
-
-    float* Sst = stage_f + (size_t)s * V * K + row0 * K + 4 * lane;
-    float4 S[kRowsPerWarp];
-    float vals[32];
-#pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r) {
-      float4 x = *reinterpret_cast<const float4*>(Sst + r * K);
-      if (P.chan_decay) {
-        x.x *= cur.g4.x; x.y *= cur.g4.y; x.z *= cur.g4.z; x.w *= cur.g4.w;
+  if (warp == kWarps) {
+    // ---- copy warp: loads two states ahead, stores each updated state, refills its stage ----
+    if (lane == 0) {
+      for (int64_t j = 0; j < nmine && j < kStages - 1; ++j) issue_load(j);
+      int64_t j = 0;
+      for (; j < nmine; ++j) {
+        const int s = (int)(j % kStages);
+        if (!tc::mbar_wait(&done[s], (uint32_t)((j / kStages) & 1), kWaitLimit) || *s_abort) {
+          *s_abort = 1;
+          break;
+        }
+        bulk_store(a.S + chain_of(j) * (int64_t)V * K, tc::smem_u32(stage_f + (size_t)s * V * K), kStateBytes);
+        bulk_commit();
+        // the stage of chain j-1 is free once its store has read shared memory
+        if (j + kStages - 1 < nmine) {
+          bulk_wait_read_le1();
+          issue_load(j + kStages - 1);
+        }
       }
-      S[r] = x;
-      vals[r] = x.x * cur.h4.x + x.y * cur.h4.y + x.z * cur.h4.z + x.w * cur.h4.w;
-      vals[r + 16] = x.x * cur.q4.x + x.y * cur.q4.y + x.z * cur.q4.z + x.w * cur.q4.w;
-    }
-    const float tot = transpose_reduce32(vals, lane);
-    // lane l < 16: tot = (S h)_row(l); lane l >= 16: tot = (S q)_row(l-16)
-    const float d_own = cur.cw * cur.u - cur.ce * (cur.gam * tot);
-    const float d_row = __shfl_sync(0xffffffffu, d_own, lane & 15);
-    if (lane >= 16) {
-      const float y = fmaf(d_row, cur.kq, cur.gam * tot);
-      st_from_f32(a.y, a.y_dtype, b * a.y_sb + h * a.y_sh + m * a.y_sm + row0 + (lane - 16), y);
-    }
-#pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r) {
-      const float d = __shfl_sync(0xffffffffu, d_own, r);
-      float4 x = S[r];
-      x.x = fmaf(cur.gam, x.x, d * cur.k4.x);
-      x.y = fmaf(cur.gam, x.y, d * cur.k4.y);
-      x.z = fmaf(cur.gam, x.z, d * cur.k4.z);
-      x.w = fmaf(cur.gam, x.w, d * cur.k4.w);
-      *reinterpret_cast<float4*>(Sst + r * K) = x;
-    }
-    tc::fence_async_smem();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      bulk_store(a.S + n * (int64_t)V * K, tc::smem_u32(stage_f + (size_t)s * V * K), kStateBytes);
-      bulk_commit();
-      // the stage of chain j-1 is free once its store has read shared memory
-      if (j + kStages - 1 < nmine) {
-        bulk_wait_read_le1();
-        issue_load(j + kStages - 1);
+      bulk_wait_all();
+      if (j < nmine) {
+        // gave up: drain the loads still in flight (bounded) before exiting
+        const int64_t issued = nmine < j + kStages - 1 ? nmine : j + kStages - 1;
+        for (int64_t jj = j; jj < issued; ++jj)
+          tc::mbar_wait(&full[jj % kStages], (uint32_t)((jj / kStages) & 1), kWaitLimit);
       }
     }
-    if (j + 1 < nmine) finish_chain(P, chain_of(j + 1), lane, raw, sk, sq, ropeC, ropeS, cur);
-  }
-  if (threadIdx.x == 0) {
-    bulk_wait_all();
-    if (!ok) {
-      // a wait gave up: drain this CTA's loads still in flight (bounded) before exiting
-      const int64_t issued = nmine < consumed + kStages - 1 ? nmine : consumed + kStages - 1;
-      for (int64_t j = consumed; j < issued; ++j)
-        tc::mbar_wait(&full[j % kStages], (uint32_t)((j / kStages) & 1), kWaitLimit);
+  } else {
+    // ---- update warps: each owns 16 rows of every state ----
+    ChainRaw raw;
+    ChainVals cur;
+    if (nmine > 0) {
+      load_raw(P, chain_of(0), warp, lane, raw);
+      finish_chain(P, chain_of(0), lane, raw, sk, sq, ropeC, ropeS, cur);
+    }
+    const int row0 = warp * kRowsPerWarp;
+    for (int64_t j = 0; j < nmine; ++j) {
+      const int64_t n = chain_of(j);
+      int64_t b, h, m;
+      chain_index(a, n, b, h, m);
+      const int s = (int)(j % kStages);
+      if (!tc::mbar_wait(&full[s], (uint32_t)((j / kStages) & 1), kWaitLimit)) *s_abort = 1;
+      if (*s_abort) break;
+      // next chain's vectors: raw loads now, consumed after this chain's math
+      if (j + 1 < nmine) load_raw(P, chain_of(j + 1), warp, lane, raw);
+
+      float* Sst = stage_f + (size_t)s * V * K + row0 * K + 4 * lane;
+      float4 S[kRowsPerWarp];
+      float vals[32];
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) {
+        float4 x = *reinterpret_cast<const float4*>(Sst + r * K);
+        if (P.chan_decay) {
+          x.x *= cur.g4.x; x.y *= cur.g4.y; x.z *= cur.g4.z; x.w *= cur.g4.w;
+        }
+        S[r] = x;
+        vals[r] = x.x * cur.h4.x + x.y * cur.h4.y + x.z * cur.h4.z + x.w * cur.h4.w;
+        vals[r + 16] = x.x * cur.q4.x + x.y * cur.q4.y + x.z * cur.q4.z + x.w * cur.q4.w;
+      }
+      const float tot = transpose_reduce32(vals, lane);
+      // lane l < 16: tot = (S h)_row(l); lane l >= 16: tot = (S q)_row(l-16)
+      const float d_own = cur.cw * cur.u - cur.ce * (cur.gam * tot);
+      const float d_row = __shfl_sync(0xffffffffu, d_own, lane & 15);
+      if (lane >= 16) {
+        const float y = fmaf(d_row, cur.kq, cur.gam * tot);
+        st_from_f32(a.y, a.y_dtype, b * a.y_sb + h * a.y_sh + m * a.y_sm + row0 + (lane - 16), y);
+      }
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) {
+        const float d = __shfl_sync(0xffffffffu, d_own, r);
+        float4 x = S[r];
+        x.x = fmaf(cur.gam, x.x, d * cur.k4.x);
+        x.y = fmaf(cur.gam, x.y, d * cur.k4.y);
+        x.z = fmaf(cur.gam, x.z, d * cur.k4.z);
+        x.w = fmaf(cur.gam, x.w, d * cur.k4.w);
+        *reinterpret_cast<float4*>(Sst + r * K) = x;
+      }
+      tc::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&done[s]);  // this warp's rows are written back (the copy warp stores them)
+      if (j + 1 < nmine) finish_chain(P, chain_of(j + 1), lane, raw, sk, sq, ropeC, ropeS, cur);
     }
   }
   __syncthreads();
@@ -329,11 +349,11 @@ gdnx_status launch_decode_128(const gdnx_decode_args& a, cudaStream_t st) {
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return GDNX_ELAUNCH;
-  const size_t smem = (size_t)kStages * kStateBytes + kWarps * 2 * K * 4 + 2 * 4 * 64 * 4 + kStages * 8 + 128;
+  const size_t smem = (size_t)kStages * kStateBytes + kWarps * 2 * K * 4 + 2 * 4 * 64 * 4 + 2 * kStages * 8 + 16 + 128;
   if (cudaFuncSetAttribute(decode128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return GDNX_ELAUNCH;
   const int64_t grid = P.N < sms ? P.N : sms;
-  decode128_kernel<<<(unsigned)grid, 256, smem, st>>>(P);
+  decode128_kernel<<<(unsigned)grid, kThreads, smem, st>>>(P);
   return cudaGetLastError() == cudaSuccess ? GDNX_OK : GDNX_ELAUNCH;
 }
 
