@@ -277,6 +277,54 @@ __global__ void __launch_bounds__(P_NT, 2) wyg_prep_kernel(const GenParams P) {
   __syncthreads();
 
   // ---- 2. token rows: loads, lane RoPE, gates, operands ----
+  // A warp's next token is fetched with cp.async into its staging slot (over the K^(J)
+  // buffers, free until section 3) while the current one is processed: rows of q (each
+  // query slot), k, v and the vector gates, this lane's 4 elements of each.
+  constexpr int kStgRows = 6, kStgBytes = kStgRows * 128 * 4;
+  const bool stage = a.r_out <= 4 && a.r_out + 2 + P.vec_e + P.vec_w <= kStgRows;
+  char* stg = reinterpret_cast<char*>(sm + P_OFF_KB) + warp * kStgBytes;
+  const int nq = a.r_out > 1 ? a.r_out : 1;
+  auto es_of = [](int dt) { return dt == GDNX_F32 ? 4 : 2; };
+  auto cp_row = [&](int row, const gdnx_view& v, int64_t off) {  // this lane's 4 elements
+    const int es = es_of(v.dtype);
+    const char* src = reinterpret_cast<const char*>(v.ptr) + (off + 4 * lane) * es;
+    const uint32_t dst = tc::smem_u32(stg + row * 512 + 16 * lane);
+    if (es == 4)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    else
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+  };
+  auto rd_row = [&](int row, int dt, float* x) {  // this lane's 4 staged elements as fp32
+    const char* p = stg + row * 512 + 16 * lane;
+    if (dt == GDNX_F32) {
+      to4(*reinterpret_cast<const float4*>(p), x);
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2*>(p);
+      if (dt == GDNX_BF16) {
+        x[0] = __uint_as_float(u.x << 16); x[1] = __uint_as_float(u.x & 0xffff0000u);
+        x[2] = __uint_as_float(u.y << 16); x[3] = __uint_as_float(u.y & 0xffff0000u);
+      } else {
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        x[0] = lo.x; x[1] = lo.y; x[2] = hi.x; x[3] = hi.y;
+      }
+    }
+  };
+  float nbe = 0.f, nbw = 0.f;  // scalar gates of the staged token
+  auto issue = [&](int jj) {
+    const int64_t t = t0 + 8 * warp + jj;
+    if (t >= a.T) return;
+    for (int r = 0; r < nq; ++r)
+      cp_row(r, a.q, a.r_out <= 1 ? view_off(a.q, b, t, h, m) : view_off(a.q, b, t, h, m, r));
+    cp_row(nq, a.k, view_off(a.k, b, t, h, m));
+    cp_row(nq + 1, a.v, view_off(a.v, b, t, h, m));
+    if (P.vec_e) cp_row(nq + 2, a.gate_e, view_off(a.gate_e, b, t, h, m));
+    else nbe = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m));
+    if (P.vec_w) cp_row(nq + 2 + P.vec_e, a.gate_w, view_off(a.gate_w, b, t, h, m));
+    else nbw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m));
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (stage) issue(0);
   float kreg[8][4];
   {
     const bool role1 = lane < dp4, role2 = lane >= dp4 && lane < 2 * dp4;
@@ -290,7 +338,31 @@ __global__ void __launch_bounds__(P_NT, 2) wyg_prep_kernel(const GenParams P) {
       const bool valid = t < a.T;
       float q[4] = {0.f, 0.f, 0.f, 0.f}, k[4] = {0.f, 0.f, 0.f, 0.f}, hv[4], u[4] = {0.f, 0.f, 0.f, 0.f};
       float ce = 0.f, cw = 0.f;
-      if (valid) {
+      float sge[4] = {0.f, 0.f, 0.f, 0.f}, sgw[4] = {0.f, 0.f, 0.f, 0.f}, sbe = 0.f, sbw = 0.f;
+      if (stage) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        if (valid) {
+          if (a.r_out <= 1) {
+            rd_row(0, a.q.dtype, q);
+          } else {
+            for (int r = 0; r < a.r_out; ++r) {
+              float qr[4];
+              rd_row(r, a.q.dtype, qr);
+              const float mix = a.out_mix[h * a.r_out + r];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) q[e] = fmaf(mix, qr[e], q[e]);
+            }
+          }
+          rd_row(nq, a.k.dtype, k);
+          rd_row(nq + 1, a.v.dtype, u);
+          if (P.vec_e) rd_row(nq + 2, a.gate_e.dtype, sge);
+          if (P.vec_w) rd_row(nq + 2 + P.vec_e, a.gate_w.dtype, sgw);
+          sbe = nbe;
+          sbw = nbw;
+        }
+        __syncwarp();
+        if (jj + 1 < 8) issue(jj + 1);
+      } else if (valid) {
         if (a.r_out <= 1) {
           to4(ld4(a.q.ptr, a.q.dtype, view_off(a.q, b, t, h, m) + 4 * lane), q);
         } else {
@@ -333,21 +405,31 @@ __global__ void __launch_bounds__(P_NT, 2) wyg_prep_kernel(const GenParams P) {
       if (valid) {
         if (P.vec_e) {
           float g4[4];
-          to4(ld4(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m) + 4 * lane), g4);
+          if (stage) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) g4[e] = sge[e];
+          } else {
+            to4(ld4(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m) + 4 * lane), g4);
+          }
 #pragma unroll
           for (int e = 0; e < 4; ++e) hv[e] = g4[e] * k[e];
         } else {
-          be = ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m));
+          be = stage ? sbe : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m));
 #pragma unroll
           for (int e = 0; e < 4; ++e) hv[e] = kmd2 ? k[e] : be * k[e];
         }
         if (P.vec_w) {
           float w4[4];
-          to4(ld4(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m) + 4 * lane), w4);
+          if (stage) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) w4[e] = sgw[e];
+          } else {
+            to4(ld4(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m) + 4 * lane), w4);
+          }
 #pragma unroll
           for (int e = 0; e < 4; ++e) u[e] *= w4[e];
         } else {
-          bw = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m));
+          bw = stage ? sbw : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m));
           if (!kmd2)
 #pragma unroll
             for (int e = 0; e < 4; ++e) u[e] *= bw;
