@@ -230,13 +230,22 @@ __global__ void __launch_bounds__(P_NT, 2) wyg_prep_kernel(const GenParams P) {
       const int64_t t = t0 + 8 * warp + lane;
       if (t < a.T) sl = scalar_log2_decay(a, kmd2, view_off(a.decay, b, t, h, m));
     }
+    float4 graw[8];  // per-channel decays of the warp's 8 tokens, all loads issued first
+    if (P.chan_decay) {
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int64_t t = t0 + 8 * warp + jj;
+        graw[jj] = t < a.T ? ld4(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m) + 4 * lane)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) {
       const int64_t t = t0 + 8 * warp + jj;
       float l4[4];
       if (P.chan_decay) {
         if (t < a.T) {
-          to4(ld4(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m) + 4 * lane), l4);
+          to4(graw[jj], l4);
 #pragma unroll
           for (int e = 0; e < 4; ++e) l4[e] = chan_log2_decay(l4[e], a.decay_kind, kmd2);
         } else {
