@@ -697,8 +697,9 @@ constexpr int S_OFF_BAR = S_OFF_KN + 1024;
 constexpr int S_SMEM = S_OFF_BAR + 128 + 1024;
 static_assert(S_SMEM <= 232448, "shared memory");
 static_assert(ST_GC + 1024 == ST_BYTES, "stage layout");
-// TMEM columns: S | W^T(0) | y(0) | W^T(1) | y(1)
-constexpr uint32_t T_S = 0;
+// TMEM columns: S | W^T(0) | y(0) | W^T(1) | y(1) | S bf16 (64) | W^T bf16 (32).  The A operands of
+// G2 (S0) and G3 (W^T) are read from TMEM as packed bf16 pairs; the fp32 W^T stays for the scores.
+constexpr uint32_t T_S = 0, T_SB = 384, T_WB = 448;
 GDNX_DEV uint32_t t_w(int s) { return 128u + 128u * (uint32_t)s; }
 GDNX_DEV uint32_t t_y(int s) { return 192u + 128u * (uint32_t)s; }
 
@@ -789,7 +790,7 @@ __global__ void __launch_bounds__(S_NT, 1) wyg_chain_kernel(const GenParams P) {
   constexpr uint32_t ID_N64 = tc::idesc_bf16(128, 64, false, false);
   constexpr uint32_t ID_Y3 = tc::idesc_bf16(128, 64, false, true);
   constexpr uint32_t ID_S3 = tc::idesc_bf16(128, 128, false, true);
-  const uint32_t sSB = sbase + S_OFF_SB, sWT = sbase + S_OFF_WT, sI = sbase + S_OFF_I;
+  const uint32_t sI = sbase + S_OFF_I;
 
   if (warp < 8) {
     // ============================ state chain ============================
@@ -816,9 +817,10 @@ __global__ void __launch_bounds__(S_NT, 1) wyg_chain_kernel(const GenParams P) {
           const int col = 64 * half + 32 * hh;
           float vals[32];
           tc::tmem_ld32(tmem + T_S + lbase + col, vals);
+          uint32_t pk[16];
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            tc::st_chunk_bf16(reinterpret_cast<char*>(sm + S_OFF_SB), tc::sw128(row, col / 8 + q4, 128), vals + 8 * q4);
+          for (int e = 0; e < 16; ++e) pk[e] = tc::pack_bf16(vals[2 * e], vals[2 * e + 1]);
+          tc::tmem_st16u(tmem + T_SB + lbase + col / 2, pk);
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
             const float4 g = *reinterpret_cast<const float4*>(gc + col + e);
@@ -827,7 +829,6 @@ __global__ void __launch_bounds__(S_NT, 1) wyg_chain_kernel(const GenParams P) {
           tc::tmem_st32(tmem + T_S + lbase + col, vals);
         }
       }
-      tc::fence_async_smem();
       tc::fence_before();
       pipe::group_sync(2, G_NT);
       // G2: W^T += S0 (-Wk)^T;  y = S0 Qd^T
@@ -835,10 +836,10 @@ __global__ void __launch_bounds__(S_NT, 1) wyg_chain_kernel(const GenParams P) {
         tc::fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint64_t a_d = tc::smem_desc(sSB + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024);
+          const uint32_t a_t = tmem + T_SB + 8 * k;
           const uint32_t kq = st + ST_KQ + (k >> 2) * KB + (k & 3) * 32;
-          tc::mma_bf16(tmem + t_w(s), a_d, tc::smem_desc(kq + 64 * 128, 16, 1024), ID_N64, 1);
-          tc::mma_bf16(tmem + t_y(s), a_d, tc::smem_desc(kq + 128 * 128, 16, 1024), ID_N64, k > 0);
+          tc::mma_bf16_ts(tmem + t_w(s), a_t, tc::smem_desc(kq + 64 * 128, 16, 1024), ID_N64, 1);
+          tc::mma_bf16_ts(tmem + t_y(s), a_t, tc::smem_desc(kq + 128 * 128, 16, 1024), ID_N64, k > 0);
         }
         tc::commit(g2);
       }
@@ -848,11 +849,11 @@ __global__ void __launch_bounds__(S_NT, 1) wyg_chain_kernel(const GenParams P) {
       {  // W^T -> bf16 A operand
         float w[32];
         tc::tmem_ld32(tmem + t_w(s) + lbase + 32 * half, w);
-        char* wt = reinterpret_cast<char*>(sm + S_OFF_WT);
+        uint32_t pk[16];
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) tc::st_chunk_bf16(wt, tc::sw128(row, 4 * half + q4, 128), w + 8 * q4);
+        for (int e = 0; e < 16; ++e) pk[e] = tc::pack_bf16(w[2 * e], w[2 * e + 1]);
+        tc::tmem_st16u(tmem + T_WB + lbase + 16 * half, pk);
       }
-      tc::fence_async_smem();
       tc::fence_before();
       pipe::group_sync(2, G_NT);
       // G3: y += W^T Mq^T;  S += W^T K'
@@ -860,9 +861,9 @@ __global__ void __launch_bounds__(S_NT, 1) wyg_chain_kernel(const GenParams P) {
         tc::fence_after();
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint64_t a_d = tc::smem_desc(sWT + k * 32, 16, 1024);
-          tc::mma_bf16(tmem + t_y(s), a_d, tc::smem_desc(st + ST_MQ + k * 2048, 8192, 1024), ID_Y3, 1);
-          tc::mma_bf16(tmem + T_S, a_d, tc::smem_desc(st + ST_KQ + k * 2048, KB, 1024), ID_S3, 1);
+          const uint32_t a_t = tmem + T_WB + 8 * k;
+          tc::mma_bf16_ts(tmem + t_y(s), a_t, tc::smem_desc(st + ST_MQ + k * 2048, 8192, 1024), ID_Y3, 1);
+          tc::mma_bf16_ts(tmem + T_S, a_t, tc::smem_desc(st + ST_KQ + k * 2048, KB, 1024), ID_S3, 1);
         }
         tc::commit(g3 + s);
       }
