@@ -35,6 +35,7 @@ constexpr size_t STATE = (size_t)VD * KD;  // floats
 struct BwdParams {
   gdnx_scan_bwd_args a;
   int kmd2, vec_e, vec_w, chan_decay;
+  int prefetch;  // rows 4-element aligned: the next staging's rows go by cp.async (see stage())
   int64_t nblk;
   float* ckpt;   // [N][nblk][V][K]
   float* sub;    // [N][8][V][K]
@@ -74,22 +75,123 @@ GDNX_DEV void decay_factor_grad(float raw, int kind, bool kmd2, float* f, float*
   }
 }
 
-// Stage tokens t0 .. t0 + nt - 1 (nt <= SUB) of chain (b, h, m): warp j < nt takes token j,
-// lane l channels l, l + 32, l + 64, l + 96.
-GDNX_DEV void stage(const BwdParams& P, Tok* tk, float* graw, int64_t b, int64_t h, int64_t m, int64_t t0, int nt,
-                    int warp, int lane, bool with_dy) {
+// Raw rows of one staged token, fetched ahead with cp.async: query slots 0-3, k, v, vector erase
+// gate, vector write gate, per-channel decay, dy (128 elements of up to 4 bytes each).
+constexpr int RAWROW = 512, RAW_Q = 0, RAW_K = 4, RAW_V = 5, RAW_B = 6, RAW_W = 7, RAW_D = 8, RAW_DY = 9,
+              RAWROWS = 10, RAWTOK = RAWROWS * RAWROW;
+
+// The stagings of one chain, in the order the kernel runs them (index k): the forward sweep's
+// full sub-blocks, then per block from the last one down the sub-block start states (no dy)
+// and the sub-blocks in reverse (with dy).
+struct StageCall {
+  int64_t t0;
+  int nt, dy;
+};
+GDNX_DEV int64_t stage_calls(const BwdParams& P) {
+  const int64_t T = P.a.fwd.T, nb_last = T - (P.nblk - 1) * BLK, ns_last = (nb_last + SUB - 1) / SUB;
+  return (P.nblk - 1) * (BLK / SUB) + (2 * ns_last - 1) + (P.nblk - 1) * (2 * (BLK / SUB) - 1);
+}
+GDNX_DEV StageCall stage_call(const BwdParams& P, int64_t k) {
+  const int64_t T = P.a.fwd.T, F = (P.nblk - 1) * (BLK / SUB);
+  if (k < F) return {k * SUB, SUB, 0};
+  k -= F;
+  const int64_t nb_last = T - (P.nblk - 1) * BLK, ns_last = (nb_last + SUB - 1) / SUB, c0 = 2 * ns_last - 1;
+  int64_t blk, j, nsub;
+  if (k < c0) {
+    blk = P.nblk - 1;
+    j = k;
+    nsub = ns_last;
+  } else {
+    k -= c0;
+    blk = P.nblk - 2 - k / (2 * (BLK / SUB) - 1);
+    j = k % (2 * (BLK / SUB) - 1);
+    nsub = BLK / SUB;
+  }
+  const int64_t tb = blk * BLK;
+  if (j < nsub - 1) return {tb + SUB * j, SUB, 0};
+  const int64_t sb = nsub - 1 - (j - (nsub - 1)), t0 = tb + SUB * sb;
+  return {t0, (int)((T - t0) < SUB ? (T - t0) : SUB), 1};
+}
+GDNX_DEV float raw_elem(const uint8_t* row, int dt, int i) {
+  if (dt == GDNX_F32) return reinterpret_cast<const float*>(row)[i];
+  if (dt == GDNX_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[i]);
+  return __half2float(reinterpret_cast<const __half*>(row)[i]);
+}
+// Scalars of the staged token (fetched with the rows, into registers).
+struct RawScal {
+  float be, bw, sg;
+};
+// Warp `warp` fetches its token of staging k into raw buffer k & 1 (nothing past the last staging).
+GDNX_DEV void prefetch(const BwdParams& P, uint8_t* raw, int64_t k, int64_t b, int64_t h, int64_t m, int warp,
+                       int lane, RawScal& sc) {
   const gdnx_scan_args& a = P.a.fwd;
+  if (k >= stage_calls(P)) return;
+  const StageCall c = stage_call(P, k);
+  if (warp >= c.nt) return;
+  const int64_t t = c.t0 + warp;
+  uint8_t* rt = raw + ((k & 1) * SUB + warp) * RAWTOK;
+  auto cp_row = [&](int r, const gdnx_view& vw, int64_t off) {  // this lane's 4 elements
+    const int es = vw.dtype == GDNX_F32 ? 4 : 2;
+    const char* src = reinterpret_cast<const char*>(vw.ptr) + (off + 4 * lane) * es;
+    const uint32_t dst = (uint32_t)__cvta_generic_to_shared(rt + r * RAWROW + 4 * es * lane);
+    if (es == 4)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    else
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+  };
+  const int rs = a.r_out <= 1 ? 1 : (a.r_out < MAXR ? a.r_out : MAXR);
+  for (int r = 0; r < rs; ++r) cp_row(RAW_Q + r, a.q, view_off(a.q, b, t, h, m, r));
+  cp_row(RAW_K, a.k, view_off(a.k, b, t, h, m));
+  cp_row(RAW_V, a.v, view_off(a.v, b, t, h, m));
+  if (P.vec_e) cp_row(RAW_B, a.gate_e, view_off(a.gate_e, b, t, h, m));
+  if (P.vec_w) cp_row(RAW_W, a.gate_w, view_off(a.gate_w, b, t, h, m));
+  if (P.chan_decay) cp_row(RAW_D, a.decay, view_off(a.decay, b, t, h, m));
+  if (c.dy) cp_row(RAW_DY, P.a.dy, view_off(P.a.dy, b, t, h, m));
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  sc.be = P.vec_e ? 0.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m));
+  sc.bw = P.vec_w ? 0.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m));
+  sc.sg = P.chan_decay ? 0.f : ld_as_f32(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
+}
+
+// Stage tokens t0 .. t0 + nt - 1 (nt <= SUB) of chain (b, h, m): warp j < nt takes token j,
+// lane l channels l, l + 32, l + 64, l + 96.  With P.prefetch this is staging k: its rows are
+// already in raw buffer k & 1 (fetched by the same warp during staging k - 1), and staging
+// k + 1's rows are fetched into the other buffer before this one is converted.
+GDNX_DEV void stage(const BwdParams& P, Tok* tk, float* graw, int64_t b, int64_t h, int64_t m, int64_t t0, int nt,
+                    int warp, int lane, bool with_dy, uint8_t* raw, int64_t k, RawScal& sc) {
+  const gdnx_scan_args& a = P.a.fwd;
+  RawScal cur = sc;
+  const uint8_t* rt = raw + ((k & 1) * SUB + warp) * RAWTOK;
+  if (P.prefetch) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+    prefetch(P, raw, k + 1, b, h, m, warp, lane, sc);
+  }
   if (warp >= nt) return;
   const int64_t t = t0 + warp;
   Tok& T = tk[warp];
   float kh = 0.f;
-  const float be = P.vec_e ? 0.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m));
-  const float bw = P.vec_w ? 0.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m));
-  const float sg = P.chan_decay ? 0.f : ld_as_f32(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
+  const float be = P.vec_e ? 0.f : (P.prefetch ? cur.be : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m)));
+  const float bw = P.vec_w ? 0.f : (P.prefetch ? cur.bw : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m)));
+  const float sg = P.chan_decay ? 0.f : (P.prefetch ? cur.sg : ld_as_f32(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m)));
   // every global load first (four channels per lane), then the shared-memory writes: the
   // stores go through a generic reference, so loads issued after them would be serialised
   float qv[4] = {0.f, 0.f, 0.f, 0.f}, qsv[MAXR][4], kv[4], vv[4], bvv[4], wvv[4], rv[4], dyv[4];
   const int rs = a.r_out <= 1 ? 1 : (a.r_out < MAXR ? a.r_out : MAXR);
+  if (P.prefetch) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = lane + 32 * i;
+#pragma unroll
+      for (int r = 0; r < MAXR; ++r) qsv[r][i] = r < rs ? raw_elem(rt + (RAW_Q + r) * RAWROW, a.q.dtype, c) : 0.f;
+      kv[i] = raw_elem(rt + RAW_K * RAWROW, a.k.dtype, c);
+      vv[i] = raw_elem(rt + RAW_V * RAWROW, a.v.dtype, c);
+      bvv[i] = P.vec_e ? raw_elem(rt + RAW_B * RAWROW, a.gate_e.dtype, c) : be;
+      wvv[i] = P.vec_w ? raw_elem(rt + RAW_W * RAWROW, a.gate_w.dtype, c) : bw;
+      rv[i] = P.chan_decay ? raw_elem(rt + RAW_D * RAWROW, a.decay.dtype, c) : sg;
+      dyv[i] = with_dy ? raw_elem(rt + RAW_DY * RAWROW, P.a.dy.dtype, c) : 0.f;
+    }
+  } else
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int c = lane + 32 * i;
@@ -297,6 +399,7 @@ __device__ unsigned long long g_bwd_probe[8];
 // shared memory
 struct BwdSmem {
   Tok tk[SUB];
+  uint8_t raw[2 * SUB * RAWTOK];  // rows fetched ahead (two stagings)
   float graw[SUB][KD];       // d factor / d raw decay per channel
   float red[4][NW][KD];      // column partials per warp: dq, dk (S part), dh, dG
   float gvec[4][KD];         // their sums
@@ -326,6 +429,9 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
   unsigned long long pacc[8] = {};
 #endif
 
+  int64_t kcall = 0;  // index of the next staging (the prefetch schedule follows it)
+  RawScal rsc{0.f, 0.f, 0.f};
+  if (P.prefetch) prefetch(P, sm.raw, 0, b, h, m, warp, lane, rsc);
   // ---- forward sweep: state at every block start ----
   if (a.state_in) ld_state(a.state_in + (size_t)n * STATE, v, qd, S);
   else
@@ -336,7 +442,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
     if (blk == P.nblk - 1) break;  // the last block's end state is not needed
     for (int64_t t0 = blk * BLK; t0 < (blk + 1) * BLK; t0 += SUB) {
       BWD_MARK(0);
-      stage(P, sm.tk, &sm.graw[0][0], b, h, m, t0, SUB, warp, lane, false);
+      stage(P, sm.tk, &sm.graw[0][0], b, h, m, t0, SUB, warp, lane, false, sm.raw, kcall++, rsc);
       __syncthreads();
       BWD_MARK(7);
 #pragma unroll 1
@@ -361,7 +467,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
     for (int sb = 0; sb < nsub; ++sb) {  // sub-block start states
       st_state(subs + sb * STATE, v, qd, S);
       if (sb == nsub - 1) break;
-      stage(P, sm.tk, &sm.graw[0][0], b, h, m, tb + SUB * sb, SUB, warp, lane, false);
+      stage(P, sm.tk, &sm.graw[0][0], b, h, m, tb + SUB * sb, SUB, warp, lane, false, sm.raw, kcall++, rsc);
       __syncthreads();
 #pragma unroll 1
       for (int j = 0; j < SUB; ++j) fwd_step(S, sm.tk[j], v, qd);
@@ -371,7 +477,7 @@ __global__ void __launch_bounds__(NT, 1) scan_bwd_kernel(const BwdParams P) {
     for (int sb = nsub - 1; sb >= 0; --sb) {
       const int64_t t0 = tb + SUB * sb;
       const int nt = (int)((T - t0) < SUB ? (T - t0) : SUB);
-      stage(P, sm.tk, &sm.graw[0][0], b, h, m, t0, nt, warp, lane, true);
+      stage(P, sm.tk, &sm.graw[0][0], b, h, m, t0, nt, warp, lane, true, sm.raw, kcall++, rsc);
       ld_state(subs + sb * STATE, v, qd, S);
       st_state(ring, v, qd, S);
       __syncthreads();
@@ -531,6 +637,14 @@ gdnx_status launch_scan_bwd(const gdnx_scan_bwd_args& A, cudaStream_t st) {
   P.vec_e = a.gate_e.dim != 1;
   P.vec_w = a.gate_w.dim != 1;
   P.chan_decay = a.decay.dim == KD;
+  // rows are fetched ahead as 8/16-byte pieces of 4 elements: every row start must keep that alignment
+  auto row_ok = [](const gdnx_view& vw) {
+    const int es = vw.dtype == GDNX_F32 ? 4 : 2;
+    return (reinterpret_cast<uintptr_t>(vw.ptr) % (4 * es)) == 0 && vw.sb % 4 == 0 && vw.st % 4 == 0 &&
+           vw.sh % 4 == 0 && vw.sm % 4 == 0 && vw.ss % 4 == 0;
+  };
+  P.prefetch = row_ok(a.q) && row_ok(a.k) && row_ok(a.v) && (!P.vec_e || row_ok(a.gate_e)) &&
+               (!P.vec_w || row_ok(a.gate_w)) && (!P.chan_decay || row_ok(a.decay)) && row_ok(A.dy);
   const int64_t N = a.B * a.H * a.M;
   P.nblk = (a.T + BLK - 1) / BLK;
   float* ws = reinterpret_cast<float*>(A.workspace);
