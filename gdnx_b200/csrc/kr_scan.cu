@@ -168,7 +168,33 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
                         a.v.sh | a.v.sm) & 7) == 0;
   constexpr int kRowK = K / 8, kRowV = V / 8;  // 16-byte chunks per row
   constexpr int kRawPer = 2 * K + V;           // bf16 elements per staged token
+  // the scalar gates and decay of each staged token ride along as the aligned 4-byte words that
+  // hold them (3 words a token after the rows)
+  const bool sc_ok = raw_ok && a.decay_kind != GDNX_DECAY_BRAIDED;
+  uint32_t* rawsc = reinterpret_cast<uint32_t*>(rawst + kTB * kRawPer);
+  auto word_src = [](const void* base, int dt, int64_t off) {
+    const int es = dt == GDNX_F32 ? 4 : 2;
+    return reinterpret_cast<const char*>(reinterpret_cast<uintptr_t>(reinterpret_cast<const char*>(base) + off * es) &
+                                         ~uintptr_t(3));
+  };
+  auto word_val = [](uint32_t w, const void* base, int dt, int64_t off) {
+    if (dt == GDNX_F32) return __uint_as_float(w);
+    const uint32_t hv = ((reinterpret_cast<uintptr_t>(base) + off * 2) & 2) ? (w >> 16) : (w & 0xffffu);
+    if (dt == GDNX_BF16) return __uint_as_float(hv << 16);
+    return __half2float(__ushort_as_half((unsigned short)hv));
+  };
   auto prefetch_raw = [&](int64_t ts) {
+    if (sc_ok && tid < 3 * kTB) {
+      const int tt = tid / 3, w = tid % 3;
+      const int64_t t = ts + tt;
+      if (t < a.T && (w != 0 || !P.vec_e) && (w != 1 || !P.vec_w)) {
+        const char* src = w == 0   ? word_src(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m))
+                          : w == 1 ? word_src(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m))
+                                   : word_src(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
+        const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(rawsc + 3 * tt + w));
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+      }
+    }
     for (int idx = tid; idx < kTB * (2 * kRowK + kRowV); idx += kNT) {
       const int tt = idx / (2 * kRowK + kRowV), c = idx - tt * (2 * kRowK + kRowV);
       const int64_t t = ts + tt;
@@ -234,10 +260,18 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
           if (P.vec_w) rw[c] = ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo + i);
         }
       }
-      const float be = P.vec_e ? 1.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
-      const float bw = P.vec_w ? 1.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo);
-      const float gdec = decay_factor(a.decay, a.decay_kind, view_off(a.decay, b, t, h, m), true, a.braid_rates,
-                                      a.braid_clamp);
+      float be, bw, gdec;
+      if (sc_ok) {
+        const uint32_t* wv = rawsc + 3 * tt;
+        be = P.vec_e ? 1.f : word_val(wv[0], a.gate_e.ptr, a.gate_e.dtype, eo);
+        bw = P.vec_w ? 1.f : word_val(wv[1], a.gate_w.ptr, a.gate_w.dtype, wo);
+        const float x = word_val(wv[2], a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
+        gdec = fminf(fmaxf(a.decay_kind == GDNX_DECAY_LOG ? expf(x) : x, 0.f), 1.f);
+      } else {
+        be = P.vec_e ? 1.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
+        bw = P.vec_w ? 1.f : ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, wo);
+        gdec = decay_factor(a.decay, a.decay_kind, view_off(a.decay, b, t, h, m), true, a.braid_rates, a.braid_clamp);
+      }
 #pragma unroll
       for (int c = 0; c < KW; ++c) {
         const int i = lane + 32 * c;
@@ -416,7 +450,7 @@ gdnx_status launch_kr(const KrParams& P, cudaStream_t st) {
   const CD d{};
   const size_t floats = (size_t)d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) + kMaxP +
                         kTB * KrSmem<K, V>::kTokPer + 2 * kTB * V + 2 * (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
-  const size_t smem = floats * sizeof(float) + (size_t)kTB * (2 * K + V) * 2 + 16;  // + bf16 staging
+  const size_t smem = floats * sizeof(float) + (size_t)kTB * (2 * K + V) * 2 + (size_t)kTB * 12 + 16;  // + bf16 staging, scalar words
   const int64_t N = P.a.base.B * P.a.base.H * P.a.base.M;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
