@@ -11,9 +11,10 @@
 // Design (one CTA of 256 threads per chain):
 //  * the residual operator U Vb^T (V x K) is kept DENSE in registers, row v
 //    split over TPR threads; each token applies the rank-2 update
-//    "decay, evict the overwritten slot, add the new write".  It is rebuilt
-//    exactly from the slots at every compaction (and at call start), so
-//    rounding cannot drift over a long sequence;
+//    "decay, evict the overwritten slot, add the new write".  Compactions read
+//    it from the registers; it is rebuilt exactly from the slots at call start
+//    and every kExactEvery-th compaction, so rounding cannot drift over a long
+//    sequence;
 //  * the slot ring lives in the caller's U / Vb buffers (global, L2
 //    resident).  New writes store the raw key and a per-slot decay factor
 //    d_p (smem) carries Vb = d_p k_p, exactly the product of per-token
@@ -35,6 +36,7 @@ namespace {
 constexpr int kNT = kCompThreads;  // 256
 constexpr int kTB = 16;            // tokens staged per block (<= P handled by the block split)
 constexpr int kMaxP = 1024;
+constexpr int kExactEvery = 16;  // compactions between exact rebuilds of the residual
 
 struct KrParams {
   gdnx_kr_scan_args a;
@@ -138,6 +140,31 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
     }
     __syncthreads();
   };
+  // Rm = rearrange(residual) from the registers (both CTAs' rows: the other CTA's half arrives
+  // through distributed shared memory).  The register residual carries the per-token rounding
+  // of its updates, so every kExactEvery-th compaction rebuilds it exactly from the slots instead.
+  auto rm_from_regs = [&]() {
+    uint32_t rbase = 0;
+    if (CL > 1) {
+      const uint32_t lbase = static_cast<uint32_t>(__cvta_generic_to_shared(Rm));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbase) : "r"(lbase), "r"(1u - (uint32_t)cr));
+    }
+#pragma unroll
+    for (int c = 0; c < KC; ++c) {
+      const int k0 = 4 * (c * TPR + j);
+      const float x4[4] = {Rs[c].x, Rs[c].y, Rs[c].z, Rs[c].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int ri = rmat_index(v, k0 + e, d);
+        Rm[ri] = x4[e];
+        if (CL > 1)
+          asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(rbase + 4u * (uint32_t)ri), "f"(x4[e]) : "memory");
+      }
+    }
+    if (CL > 1) cluster_sync_all();
+    __syncthreads();
+  };
+  int comp_count = 0;
   // dense Kronecker operator sum_r A_r (x) B_r (row v, this thread's keys), materialised
   // whenever A_s / B_s change (start, compaction); its decay is the scalar fac^2
   float4 Ks[KC];
@@ -421,7 +448,8 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       for (int i = tid; i < R * d.n; i += kNT) B_s[i] *= fac;
       fac = 1.f;
       if (CL > 1) cluster_sync_all();  // the other CTA's slot writes are visible
-      rebuild();                      // Rm = rearrange(U Vb^T), Rs exact again
+      if (++comp_count % kExactEvery == 0) rebuild();  // Rm = rearrange(U Vb^T), Rs exact again
+      else rm_from_regs();
       add_kron_rmat(Rm, A_s, B_s, d);
       __syncthreads();
       err_acc += compact_core(Rm, A_s, B_s, Gg, work, d, sketch_mode);
