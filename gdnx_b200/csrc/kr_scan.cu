@@ -34,7 +34,7 @@ namespace gdnx {
 namespace {
 
 constexpr int kNT = kCompThreads;  // 256
-constexpr int kTB = 16;            // tokens staged per block (<= P handled by the block split)
+constexpr int kTB = 32;            // tokens staged per block (<= P handled by the block split)
 constexpr int kMaxP = 1024;
 constexpr int kExactEvery = 16;  // compactions between exact rebuilds of the residual
 
@@ -50,6 +50,14 @@ struct KrSmem {
   static constexpr int kTokU = 4 * K, kTokUold = 4 * K + V, kTokSc = 4 * K + 2 * V;
   static constexpr int kTokPer = 4 * K + 2 * V + 8;
 };
+
+// Floats of the region shared by the compaction (Rm, work) and the token vectors.
+template <class CD, int K, int V>
+__host__ __device__ constexpr int kr_union_floats() {
+  return (CD::a_v * CD::a_k) * compact_ld(CD::b_v * CD::b_k) + compact_work_floats() > kTB * KrSmem<K, V>::kTokPer
+             ? (CD::a_v * CD::a_k) * compact_ld(CD::b_v * CD::b_k) + compact_work_floats()
+             : kTB * KrSmem<K, V>::kTokPer;
+}
 
 // Cluster barrier (release / acquire at cluster scope: orders the CTAs' global-memory
 // slot writes and reads).
@@ -84,13 +92,15 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
   const int ld = compact_ld(d.n);
 
   // ---- shared memory carve-up ----
+  // The compaction's Rm and work space and a block's token vectors share one region: the token
+  // vectors are dead while a compaction (or a rebuild) runs, and vice versa.
   float* Rm = sm;                                  // m x ld (compaction / rebuild)
   float* work = Rm + d.m * ld;                     // compaction work
-  float* A_s = work + compact_work_floats();       // R x m
+  float* tok = sm;                                 // kTB x kTokPer (token phases)
+  float* A_s = sm + kr_union_floats<CD, K, V>();   // R x m
   float* B_s = A_s + R * d.m;                      // R x n
   float* dsl = B_s + R * d.n;                      // per-slot decay [P]
-  float* tok = dsl + kMaxP;                        // kTB x kTokPer
-  float* ybuf = tok + kTB * SMT::kTokPer;          // kTB x V
+  float* ybuf = dsl + kMaxP;                       // kTB x V
   float* nbuf = ybuf + kTB * V;                    // kTB x V (new U columns)
   float* tileU = nbuf + kTB * V;                   // 2 x V x kCompPT
   float* tileV = tileU + 2 * V * kCompPT;          // 2 x K x kCompPT
@@ -211,7 +221,8 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
     return __half2float(__ushort_as_half((unsigned short)hv));
   };
   auto prefetch_raw = [&](int64_t ts) {
-    if (sc_ok && tid < 3 * kTB) {
+    const int nb = kTB < Pn ? kTB : Pn;  // a block never holds more than P tokens
+    if (sc_ok && tid < 3 * nb) {
       const int tt = tid / 3, w = tid % 3;
       const int64_t t = ts + tt;
       if (t < a.T && (w != 0 || !P.vec_e) && (w != 1 || !P.vec_w)) {
@@ -222,7 +233,7 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
       }
     }
-    for (int idx = tid; idx < kTB * (2 * kRowK + kRowV); idx += kNT) {
+    for (int idx = tid; idx < nb * (2 * kRowK + kRowV); idx += kNT) {
       const int tt = idx / (2 * kRowK + kRowV), c = idx - tt * (2 * kRowK + kRowV);
       const int64_t t = ts + tt;
       if (t >= a.T) continue;
@@ -476,8 +487,8 @@ template <class CD>
 gdnx_status launch_kr(const KrParams& P, cudaStream_t st) {
   constexpr int K = CD::a_k * CD::b_k, V = CD::a_v * CD::b_v;
   const CD d{};
-  const size_t floats = (size_t)d.m * compact_ld(d.n) + compact_work_floats() + d.R * (d.m + d.n) + kMaxP +
-                        kTB * KrSmem<K, V>::kTokPer + 2 * kTB * V + 2 * (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
+  const size_t floats = (size_t)kr_union_floats<CD, K, V>() + d.R * (d.m + d.n) + kMaxP + 2 * kTB * V +
+                        2 * (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
   const size_t smem = floats * sizeof(float) + (size_t)kTB * (2 * K + V) * 2 + (size_t)kTB * 12 + 16;  // + bf16 staging, scalar words
   const int64_t N = P.a.base.B * P.a.base.H * P.a.base.M;
   int dev = 0, sms = 0;
