@@ -205,33 +205,21 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
                         a.v.sh | a.v.sm) & 7) == 0;
   constexpr int kRowK = K / 8, kRowV = V / 8;  // 16-byte chunks per row
   constexpr int kRawPer = 2 * K + V;           // bf16 elements per staged token
-  // the scalar gates and decay of each staged token ride along as the aligned 4-byte words that
-  // hold them (3 words a token after the rows)
+  // the scalar gates and decay of the next block are loaded into registers with its rows: lane
+  // 3 i + c of warp w holds component c (erase gate, write gate, raw decay) of token w + 8 i, and
+  // stage A (warp w takes tokens w, w + 8, ...) shuffles them out
+  static_assert(kTB <= 8 * 10, "three scalars of every token of a warp fit in its lanes");
   const bool sc_ok = raw_ok && a.decay_kind != GDNX_DECAY_BRAIDED;
-  uint32_t* rawsc = reinterpret_cast<uint32_t*>(rawst + kTB * kRawPer);
-  auto word_src = [](const void* base, int dt, int64_t off) {
-    const int es = dt == GDNX_F32 ? 4 : 2;
-    return reinterpret_cast<const char*>(reinterpret_cast<uintptr_t>(reinterpret_cast<const char*>(base) + off * es) &
-                                         ~uintptr_t(3));
-  };
-  auto word_val = [](uint32_t w, const void* base, int dt, int64_t off) {
-    if (dt == GDNX_F32) return __uint_as_float(w);
-    const uint32_t hv = ((reinterpret_cast<uintptr_t>(base) + off * 2) & 2) ? (w >> 16) : (w & 0xffffu);
-    if (dt == GDNX_BF16) return __uint_as_float(hv << 16);
-    return __half2float(__ushort_as_half((unsigned short)hv));
-  };
+  float pf_sc = 0.f;
   auto prefetch_raw = [&](int64_t ts) {
     const int nb = kTB < Pn ? kTB : Pn;  // a block never holds more than P tokens
-    if (sc_ok && tid < 3 * nb) {
-      const int tt = tid / 3, w = tid % 3;
+    if (sc_ok && lane < 3 * ((nb + 7) / 8)) {
+      const int tt = warp + 8 * (lane / 3), c = lane % 3;
       const int64_t t = ts + tt;
-      if (t < a.T && (w != 0 || !P.vec_e) && (w != 1 || !P.vec_w)) {
-        const char* src = w == 0   ? word_src(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m))
-                          : w == 1 ? word_src(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m))
-                                   : word_src(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
-        const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(rawsc + 3 * tt + w));
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-      }
+      if (tt < nb && t < a.T && (c != 0 || !P.vec_e) && (c != 1 || !P.vec_w))
+        pf_sc = c == 0   ? ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, view_off(a.gate_e, b, t, h, m))
+                : c == 1 ? ld_as_f32(a.gate_w.ptr, a.gate_w.dtype, view_off(a.gate_w, b, t, h, m))
+                         : ld_as_f32(a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
     }
     for (int idx = tid; idx < nb * (2 * kRowK + kRowV); idx += kNT) {
       const int tt = idx / (2 * kRowK + kRowV), c = idx - tt * (2 * kRowK + kRowV);
@@ -300,10 +288,11 @@ __global__ void __launch_bounds__(kNT, 1) kr_scan_kernel(const KrParams P) {
       }
       float be, bw, gdec;
       if (sc_ok) {
-        const uint32_t* wv = rawsc + 3 * tt;
-        be = P.vec_e ? 1.f : word_val(wv[0], a.gate_e.ptr, a.gate_e.dtype, eo);
-        bw = P.vec_w ? 1.f : word_val(wv[1], a.gate_w.ptr, a.gate_w.dtype, wo);
-        const float x = word_val(wv[2], a.decay.ptr, a.decay.dtype, view_off(a.decay, b, t, h, m));
+        const int li = 3 * (tt / 8);
+        const float se = __shfl_sync(0xffffffffu, pf_sc, li), sw = __shfl_sync(0xffffffffu, pf_sc, li + 1);
+        const float x = __shfl_sync(0xffffffffu, pf_sc, li + 2);
+        be = P.vec_e ? 1.f : se;
+        bw = P.vec_w ? 1.f : sw;
         gdec = fminf(fmaxf(a.decay_kind == GDNX_DECAY_LOG ? expf(x) : x, 0.f), 1.f);
       } else {
         be = P.vec_e ? 1.f : ld_as_f32(a.gate_e.ptr, a.gate_e.dtype, eo);
@@ -489,7 +478,7 @@ gdnx_status launch_kr(const KrParams& P, cudaStream_t st) {
   const CD d{};
   const size_t floats = (size_t)kr_union_floats<CD, K, V>() + d.R * (d.m + d.n) + kMaxP + 2 * kTB * V +
                         2 * (V + K) * kCompPT + 32 + 2 * kTB * 64 + 64;
-  const size_t smem = floats * sizeof(float) + (size_t)kTB * (2 * K + V) * 2 + (size_t)kTB * 12 + 16;  // + bf16 staging, scalar words
+  const size_t smem = floats * sizeof(float) + (size_t)kTB * (2 * K + V) * 2 + 16;  // + bf16 staging
   const int64_t N = P.a.base.B * P.a.base.H * P.a.base.M;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
