@@ -689,9 +689,7 @@ constexpr int S_NT = 512;  // warps 0-7: state chain; warps 8-15: output
 constexpr int G_NT = 256;
 constexpr int KB = 24576;  // k-block stride of a stage's [K' ; -Wk ; Qd] tile (192 rows)
 constexpr int ST_KQ = 0, ST_MQ = 49152, ST_W0 = 57344, ST_GC = 73728, ST_BYTES = REC;
-constexpr int S_OFF_SB = 2 * ST_BYTES;         // bf16 state [2 kb][128 v][128 B]
-constexpr int S_OFF_WT = S_OFF_SB + 32768;     // W^T [128 v][64 j]
-constexpr int S_OFF_I = S_OFF_WT + 16384;      // identity [64][64]
+constexpr int S_OFF_I = 2 * ST_BYTES;          // identity [64][64] (S0 and W^T operands live in TMEM)
 constexpr int S_OFF_KN = S_OFF_I + 8192;       // [2][64] |k| copies, [2][64] score sums
 constexpr int S_OFF_BAR = S_OFF_KN + 1024;
 constexpr int S_SMEM = S_OFF_BAR + 128 + 1024;
